@@ -1,0 +1,205 @@
+/*
+ * opendm_muon.h - C ABI of the B200 (sm_100a) MuonAdamW optimizer step.
+ *
+ * The reference implements this path as one PyTorch file,
+ * opendm/optimizer/muon_adamw.py, with no native code. Each entry point below
+ * replaces a group of torch ops from that file; the citation beside each
+ * names the reference lines it stands in for. The Python host
+ * (opendm_b200.optimizer.MuonAdamW) keeps the reference's torch.optim surface
+ * and calls these functions through ctypes.
+ *
+ * Conventions
+ *  - Every function returns an int status: MUON_OK (0) or a MUON_ERR_* code.
+ *    The message of the last failure on the calling thread is returned by
+ *    muon_last_error().
+ *  - Every buffer is caller-owned device memory given as a plain pointer with
+ *    sizes and leading dimensions in elements. The library allocates no device
+ *    memory, performs no host synchronisation and issues no collectives.
+ *    (muon_ns_plan_create allocates only the host-side plan object.)
+ *  - `stream` is a cudaStream_t passed as void*. NULL means the legacy
+ *    default stream.
+ *  - Device kernels bound every spin-wait. A wait that times out writes a
+ *    nonzero code to the caller's device error word (`err_dev`), which the
+ *    host reads after the stream completes (muon_read_error).
+ */
+#ifndef OPENDM_MUON_H_
+#define OPENDM_MUON_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MUON_ABI_VERSION 1
+
+enum muon_status {
+  MUON_OK = 0,
+  MUON_ERR_ARG = 1,         /* invalid argument (shape, dtype, pointer, alignment) */
+  MUON_ERR_CUDA = 2,        /* a CUDA runtime or driver call failed */
+  MUON_ERR_DEVICE = 3,      /* the current device is not sm_100 */
+  MUON_ERR_UNSUPPORTED = 4, /* the request is valid but not implemented */
+  MUON_ERR_KERNEL = 5       /* a kernel recorded an error (bounded wait expired) */
+};
+
+enum muon_dtype {
+  MUON_BF16 = 0, /* bfloat16 storage */
+  MUON_F32 = 1,  /* float32 storage */
+  MUON_TF32 = 2  /* float32 storage holding values rounded to tf32 (NS operands) */
+};
+
+/* ------------------------------------------------------------------ misc */
+
+/* ABI version of the loaded library (MUON_ABI_VERSION). */
+int muon_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* muon_last_error(void);
+
+/* MUON_OK when `device` is an sm_100 GPU this library can run on. */
+int muon_device_check(int device);
+
+/* Copy the device error word to *host_code (synchronises `stream`).
+ * Returns MUON_ERR_KERNEL when the word is nonzero, and clears it. */
+int muon_read_error(int* err_dev, int* host_code, void* stream);
+
+/* --------------------------------------------- (a) momentum + Nesterov
+ * Replaces muon_adamw.py:381-394 (step += 1 is done by the host):
+ *   g = grad.float() (zeros when grad is absent)
+ *   exp_avg = momentum * exp_avg + g
+ *   d = g + momentum * exp_avg   (nesterov)   |   d = exp_avg   (otherwise)
+ * and the Frobenius norm of muon_adamw.py:118-121, fused: each segment's
+ * sum of d^2 is reduced and turned into the Newton-Schulz input scale
+ *   scale = 0                       if the norm is 0 or not finite
+ *   scale = 1 / max(norm, eps)      otherwise.
+ * d is written rounded to `dir_dtype` (MUON_BF16 or MUON_TF32) into
+ * `direction` with row stride `ld` (the matrix keeps the parameter's layout).
+ */
+typedef struct muon_momentum_seg {
+  const void* grad;    /* [rows*cols] of grad_dtype, or NULL for an absent grad */
+  float* exp_avg;      /* [rows*cols] fp32, updated in place */
+  void* direction;     /* [rows][ld] of dir_dtype, or NULL: update exp_avg only */
+  int64_t rows;
+  int64_t cols;
+  int64_t ld;          /* >= cols */
+  int64_t chunk_begin; /* prefix sum of muon_momentum_chunks() over previous segments */
+} muon_momentum_seg;
+
+/* Number of work chunks the momentum kernel uses for a rows x cols segment. */
+int64_t muon_momentum_chunks(int64_t rows, int64_t cols);
+
+int muon_momentum(const muon_momentum_seg* segs_dev, int n_segs, int64_t total_chunks,
+                  int grad_dtype, int dir_dtype, float momentum, int nesterov, float eps,
+                  float* partials_dev /* [total_chunks] scratch */,
+                  float* scales_dev /* [n_segs] out */, void* stream);
+
+/* ------------------------------------ (b) Newton-Schulz orthogonalisation
+ * Replaces zeropower_via_newtonschulz5 (muon_adamw.py:101-128) for a set of
+ * same-shape matrices ("class"), and optionally the update of
+ * muon_adamw.py:395-398 and :407-414.
+ *
+ * The quintic iteration X <- a X + (b A + c A A) X, A = X X^T, is evaluated
+ * in the algebraically identical form
+ *   A' = X X^T - I,  M = alpha I + beta A' + gamma A' A',  X <- M X,
+ *   alpha = a + b + c, beta = b + 2c, gamma = c,
+ * which avoids cancellation between a X and (b A + c A A) X when the operands
+ * are rounded (tf32 or bf16) for the tensor cores. A matrix with rows > cols
+ * is orthogonalised through its transpose, as in the reference; here the
+ * transpose is expressed by operand majorness, so X keeps the parameter's
+ * layout and no transposed copy is made.
+ *
+ * Each class owns four caller-provided buffers of op dtype (MUON_BF16:
+ * 2 bytes, MUON_TF32: 4 bytes per element):
+ *   x0, x1: [count][rows][ld_x]  (x0 holds the direction written by
+ *           muon_momentum; x1 is the ping-pong partner)
+ *   ap, mm: [count][m][ld_m]     m = min(rows, cols)
+ * ld_x and ld_m must make rows 16-byte aligned (multiple of 8 for bf16, of 4
+ * for tf32), and every buffer must be 16-byte aligned.
+ * `scales` holds the per-matrix input scale produced by muon_momentum.
+ *
+ * Output of the last iteration, per class:
+ *   u_out != NULL: U = orthogonalised update, fp32 [count][rows][ld_u];
+ *   params != NULL: in-place parameter update, for matrix i of the class
+ *       p = p * wd_factor   (skipped when wd_factor == 1)
+ *       p = p - eff * cast(U, param_dtype)
+ *     with the reference's rounding order for bf16 parameters.
+ *   Exactly one of u_out / params must be set.
+ */
+typedef struct muon_ns_class {
+  int32_t rows;
+  int32_t cols;
+  int32_t count;
+  int32_t param_dtype; /* MUON_BF16 or MUON_F32 (used when params != NULL) */
+  void* x0;
+  void* x1;
+  int64_t ld_x;
+  void* ap;
+  void* mm;
+  int64_t ld_m;
+  const float* scales; /* [count] device */
+  float* u_out;        /* optional [count][rows][ld_u] fp32 */
+  int64_t ld_u;
+  void* const* params; /* optional device array [count] of parameter pointers ([rows][cols]) */
+} muon_ns_class;
+
+typedef struct muon_ns_plan muon_ns_plan;
+
+/* Build launch descriptors (tensor maps, tile schedules) for `n_classes`
+ * classes iterated `steps` times with operands of `op_dtype`
+ * (MUON_TF32 or MUON_BF16). The plan stores pointers, not data: buffers must
+ * outlive it and stay at the same addresses. */
+int muon_ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, int steps,
+                        muon_ns_plan** plan_out);
+
+/* Run the plan: 3 grouped GEMM launches per iteration. `eff` is a host array
+ * [n_classes] of lr * lr_scale * coefficient * scale(shape) and wd_factor is
+ * 1 - lr * weight_decay; both are read at launch time, so a scheduler may
+ * change lr between steps. `err_dev` is a device int (0 before the call). */
+int muon_ns_plan_run(const muon_ns_plan* plan, const float* eff, float wd_factor, int* err_dev,
+                     void* stream);
+
+void muon_ns_plan_destroy(muon_ns_plan* plan);
+
+/* Bytes of one class's workspace when x0, x1, ap and mm are carved from a
+ * single buffer with muon_ns_class_layout (each part 256-byte aligned). */
+int64_t muon_ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype);
+
+/* Fill x0/x1/ap/mm/ld_x/ld_m of `cls` from one workspace buffer `base` of
+ * muon_ns_class_workspace_bytes() bytes. */
+int muon_ns_class_layout(muon_ns_class* cls, void* base, int op_dtype);
+
+/* ------------------------------------------------- AdamW fallback group
+ * Replaces _adamw_step / _call_adamw_functional (muon_adamw.py:131-175,
+ * :333-343), i.e. torch.optim.adamw single-tensor AdamW with decoupled weight
+ * decay, fused into one pass per element:
+ *   p = p * (1 - lr*wd)            (skipped when wd == 0)
+ *   m = lerp(m, g, 1 - beta1)
+ *   v = beta2 * v + (1 - beta2) * g * g
+ *   p = p - step_size * m / (sqrt(v) / bc2_sqrt + eps)
+ * step_size = lr / (1 - beta1^step) and bc2_sqrt = sqrt(1 - beta2^step) are
+ * computed by the host per segment from its step count.
+ */
+typedef struct muon_adamw_seg {
+  void* param;        /* [numel] of param_dtype */
+  const void* grad;   /* [numel] of grad_dtype */
+  float* exp_avg;     /* [numel] fp32 */
+  float* exp_avg_sq;  /* [numel] fp32 */
+  int64_t numel;
+  int64_t chunk_begin;/* prefix sum of muon_adamw_chunks() */
+  float step_size;
+  float bc2_sqrt;
+  int32_t param_dtype;
+  int32_t grad_dtype;
+} muon_adamw_seg;
+
+int64_t muon_adamw_chunks(int64_t numel);
+
+int muon_adamw(const muon_adamw_seg* segs_dev, int n_segs, int64_t total_chunks, double beta1,
+               double beta2, float eps, float wd_factor, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OPENDM_MUON_H_ */

@@ -1,0 +1,109 @@
+// extern "C" entry points declared in include/opendm_muon.h. Each forwards to
+// the kernel file that implements it; this file owns error reporting.
+
+#include <cstdio>
+#include <string>
+
+#include "internal.h"
+
+namespace muon {
+
+static thread_local std::string g_last_error;
+
+int set_error(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return MUON_OK;
+  char buf[256];
+  snprintf(buf, sizeof(buf), "%s: %s (%d)", what, cudaGetErrorString(e), int(e));
+  return set_error(MUON_ERR_CUDA, buf);
+}
+
+}  // namespace muon
+
+using muon::set_error;
+
+extern "C" {
+
+int muon_version(void) { return MUON_ABI_VERSION; }
+
+const char* muon_last_error(void) { return muon::g_last_error.c_str(); }
+
+int muon_device_check(int device) {
+  int major = 0, minor = 0;
+  if (muon::check_cuda(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device),
+                       "compute capability"))
+    return MUON_ERR_CUDA;
+  if (muon::check_cuda(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device),
+                       "compute capability"))
+    return MUON_ERR_CUDA;
+  if (major != 10 || minor != 0) {
+    char buf[128];
+    snprintf(buf, sizeof(buf), "device %d is sm_%d%d; this library is built for sm_100a only", device,
+             major, minor);
+    return set_error(MUON_ERR_DEVICE, buf);
+  }
+  return MUON_OK;
+}
+
+int muon_read_error(int* err_dev, int* host_code, void* stream) {
+  if (!err_dev || !host_code) return set_error(MUON_ERR_ARG, "null error pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int code = 0;
+  if (muon::check_cuda(cudaMemcpyAsync(&code, err_dev, sizeof(int), cudaMemcpyDeviceToHost, s),
+                       "read error word"))
+    return MUON_ERR_CUDA;
+  if (muon::check_cuda(cudaStreamSynchronize(s), "stream synchronize")) return MUON_ERR_CUDA;
+  *host_code = code;
+  if (code != 0) {
+    if (muon::check_cuda(cudaMemsetAsync(err_dev, 0, sizeof(int), s), "clear error word"))
+      return MUON_ERR_CUDA;
+    char buf[128];
+    snprintf(buf, sizeof(buf), "kernel reported error code 0x%x (bounded wait expired)", code);
+    return set_error(MUON_ERR_KERNEL, buf);
+  }
+  return MUON_OK;
+}
+
+int64_t muon_momentum_chunks(int64_t rows, int64_t cols) { return muon::momentum_chunks(rows, cols); }
+
+int muon_momentum(const muon_momentum_seg* segs_dev, int n_segs, int64_t total_chunks, int grad_dtype,
+                  int dir_dtype, float momentum, int nesterov, float eps, float* partials_dev,
+                  float* scales_dev, void* stream) {
+  return muon::launch_momentum(segs_dev, n_segs, total_chunks, grad_dtype, dir_dtype, momentum, nesterov,
+                               eps, partials_dev, scales_dev, static_cast<cudaStream_t>(stream));
+}
+
+int muon_ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, int steps,
+                        muon_ns_plan** plan_out) {
+  if (!classes) return set_error(MUON_ERR_ARG, "classes is null");
+  return muon::ns_plan_create(classes, n_classes, op_dtype, steps, plan_out);
+}
+
+int muon_ns_plan_run(const muon_ns_plan* plan, const float* eff, float wd_factor, int* err_dev,
+                     void* stream) {
+  return muon::ns_plan_run(plan, eff, wd_factor, err_dev, static_cast<cudaStream_t>(stream));
+}
+
+void muon_ns_plan_destroy(muon_ns_plan* plan) { muon::ns_plan_destroy(plan); }
+
+int64_t muon_ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype) {
+  return muon::ns_class_workspace_bytes(rows, cols, count, op_dtype);
+}
+
+int muon_ns_class_layout(muon_ns_class* cls, void* base, int op_dtype) {
+  return muon::ns_class_layout(cls, base, op_dtype);
+}
+
+int64_t muon_adamw_chunks(int64_t numel) { return muon::adamw_chunks(numel); }
+
+int muon_adamw(const muon_adamw_seg* segs_dev, int n_segs, int64_t total_chunks, double beta1, double beta2,
+               float eps, float wd_factor, void* stream) {
+  return muon::launch_adamw(segs_dev, n_segs, total_chunks, beta1, beta2, eps, wd_factor,
+                            static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

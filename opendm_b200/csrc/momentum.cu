@@ -1,0 +1,213 @@
+// (a) Fused momentum + Nesterov + Frobenius norm for every Muon matrix.
+// Reference: opendm/optimizer/muon_adamw.py:381-394 (momentum, Nesterov
+// blend) and :118-121 (Frobenius normalisation input of the Newton-Schulz).
+//
+// One pass over the segment table: each 16 Ki-element chunk reads grad
+// (bf16/fp32) and exp_avg (fp32) with 128-bit loads, writes exp_avg and the
+// direction (rounded to the Newton-Schulz operand type) with 128-bit stores,
+// and writes its partial sum of d^2. A second tiny kernel reduces the partials
+// of each matrix in a fixed order (deterministic) and produces the input scale
+// 1 / max(||d||_F, eps), or 0 for a zero or non-finite norm.
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace muon {
+
+constexpr int MOM_THREADS = 256;
+constexpr int MOM_VEC = 8;
+constexpr int MOM_ITERS = 8;
+constexpr int64_t MOM_CHUNK = int64_t(MOM_THREADS) * MOM_VEC * MOM_ITERS;  // 16384
+
+int64_t momentum_chunks(int64_t rows, int64_t cols) {
+  const int64_t n = rows * cols;
+  return n <= 0 ? 0 : (n + MOM_CHUNK - 1) / MOM_CHUNK;
+}
+
+__device__ __forceinline__ int find_segment(const muon_momentum_seg* segs, int n_segs, int64_t chunk) {
+  int lo = 0, hi = n_segs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (segs[mid].chunk_begin <= chunk)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  return lo;
+}
+
+struct MomOut {
+  float m, d;
+};
+
+// exp_avg = momentum * exp_avg + g  (two roundings, as buffer.mul_().add_())
+// d = g + momentum * exp_avg        (one fused multiply-add, as add_(alpha=))
+__device__ __forceinline__ MomOut mom_op(float g, float m, float mu, bool nesterov) {
+  MomOut o;
+  o.m = __fadd_rn(__fmul_rn(mu, m), g);
+  o.d = nesterov ? __fmaf_rn(mu, o.m, g) : o.m;
+  return o;
+}
+
+template <int kGradDt, int kDirDt>
+__device__ __forceinline__ void load_grad8(const void* grad, int64_t e, float (&g)[8]) {
+  if (grad == nullptr) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) g[i] = 0.f;
+  } else if constexpr (kGradDt == MUON_BF16) {
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(grad) + e));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      g[2 * i] = f.x;
+      g[2 * i + 1] = f.y;
+    }
+  } else {
+    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(grad) + e);
+    const float4 a = __ldg(p), b = __ldg(p + 1);
+    g[0] = a.x, g[1] = a.y, g[2] = a.z, g[3] = a.w, g[4] = b.x, g[5] = b.y, g[6] = b.z, g[7] = b.w;
+  }
+}
+
+template <int kDirDt>
+__device__ __forceinline__ void store_dir8(void* dir, int64_t e, const float (&d)[8]) {
+  if constexpr (kDirDt == MUON_BF16) {
+    uint4 raw;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(d[2 * i], d[2 * i + 1]);
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(dir) + e) = raw;
+  } else {
+    float4* p = reinterpret_cast<float4*>(reinterpret_cast<float*>(dir) + e);
+    p[0] = make_float4(round_tf32(d[0]), round_tf32(d[1]), round_tf32(d[2]), round_tf32(d[3]));
+    p[1] = make_float4(round_tf32(d[4]), round_tf32(d[5]), round_tf32(d[6]), round_tf32(d[7]));
+  }
+}
+
+template <int kGradDt, int kDirDt>
+__global__ void __launch_bounds__(MOM_THREADS) momentum_kernel(const muon_momentum_seg* __restrict__ segs,
+                                                               int n_segs, float mu, int nesterov,
+                                                               float* __restrict__ partials) {
+  __shared__ float red[MOM_THREADS / 32];
+  const int64_t chunk = blockIdx.x;
+  const int s = find_segment(segs, n_segs, chunk);
+  const muon_momentum_seg sg = segs[s];
+  const int64_t numel = sg.rows * sg.cols;
+  const int64_t e0 = (chunk - sg.chunk_begin) * MOM_CHUNK;
+  const int64_t e1 = min(e0 + MOM_CHUNK, numel);
+  const bool nest = nesterov != 0;
+  const int gsz = kGradDt == MUON_BF16 ? 2 : 4;
+  const int dsz = kDirDt == MUON_BF16 ? 2 : 4;
+  const bool vec_ok = sg.ld == sg.cols && (numel % 8) == 0 &&
+                      ((reinterpret_cast<uintptr_t>(sg.grad) | reinterpret_cast<uintptr_t>(sg.exp_avg) |
+                        reinterpret_cast<uintptr_t>(sg.direction)) & 15u) == 0 &&
+                      gsz > 0 && dsz > 0;
+  float acc = 0.f;
+  if (vec_ok) {
+#pragma unroll 2
+    for (int it = 0; it < MOM_ITERS; ++it) {
+      const int64_t e = e0 + (int64_t(it) * MOM_THREADS + threadIdx.x) * MOM_VEC;
+      if (e >= e1) break;
+      float g[8];
+      load_grad8<kGradDt, kDirDt>(sg.grad, e, g);
+      float4* mp = reinterpret_cast<float4*>(sg.exp_avg + e);
+      const float4 m0 = mp[0], m1 = mp[1];
+      const float mo[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+      float mn[8], d[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const MomOut o = mom_op(g[i], mo[i], mu, nest);
+        mn[i] = o.m;
+        d[i] = o.d;
+        acc = fmaf(o.d, o.d, acc);
+      }
+      mp[0] = make_float4(mn[0], mn[1], mn[2], mn[3]);
+      mp[1] = make_float4(mn[4], mn[5], mn[6], mn[7]);
+      if (sg.direction != nullptr) store_dir8<kDirDt>(sg.direction, e, d);
+    }
+  } else {
+    for (int64_t e = e0 + threadIdx.x; e < e1; e += MOM_THREADS) {
+      float g = 0.f;
+      if (sg.grad) {
+        if constexpr (kGradDt == MUON_BF16)
+          g = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sg.grad)[e]);
+        else
+          g = reinterpret_cast<const float*>(sg.grad)[e];
+      }
+      const MomOut o = mom_op(g, sg.exp_avg[e], mu, nest);
+      sg.exp_avg[e] = o.m;
+      acc = fmaf(o.d, o.d, acc);
+      if (sg.direction == nullptr) continue;
+      const int64_t r = e / sg.cols, c = e - r * sg.cols;
+      const int64_t di = r * sg.ld + c;
+      if constexpr (kDirDt == MUON_BF16)
+        reinterpret_cast<__nv_bfloat16*>(sg.direction)[di] = __float2bfloat16_rn(o.d);
+      else
+        reinterpret_cast<float*>(sg.direction)[di] = round_tf32(o.d);
+    }
+  }
+  // Deterministic block reduction of sum(d^2).
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < MOM_THREADS / 32 ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if (threadIdx.x == 0) partials[chunk] = v;
+  }
+}
+
+// One warp per segment: fixed-order reduction of its chunk partials, then the
+// Newton-Schulz input scale (reference muon_adamw.py:118-121).
+__global__ void momentum_scale_kernel(const muon_momentum_seg* __restrict__ segs, int n_segs,
+                                      int64_t total_chunks, const float* __restrict__ partials, float eps,
+                                      float* __restrict__ scales) {
+  const int s = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (s >= n_segs) return;
+  const int64_t b = segs[s].chunk_begin;
+  const int64_t e = (s + 1 < n_segs) ? segs[s + 1].chunk_begin : total_chunks;
+  float acc = 0.f;
+  for (int64_t c = b + lane; c < e; c += 32) acc += partials[c];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    const float norm = sqrtf(acc);
+    scales[s] = (isfinite(norm) && norm > 0.f) ? 1.0f / fmaxf(norm, eps) : 0.f;
+  }
+}
+
+int launch_momentum(const muon_momentum_seg* segs_dev, int n_segs, int64_t total_chunks, int grad_dtype,
+                    int dir_dtype, float momentum, int nesterov, float eps, float* partials_dev,
+                    float* scales_dev, cudaStream_t stream) {
+  if (n_segs <= 0) return MUON_OK;
+  if (!segs_dev || !partials_dev || !scales_dev) return set_error(MUON_ERR_ARG, "null momentum buffer");
+  if (grad_dtype != MUON_BF16 && grad_dtype != MUON_F32)
+    return set_error(MUON_ERR_ARG, "grad_dtype must be MUON_BF16 or MUON_F32");
+  if (dir_dtype != MUON_BF16 && dir_dtype != MUON_TF32)
+    return set_error(MUON_ERR_ARG, "dir_dtype must be MUON_BF16 or MUON_TF32");
+  if (total_chunks > 0x7fffffffLL) return set_error(MUON_ERR_ARG, "too many momentum chunks");
+  if (total_chunks > 0) {
+    const dim3 grid(static_cast<unsigned>(total_chunks));
+    if (grad_dtype == MUON_BF16 && dir_dtype == MUON_BF16)
+      momentum_kernel<MUON_BF16, MUON_BF16><<<grid, MOM_THREADS, 0, stream>>>(segs_dev, n_segs, momentum, nesterov, partials_dev);
+    else if (grad_dtype == MUON_BF16)
+      momentum_kernel<MUON_BF16, MUON_TF32><<<grid, MOM_THREADS, 0, stream>>>(segs_dev, n_segs, momentum, nesterov, partials_dev);
+    else if (dir_dtype == MUON_BF16)
+      momentum_kernel<MUON_F32, MUON_BF16><<<grid, MOM_THREADS, 0, stream>>>(segs_dev, n_segs, momentum, nesterov, partials_dev);
+    else
+      momentum_kernel<MUON_F32, MUON_TF32><<<grid, MOM_THREADS, 0, stream>>>(segs_dev, n_segs, momentum, nesterov, partials_dev);
+    if (check_cuda(cudaGetLastError(), "momentum launch")) return MUON_ERR_CUDA;
+  }
+  const int warps_per_block = 8;
+  const int blocks = (n_segs + warps_per_block - 1) / warps_per_block;
+  momentum_scale_kernel<<<blocks, warps_per_block * 32, 0, stream>>>(segs_dev, n_segs, total_chunks, partials_dev,
+                                                                      eps, scales_dev);
+  if (check_cuda(cudaGetLastError(), "momentum scale launch")) return MUON_ERR_CUDA;
+  return MUON_OK;
+}
+
+}  // namespace muon

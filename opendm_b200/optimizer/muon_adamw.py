@@ -1,0 +1,532 @@
+"""Drop-in B200 MuonAdamW: Muon for marked 2-D matrices, AdamW for the rest.
+
+Same public surface as the reference ``opendm/optimizer/muon_adamw.py``
+(dexmal/opendm): ``MuonAdamW(model, *, lr, betas, eps, weight_decay,
+muon_momentum, muon_nesterov, muon_ns_steps, muon_lr_scale,
+muon_moonlight_coefficient)``, param groups ``[AdamW, Muon]`` with the same
+keys, ``state_dict``/``load_state_dict`` with the same per-parameter state
+(``step`` 0-d fp32 tensor, ``exp_avg``, ``exp_avg_sq``) and the legacy forms,
+``mark_muon_parameters``, ``is_default_muon_parameter``,
+``zeropower_via_newtonschulz5`` and ``MuonShardPlan``. Parameters marked by
+either library are interchangeable (same attribute names).
+
+The arithmetic runs in the sm_100a kernels of ``libopendm_muon.so`` through
+``opendm_b200.engine``; there is no CPU path. Optional keyword arguments
+(defaults reproduce the reference):
+
+* ``precision``: "tf32" (default; Newton-Schulz operands rounded to tf32,
+  fp32 accumulation) or "bf16" (faster, ~1e-2 relative update error).
+* ``scale_mode``: "reference" (lr * lr_scale * coefficient * sqrt(max(r, c)))
+  or "shape" (lr * lr_scale * max(1, r / c) ** 0.5).
+* ``sharding``: "auto" (default: with world size > 1 and replicated
+  parameters, each matrix is orthogonalised by one owner rank, chosen by
+  FLOP-balanced LPT, and updated parameters are all-gathered) or "off"
+  (every rank runs every matrix, as the reference does).
+* ``state_sharding``: False (default: every rank keeps every momentum buffer
+  current, so ``state_dict()`` on any rank equals the reference's) or True
+  (momentum is advanced only by the owner; call ``consolidate_state_dict()``
+  on all ranks before saving from one rank).
+* ``process_group``: group for the sharded path (default: the world).
+"""
+
+from __future__ import annotations
+
+import math
+from collections.abc import Callable
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from ..engine import AdamItem, CudaMuonEngine, MatrixItem, effective_lr
+from ..sharding import FlatParamBuckets, assign_owners
+
+_MUON_SHAPE = "_opendm_muon_shape"
+_MUON_NAME = "_opendm_muon_name"
+
+
+@dataclass(frozen=True)
+class MuonShardPlan:
+    """How one Muon matrix is laid out over the ranks (reference :15-23).
+
+    kind: "local" (single process, whole matrix), "empty" (no elements here),
+    "owner_only" (one rank holds the whole matrix), "partial" (the matrix is
+    split into flat shards over several ranks) or "replicated" (every rank
+    holds the whole matrix).
+    """
+
+    kind: str
+    full_numel: int
+    local_numel: int
+    sizes: tuple[int, ...]
+    active_ranks: tuple[int, ...]
+    local_offset: int
+    process_group: object | None = None
+
+
+def _dist_ready() -> bool:
+    return dist.is_available() and dist.is_initialized()
+
+
+def _normalize_parameter_name(name: str) -> str:
+    """Strip wrapper prefixes (DDP ``module.``, FSDP ``_fsdp_wrapped_module.``,
+    torch.compile ``_orig_mod.``) repeatedly (reference :30-38)."""
+    prefixes = ("module.", "_fsdp_wrapped_module.", "_orig_mod.")
+    changed = True
+    while changed:
+        changed = False
+        for prefix in prefixes:
+            if name.startswith(prefix):
+                name = name[len(prefix):]
+                changed = True
+                break
+    return name
+
+
+_EXCLUDED_MARKERS = ("embed_tokens", "embedding", "layernorm.weight", "_norm.weight", ".norm.weight", ".norm.")
+
+
+def is_default_muon_parameter(name: str, param: torch.nn.Parameter) -> bool:
+    """Default Muon selection (reference :41-65): trainable 2-D ``.weight``
+    matrices inside the action expert's ``.layers.``, excluding embeddings and
+    norms."""
+    if not param.requires_grad or param.ndim != 2:
+        return False
+    n = _normalize_parameter_name(name)
+    in_expert = n.startswith("model.action_expert.") or n.startswith("action_expert.") or \
+        ".model.action_expert." in n
+    if not in_expert:
+        return False
+    low = n.lower()
+    if ".layers." not in low or not low.endswith(".weight"):
+        return False
+    return not any(m in low for m in _EXCLUDED_MARKERS)
+
+
+def mark_muon_parameters(model: torch.nn.Module,
+                         predicate: Callable[[str, torch.nn.Parameter], bool] | None = None) -> list[str]:
+    """Tag selected parameters with their pre-sharding 2-D shape and name
+    (reference :68-98). Must run before FSDP flattens the parameters."""
+    predicate = predicate or is_default_muon_parameter
+    selected: list[str] = []
+    seen: set[int] = set()
+    for name, param in model.named_parameters():
+        if id(param) in seen:
+            continue
+        seen.add(id(param))
+        for attr in (_MUON_SHAPE, _MUON_NAME):
+            if hasattr(param, attr):
+                delattr(param, attr)
+        if not predicate(name, param):
+            continue
+        if param.ndim != 2:
+            raise RuntimeError(f"Muon parameter {name} must be 2D, got shape {tuple(param.shape)}.")
+        setattr(param, _MUON_SHAPE, (int(param.shape[0]), int(param.shape[1])))
+        setattr(param, _MUON_NAME, name)
+        selected.append(name)
+    if not selected:
+        raise RuntimeError("MuonAdamW selected 0 parameters.")
+    return selected
+
+
+_ENGINES: dict[tuple, CudaMuonEngine] = {}
+
+
+def _engine_for(device: torch.device, precision: str) -> CudaMuonEngine:
+    if device.type != "cuda":
+        raise RuntimeError("opendm_b200 runs on CUDA (sm_100) tensors only; got a tensor on " + str(device))
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx, precision)
+    if key not in _ENGINES:
+        _ENGINES[key] = CudaMuonEngine(torch.device("cuda", idx), precision)
+    return _ENGINES[key]
+
+
+def zeropower_via_newtonschulz5(matrix: torch.Tensor, steps: int = 5, eps: float = 1e-7, *,
+                                precision: str = "tf32") -> torch.Tensor:
+    """Quintic Newton-Schulz orthogonalisation on the GPU (reference :101-128).
+
+    Returns fp32 with the input's shape; a zero or non-finite input gives
+    zeros. Raises ``ValueError`` for non-2-D input and ``RuntimeError`` for
+    tensors that are not on an sm_100 device.
+    """
+    if matrix.ndim != 2:
+        raise ValueError("Muon orthogonalization expects a 2D tensor.")
+    engine = _engine_for(matrix.device, precision)
+    with torch.cuda.device(matrix.device):
+        return engine.orthogonalize(matrix.detach(), steps=max(int(steps), 0), eps=eps)
+
+
+class MuonAdamW(torch.optim.Optimizer):
+    """One optimizer with an AdamW group and a Muon group (reference :178-238)."""
+
+    def __init__(self, model: torch.nn.Module, *, lr: float, betas: tuple[float, float], eps: float,
+                 weight_decay: float, muon_momentum: float = 0.95, muon_nesterov: bool = True,
+                 muon_ns_steps: int = 5, muon_lr_scale: float = 1.0, muon_moonlight_coefficient: float = 0.2,
+                 precision: str = "tf32", scale_mode: str = "reference", sharding: str = "auto",
+                 state_sharding: bool = False, process_group=None, _engine=None) -> None:
+        adamw_params, muon_params, muon_shapes, muon_names = [], [], [], []
+        for param in model.parameters():
+            if not param.requires_grad:
+                continue
+            shape = getattr(param, _MUON_SHAPE, None)
+            if shape is None:
+                adamw_params.append(param)
+            else:
+                muon_params.append(param)
+                muon_shapes.append(tuple(int(d) for d in shape))
+                muon_names.append(getattr(param, _MUON_NAME, None))
+        if not muon_params:
+            raise RuntimeError("MuonAdamW metadata is missing; mark parameters before FSDP wrapping.")
+        if sharding not in ("auto", "off"):
+            raise ValueError(f"sharding must be 'auto' or 'off', got {sharding!r}")
+        if precision not in ("tf32", "bf16"):
+            raise ValueError(f"precision must be 'tf32' or 'bf16', got {precision!r}")
+        effective_lr(1.0, 1.0, 1.0, (1, 1), scale_mode)  # validates scale_mode
+        groups = [
+            {"params": adamw_params, "use_muon": False},
+            {"params": muon_params, "use_muon": True, "muon_shapes": muon_shapes, "muon_names": muon_names},
+        ]
+        defaults = {
+            "lr": lr, "betas": betas, "eps": eps, "weight_decay": weight_decay, "use_muon": False,
+            "muon_momentum": muon_momentum, "muon_nesterov": muon_nesterov, "muon_ns_steps": muon_ns_steps,
+            "muon_lr_scale": muon_lr_scale, "muon_moonlight_coefficient": muon_moonlight_coefficient,
+        }
+        super().__init__(groups, defaults)
+        self._muon_shard_plan_cache: dict[int, list[MuonShardPlan]] = {}
+        self._normalize_param_groups()
+        self.precision = precision
+        self.scale_mode = scale_mode
+        self.sharding = sharding
+        self.state_sharding = bool(state_sharding)
+        self.process_group = process_group
+        self._engine = _engine
+        self._host_steps: dict = {}
+        self._owners: dict[int, list[int]] = {}
+        self._buckets: dict[int, FlatParamBuckets] = {}
+
+    # ---------------------------------------------------------------- groups
+    def _normalize_param_groups(self) -> None:
+        """Fill default keys and normalise Muon metadata, accepting the legacy
+        ``muon_matrix_shapes`` / ``muon_param_infos`` forms (reference :240-276)."""
+        for group in self.param_groups:
+            for key, value in self.defaults.items():
+                group.setdefault(key, value)
+            if not group.get("use_muon", False):
+                continue
+            shapes = group.get("muon_shapes") or group.pop("muon_matrix_shapes", None)
+            names = group.get("muon_names")
+            infos = group.pop("muon_param_infos", None)
+            if shapes is None and infos is not None:
+                shapes = [self._info_shape(info) for info in infos]
+            if names is None and infos is not None:
+                names = [info.get("name") if isinstance(info, dict) else getattr(info, "name", None)
+                         for info in infos]
+            if shapes is None or len(shapes) != len(group["params"]):
+                raise RuntimeError("Muon parameter metadata does not match parameters.")
+            group["muon_shapes"] = [tuple(int(d) for d in s) for s in shapes]
+            names = list(names or [None] * len(shapes))
+            if len(names) != len(shapes):
+                raise RuntimeError("Muon parameter names do not match parameters.")
+            group["muon_names"] = names
+
+    @staticmethod
+    def _info_shape(info):
+        if isinstance(info, dict):
+            return info["matrix_shape"]
+        if hasattr(info, "matrix_shape"):
+            return info.matrix_shape
+        return info[1]
+
+    @staticmethod
+    def _state_for_param(param: torch.Tensor, state: dict) -> dict:
+        """Per-parameter state in the reference layout (:279-306): legacy
+        ``momentum_buffer`` becomes ``exp_avg``; ``step`` is a 0-d fp32 tensor;
+        ``exp_avg``/``exp_avg_sq`` are fp32 on the parameter's device."""
+        if "momentum_buffer" in state:
+            state.setdefault("exp_avg", state.pop("momentum_buffer"))
+        step = state.get("step")
+        if step is None:
+            state["step"] = torch.zeros((), dtype=torch.float32, device=param.device)
+        elif not torch.is_tensor(step):
+            state["step"] = torch.tensor(float(step), dtype=torch.float32, device=param.device)
+        else:
+            if step.numel() != 1:
+                raise RuntimeError("Optimizer step state must contain one value.")
+            state["step"] = step.detach().to(device=param.device, dtype=torch.float32).reshape(())
+        for key in ("exp_avg", "exp_avg_sq"):
+            value = state.get(key)
+            if value is None:
+                state[key] = torch.zeros_like(param, dtype=torch.float32, memory_format=torch.preserve_format)
+            elif value.dtype != torch.float32 or value.device != param.device:
+                state[key] = value.to(device=param.device, dtype=torch.float32)
+        return state
+
+    def load_state_dict(self, state_dict: dict) -> None:
+        """Load current or legacy OpenDM optimizer state (reference :308-317)."""
+        super().load_state_dict(state_dict)
+        self._normalize_param_groups()
+        for group in self.param_groups:
+            for param in group["params"]:
+                state = self.state.get(param)
+                if state:
+                    self._state_for_param(param, state)
+        self._muon_shard_plan_cache.clear()
+        self._host_steps.clear()
+
+    # ----------------------------------------------------------------- step
+    def _get_engine(self, device: torch.device):
+        if self._engine is None:
+            self._engine = _engine_for(device, self.precision)
+        return self._engine
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        for group in self.param_groups:
+            if group.get("use_muon", False):
+                self._muon_step(group)
+            else:
+                self._adamw_step(group)
+        return loss
+
+    def _host_step(self, param, state) -> float:
+        hs = self._host_steps.get(param)
+        if hs is None:
+            hs = float(state["step"].item())
+        return hs
+
+    def _adamw_step(self, group: dict) -> None:
+        items, step_tensors = [], []
+        for param in group["params"]:
+            grad = param.grad
+            if grad is None:
+                continue
+            if grad.is_sparse:
+                raise RuntimeError("MuonAdamW does not support sparse gradients.")
+            state = self._state_for_param(param, self.state[param])
+            hs = self._host_step(param, state) + 1.0
+            self._host_steps[param] = hs
+            step_tensors.append(state["step"])
+            items.append(AdamItem(param.data, grad.detach(), state["exp_avg"], state["exp_avg_sq"], hs))
+        if not items:
+            return
+        torch._foreach_add_(step_tensors, 1.0)
+        beta1, beta2 = group["betas"]
+        self._get_engine(items[0].param.device).adamw(
+            items, lr=float(group["lr"]), beta1=float(beta1), beta2=float(beta2), eps=float(group["eps"]),
+            weight_decay=float(group.get("weight_decay", 0.0) or 0.0))
+
+    @staticmethod
+    def _device_for_params(params: list[torch.Tensor]) -> torch.device:
+        if params:
+            return params[0].device
+        return torch.device("cuda" if torch.cuda.is_available() else "cpu")
+
+    def _muon_group_is_active(self, params: list[torch.Tensor]) -> bool:
+        """True when any rank has a Muon gradient (reference :350-360)."""
+        local_active = any(p.grad is not None for p in params)
+        if not _dist_ready():
+            return local_active
+        flag = torch.tensor(int(local_active), dtype=torch.int32, device=self._device_for_params(params))
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=self.process_group)
+        return bool(flag.item())
+
+    def _world(self) -> tuple[int, int]:
+        if not _dist_ready():
+            return 1, 0
+        return dist.get_world_size(self.process_group), dist.get_rank(self.process_group)
+
+    def _sharded(self, group: dict, plans: list[MuonShardPlan]) -> bool:
+        world, _ = self._world()
+        if self.sharding == "off" or world <= 1:
+            return False
+        return all(p.kind == "replicated" for p in plans) and \
+            all(p.is_contiguous() for p in group["params"])
+
+    def _owners_for(self, group: dict) -> list[int]:
+        key = id(group)
+        owners = self._owners.get(key)
+        if owners is None or len(owners) != len(group["params"]):
+            world, rank = self._world()
+            owners = assign_owners(group["muon_shapes"], world, int(group["muon_ns_steps"]))
+            self._owners[key] = owners
+            self._buckets[key] = FlatParamBuckets(list(group["params"]), owners, world, rank,
+                                                  self.process_group)
+        return owners
+
+    def _muon_step(self, group: dict) -> None:
+        if not self._muon_group_is_active(group["params"]):
+            return
+        momentum = float(group["muon_momentum"])
+        nesterov = bool(group["muon_nesterov"])
+        lr = float(group["lr"])
+        weight_decay = float(group.get("weight_decay", 0.0) or 0.0)
+        wd_factor = (1.0 - lr * weight_decay) if weight_decay else 1.0
+        ns_steps = max(int(group["muon_ns_steps"]), 0)
+        plans = self._get_muon_shard_plans(group)
+        sharded = self._sharded(group, plans)
+        owners = self._owners_for(group) if sharded else None
+        _, rank = self._world()
+
+        owned, others, partial, step_tensors = [], [], [], []
+        for index, (param, shape, plan) in enumerate(zip(group["params"], group["muon_shapes"], plans, strict=True)):
+            if plan.local_numel == 0:
+                continue
+            grad = param.grad
+            if grad is not None and grad.is_sparse:
+                raise RuntimeError("MuonAdamW does not support sparse gradients.")
+            if grad is not None and grad.numel() != param.numel():
+                name = group["muon_names"][index] or index
+                raise RuntimeError(f"Muon gradient shape mismatch for {name}.")
+            state = self._state_for_param(param, self.state[param])
+            step_tensors.append(state["step"])
+            eff = effective_lr(lr, float(group["muon_lr_scale"]), float(group["muon_moonlight_coefficient"]),
+                               shape, self.scale_mode)
+            if plan.kind == "partial":
+                partial.append((param, grad, state, shape, plan, eff))
+                continue
+            item = MatrixItem(param.data.view(shape), grad.detach().view(shape) if grad is not None else None,
+                              state["exp_avg"].view(shape), eff)
+            if owners is not None and owners[index] != rank:
+                if not self.state_sharding:
+                    others.append(item)
+            else:
+                owned.append(item)
+        if step_tensors:
+            torch._foreach_add_(step_tensors, 1.0)
+        device = self._device_for_params(group["params"])
+        engine = self._get_engine(device)
+        engine.muon_matrices(owned, momentum=momentum, nesterov=nesterov, weight_decay_factor=wd_factor,
+                             ns_steps=ns_steps)
+        engine.momentum_only(others, momentum=momentum, nesterov=nesterov)
+        for param, grad, state, shape, plan, eff in partial:
+            self._partial_update(engine, param, grad, state, shape, plan, eff, momentum, nesterov, wd_factor,
+                                 ns_steps)
+        if sharded:
+            self._buckets[id(group)].sync()
+
+    def _partial_update(self, engine, param, grad, state, shape, plan, eff, momentum, nesterov, wd_factor,
+                        ns_steps) -> None:
+        """A matrix split into flat shards over several ranks (FSDP): gather
+        the direction among the active ranks, orthogonalise, keep the local
+        slice (reference :400-414)."""
+        direction = engine.direction(grad.detach().reshape(-1) if grad is not None else None,
+                                     state["exp_avg"].view(-1), momentum=momentum, nesterov=nesterov)
+        full, offset = self._gather_matrix(direction, plan)
+        if full.numel() == 0:
+            return
+        update = engine.orthogonalize(full.view(shape), steps=ns_steps).reshape(-1)
+        local = update.narrow(0, offset, plan.local_numel).view_as(param)
+        if wd_factor != 1.0:
+            param.mul_(wd_factor)
+        param.add_(local.to(param.dtype), alpha=-eff)
+
+    # --------------------------------------------------------- shard plans
+    @staticmethod
+    def _plan_matches_group(group: dict, plans: list[MuonShardPlan]) -> bool:
+        if len(plans) != len(group["params"]):
+            return False
+        world = dist.get_world_size() if _dist_ready() else 1
+        return all(p.full_numel == math.prod(s) and p.local_numel == param.numel() and len(p.sizes) == world
+                   for param, s, p in zip(group["params"], group["muon_shapes"], plans, strict=True))
+
+    def _get_muon_shard_plans(self, group: dict) -> list[MuonShardPlan]:
+        """Cached per-matrix layout plans (reference :430-441)."""
+        key = id(group)
+        plans = self._muon_shard_plan_cache.get(key)
+        if plans is None or not self._plan_matches_group(group, plans):
+            plans = self._build_muon_shard_plans(group)
+            self._muon_shard_plan_cache[key] = plans
+        return plans
+
+    def _build_muon_shard_plans(self, group: dict) -> list[MuonShardPlan]:
+        """Classify every matrix (reference :443-501). With a process group,
+        the local sizes of all matrices are exchanged in one all_gather."""
+        params, shapes = group["params"], group["muon_shapes"]
+        for param, shape in zip(params, shapes, strict=True):
+            full = math.prod(shape)
+            if param.numel() > full:
+                raise RuntimeError(f"Muon matrix {tuple(shape)} has only {full} elements, "
+                                   f"but the local tensor has {param.numel()}.")
+        if not _dist_ready():
+            plans = []
+            for param, shape in zip(params, shapes, strict=True):
+                n, full = int(param.numel()), math.prod(shape)
+                if n not in (0, full):
+                    raise RuntimeError(f"Muon matrix {tuple(shape)} has {n} local elements, expected 0 or {full}.")
+                plans.append(MuonShardPlan("empty" if n == 0 else "local", full, n, (n,), (0,) if n else (), 0))
+            return plans
+        world, rank = dist.get_world_size(), dist.get_rank()
+        device = self._device_for_params(params)
+        local = torch.tensor([int(p.numel()) for p in params], dtype=torch.long, device=device)
+        gathered = [torch.zeros_like(local) for _ in range(world)]
+        dist.all_gather(gathered, local)
+        table = torch.stack(gathered).cpu().tolist()  # [world][n_params]
+        plans = []
+        for j, (param, shape) in enumerate(zip(params, shapes, strict=True)):
+            full = math.prod(shape)
+            sizes = tuple(int(table[r][j]) for r in range(world))
+            active = tuple(r for r, s in enumerate(sizes) if s > 0)
+            total = sum(sizes)
+            pg = None
+            if total == 0:
+                kind = "empty"
+            elif total == full:
+                kind = "owner_only" if len(active) == 1 else "partial"
+                if kind == "partial" and len(active) < world:
+                    pg = dist.new_group(ranks=list(active))
+            elif all(s == full for s in sizes):
+                kind = "replicated"
+            else:
+                raise RuntimeError(f"Muon matrix {tuple(shape)} cannot be reconstructed from local shard sizes {sizes}.")
+            plans.append(MuonShardPlan(kind, full, int(param.numel()), sizes, active, sum(sizes[:rank]), pg))
+        return plans
+
+    @staticmethod
+    def _gather_matrix(local: torch.Tensor, plan: MuonShardPlan) -> tuple[torch.Tensor, int]:
+        """Assemble the full direction of a matrix from its shards (reference :503-535)."""
+        local = local.reshape(-1).contiguous()
+        if local.numel() != plan.local_numel:
+            raise RuntimeError("Muon local tensor no longer matches its shard plan.")
+        if plan.kind == "empty":
+            return local.new_empty(0), 0
+        if plan.kind in {"local", "owner_only", "replicated"}:
+            return local, 0
+        if plan.kind != "partial":
+            raise RuntimeError(f"Unknown Muon shard plan kind: {plan.kind}.")
+        rank = dist.get_rank()
+        if rank not in plan.active_ranks:
+            return local.new_empty(0), plan.local_offset
+        sizes = tuple(plan.sizes[r] for r in plan.active_ranks)
+        padded = local.new_zeros(max(sizes))
+        padded[: local.numel()] = local
+        shards = [torch.empty_like(padded) for _ in sizes]
+        dist.all_gather(shards, padded, group=plan.process_group)
+        return torch.cat([s[:n] for s, n in zip(shards, sizes, strict=True)]), plan.local_offset
+
+    # ----------------------------------------------------------- checkpoints
+    def consolidate_state_dict(self) -> None:
+        """With ``state_sharding=True``: bring every momentum buffer from its
+        owner to all ranks (collective; call on every rank before saving)."""
+        world, _ = self._world()
+        if world <= 1 or not self.state_sharding:
+            return
+        for group in self.param_groups:
+            if not group.get("use_muon", False):
+                continue
+            owners = self._owners.get(id(group))
+            if owners is None:
+                continue
+            for param, owner in zip(group["params"], owners):
+                state = self._state_for_param(param, self.state[param])
+                src = dist.get_global_rank(self.process_group, owner) if self.process_group is not None else owner
+                dist.broadcast(state["exp_avg"], src=src, group=self.process_group)
+
+    def check_device_errors(self) -> None:
+        """Synchronise and raise if a kernel recorded a device error."""
+        if self._engine is not None and hasattr(self._engine, "check_errors"):
+            self._engine.check_errors(block=True)

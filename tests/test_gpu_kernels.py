@@ -1,0 +1,214 @@
+"""GPU parity of the sm_100a kernels against the CPU oracle (and through it,
+the reference). Every call goes through the C ABI (libopendm_muon.so).
+
+Tolerances (relative Frobenius error vs the fp32 reference math):
+  orthogonalised update U: tf32 mode < 5e-3 (bar: 1e-2), bf16 mode < 3e-2
+  exp_avg: bit-exact (same fp32 operations)
+  direction (stored NS operand): within tf32 / bf16 rounding of the fp32 value
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import muon_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TF32_TOL = 5e-3
+BF16_TOL = 3e-2
+
+
+def _dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda", 0)
+
+
+@pytest.fixture(scope="module")
+def engine():
+    from opendm_b200.engine import CudaMuonEngine
+
+    return CudaMuonEngine(_dev(), "tf32")
+
+
+@pytest.fixture(scope="module")
+def engine_bf16():
+    from opendm_b200.engine import CudaMuonEngine
+
+    return CudaMuonEngine(_dev(), "bf16")
+
+
+def _rand(shape, seed, scale=1e-3):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(shape, generator=g) * scale
+
+
+SHAPES = [(64, 64), (48, 96), (96, 48), (33, 70), (70, 33), (1, 16), (128, 32), (256, 256), (130, 300),
+          (300, 130), (512, 2048), (2048, 512), (384, 1152), (1152, 384), (1000, 1000)]
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+def test_orthogonalize_matches_oracle_tf32(engine, shape):
+    x = _rand(shape, hash(shape) % 1000) * 1.95
+    got = engine.orthogonalize(x.to(engine.device)).cpu().numpy()
+    torch.cuda.synchronize()
+    engine.check_errors(block=True)
+    ref = O.zeropower_via_newtonschulz5(x.numpy())
+    err = O.rel_frobenius(got, ref)
+    assert got.shape == ref.shape
+    assert err < TF32_TOL, err
+
+
+@pytest.mark.parametrize("shape", [(64, 64), (96, 48), (512, 2048), (2048, 512), (130, 300)])
+def test_orthogonalize_matches_oracle_bf16(engine_bf16, shape):
+    x = _rand(shape, 7) * 1.95
+    got = engine_bf16.orthogonalize(x.to(engine_bf16.device)).cpu().numpy()
+    engine_bf16.check_errors(block=True)
+    err = O.rel_frobenius(got, O.zeropower_via_newtonschulz5(x.numpy()))
+    assert err < BF16_TOL, err
+
+
+def test_orthogonalize_golden_cases(engine, golden_dir):
+    z = np.load(os.path.join(golden_dir, "ns_cases.npz"))
+    for i in range(int(z["n_cases"])):
+        x = torch.from_numpy(z[f"in{i}"]).to(engine.device)
+        got = engine.orthogonalize(x, steps=int(z[f"steps{i}"])).cpu().numpy()
+        assert O.rel_frobenius(got, z[f"out{i}"]) < TF32_TOL, i
+    for key in ("zero", "inf"):
+        got = engine.orthogonalize(torch.from_numpy(z[f"in_{key}"]).to(engine.device)).cpu().numpy()
+        assert not got.any(), key
+    engine.check_errors(block=True)
+
+
+def test_orthogonalize_steps_variants(engine):
+    x = _rand((80, 200), 3)
+    for steps in (0, 1, 2, 3, 7):
+        got = engine.orthogonalize(x.to(engine.device), steps=steps).cpu().numpy()
+        ref = O.zeropower_via_newtonschulz5(x.numpy(), steps=steps)
+        assert O.rel_frobenius(got, ref) < TF32_TOL, steps
+
+
+def test_orthogonalize_heavy_tail(engine):
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(1024, 1024, generator=g) * 1e-3
+    mask = torch.rand(1024, 1024, generator=g) < 0.01
+    x[mask] = torch.randn(int(mask.sum()), generator=g) * 1e-1
+    got = engine.orthogonalize(x.to(engine.device)).cpu().numpy()
+    assert O.rel_frobenius(got, O.zeropower_via_newtonschulz5(x.numpy())) < TF32_TOL
+
+
+def test_orthogonalize_bf16_input(engine):
+    x = _rand((256, 512), 5).to(torch.bfloat16)
+    got = engine.orthogonalize(x.to(engine.device)).cpu().numpy()
+    ref = O.zeropower_via_newtonschulz5(x.float().numpy())
+    assert O.rel_frobenius(got, ref) < TF32_TOL
+
+
+def _items(shapes, dtype, seed, device, with_grad=True):
+    from opendm_b200.engine import MatrixItem
+
+    items, host = [], []
+    for i, s in enumerate(shapes):
+        p = _rand(s, seed + i, 0.02).to(dtype)
+        g = _rand(s, seed + 100 + i, 1e-3).to(dtype)
+        m = _rand(s, seed + 200 + i, 1e-3)
+        items.append(MatrixItem(p.to(device), g.to(device) if with_grad else None, m.clone().to(device),
+                                O.effective_lr(0.02, 1.0, 0.2, s)))
+        host.append((p.float().numpy(), g.float().numpy() if with_grad else None, m.numpy()))
+    return items, host
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_full_matrix_step_grouped(engine, dtype):
+    """Several shape classes (wide, tall, square, repeated) in one grouped plan:
+    momentum, Newton-Schulz and the fused weight decay + update."""
+    shapes = [(256, 256), (256, 256), (128, 512), (512, 128), (512, 128), (96, 160), (64, 64)]
+    items, host = _items(shapes, dtype, 10, engine.device)
+    lr, wd = 0.02, 0.01
+    engine.muon_matrices(items, momentum=0.95, nesterov=True, weight_decay_factor=1 - lr * wd, ns_steps=5)
+    torch.cuda.synchronize()
+    engine.check_errors(block=True)
+    pdt = "bfloat16" if dtype == torch.bfloat16 else "float32"
+    for it, (p, g, m) in zip(items, host):
+        m_ref, d = O.momentum_direction(g, m, 0.95, True)
+        np.testing.assert_array_equal(it.exp_avg.cpu().numpy(), m_ref)
+        u = O.zeropower_via_newtonschulz5(d)
+        p_ref = O.apply_update(p, u, lr=lr, weight_decay=wd, eff=it.eff, param_dtype=pdt, device_semantics="cuda")
+        got = it.param.float().cpu().numpy()
+        # parameters: within 1e-3 relative (the bar); the fp32 check is far tighter in practice
+        assert O.rel_frobenius(got, p_ref) < 1e-3, O.rel_frobenius(got, p_ref)
+        # the update itself, recovered from the parameter change (fp32 only)
+        if dtype == torch.float32:
+            p_wd = p * np.float32(1 - lr * wd)
+            u_got = (p_wd - got) / np.float32(it.eff)
+            assert O.rel_frobenius(u_got, u) < TF32_TOL
+
+
+def test_second_step_uses_momentum(engine):
+    shapes = [(128, 256), (256, 128)]
+    items, host = _items(shapes, torch.float32, 40, engine.device)
+    for _ in range(2):
+        engine.muon_matrices(items, momentum=0.95, nesterov=True, weight_decay_factor=1.0, ns_steps=5)
+    torch.cuda.synchronize()
+    for it, (p, g, m) in zip(items, host):
+        m1, _ = O.momentum_direction(g, m, 0.95, True)
+        m2, _ = O.momentum_direction(g, m1, 0.95, True)
+        np.testing.assert_array_equal(it.exp_avg.cpu().numpy(), m2)
+
+
+def test_absent_grad_and_plain_momentum(engine):
+    shapes = [(64, 128), (128, 64)]
+    items, host = _items(shapes, torch.float32, 60, engine.device, with_grad=False)
+    engine.muon_matrices(items, momentum=0.9, nesterov=False, weight_decay_factor=1.0, ns_steps=5)
+    torch.cuda.synchronize()
+    for it, (p, g, m) in zip(items, host):
+        m_ref, d = O.momentum_direction(None, m, 0.9, False)
+        np.testing.assert_array_equal(it.exp_avg.cpu().numpy(), m_ref)
+        u = O.zeropower_via_newtonschulz5(d)
+        p_ref = O.apply_update(p, u, lr=0.02, weight_decay=0.0, eff=it.eff, param_dtype="float32")
+        assert O.rel_frobenius(it.param.cpu().numpy(), p_ref) < 1e-3
+
+
+def test_momentum_only(engine):
+    from opendm_b200.engine import MatrixItem
+
+    g = _rand((300, 77), 1).to(engine.device)
+    m = _rand((300, 77), 2).to(engine.device)
+    ref, _ = O.momentum_direction(g.cpu().numpy(), m.cpu().numpy(), 0.95, True)
+    engine.momentum_only([MatrixItem(torch.empty(0), g, m, 0.0)], momentum=0.95, nesterov=True)
+    np.testing.assert_array_equal(m.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("pdt,gdt", [(torch.float32, torch.float32), (torch.bfloat16, torch.bfloat16),
+                                     (torch.bfloat16, torch.float32)])
+def test_adamw_matches_oracle(engine, pdt, gdt):
+    from opendm_b200.engine import AdamItem
+
+    shapes = [(1000,), (64, 33), (4096,), (7,)]
+    items, host = [], []
+    for i, s in enumerate(shapes):
+        p = _rand(s, 300 + i, 0.02).to(pdt)
+        g = _rand(s, 400 + i, 1e-3).to(gdt)
+        items.append(AdamItem(p.to(engine.device), g.to(engine.device), torch.zeros(s, device=engine.device),
+                              torch.zeros(s, device=engine.device), 1.0))
+        host.append((p.float().numpy(), g.float().numpy()))
+    engine.adamw(items, lr=1e-3, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.01)
+    torch.cuda.synchronize()
+    name = "bfloat16" if pdt == torch.bfloat16 else "float32"
+    for it, (p, g) in zip(items, host):
+        z = np.zeros_like(p)
+        p_ref, m_ref, v_ref, _ = O.adamw_step(p, g, z, z, 0.0, lr=1e-3, beta1=0.9, beta2=0.95, eps=1e-8,
+                                              weight_decay=0.01, param_dtype=name)
+        assert O.rel_frobenius(it.exp_avg.cpu().numpy(), m_ref) < 1e-6
+        assert O.rel_frobenius(it.exp_avg_sq.cpu().numpy(), v_ref) < 1e-6
+        assert O.rel_frobenius(it.param.float().cpu().numpy(), p_ref) < (1e-3 if pdt == torch.bfloat16 else 1e-6)
+
+
+def test_rejects_cpu_tensors():
+    from opendm_b200.engine import CudaMuonEngine
+
+    with pytest.raises(RuntimeError):
+        CudaMuonEngine("cpu")

@@ -1,0 +1,312 @@
+"""Host logic of the drop-in optimizer on CPU: grouping, state layout, legacy
+state, error conventions, selection, shard planning. The arithmetic is the
+oracle's (tests/oracle_engine.py), so these tests need no GPU; the GPU tests
+check the same flows through the CUDA library."""
+
+import copy
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import muon_oracle as O
+from opendm_b200.optimizer import (MuonAdamW, MuonShardPlan, is_default_muon_parameter, mark_muon_parameters,
+                                   zeropower_via_newtonschulz5)
+from opendm_b200.optimizer.muon_adamw import _normalize_parameter_name
+from opendm_b200.sharding import assign_owners, load_balance, ns_cost
+from tests.oracle_engine import OracleEngine
+
+
+class GoldenModel(torch.nn.Module):
+    """Parameters named and shaped as in tests/golden/make_golden.py."""
+
+    def __init__(self, z, dtype):
+        super().__init__()
+        keys = [k.split("/", 1)[1] for k in z.files if k.startswith("init/")]
+        for k in keys:
+            self.register_parameter(k, torch.nn.Parameter(torch.from_numpy(z[f"init/{k}"]).to(dtype)))
+        self.muon_keys = set(z["muon_keys"].tolist())
+
+
+def _golden(golden_dir, name):
+    return np.load(os.path.join(golden_dir, name))
+
+
+def _build(z, dtype, **kw):
+    model = GoldenModel(z, dtype)
+    mark_muon_parameters(model, predicate=lambda n, p: n in model.muon_keys)
+    opt = MuonAdamW(model, lr=float(z["meta_lr"]), betas=(0.9, 0.95), eps=1e-8, weight_decay=float(z["meta_wd"]),
+                    muon_nesterov=bool(z["meta_nesterov"]), _engine=OracleEngine(), **kw)
+    return model, opt
+
+
+def _set_grads(model, z, s, dtype):
+    for k, p in model.named_parameters():
+        g = z[f"grad{s}/{k}"]
+        p.grad = None if np.isnan(g).all() else torch.from_numpy(g).to(dtype)
+
+
+@pytest.mark.parametrize("name,dtype", [("step_fp32.npz", torch.float32), ("step_nonesterov.npz", torch.float32),
+                                        ("step_bf16.npz", torch.bfloat16)])
+def test_dropin_matches_reference_steps(golden_dir, name, dtype):
+    z = _golden(golden_dir, name)
+    model, opt = _build(z, dtype)
+    for s in range(int(z["meta_steps"])):
+        _set_grads(model, z, s, dtype)
+        opt.step()
+        for k, p in model.named_parameters():
+            ref = z[f"param{s}/{k}"]
+            got = p.detach().float().numpy()
+            if dtype == torch.float32:
+                assert O.rel_frobenius(got, ref) < 1e-6, (s, k)
+            else:
+                assert np.sum(got != ref) <= max(2, 2e-3 * got.size), (s, k)
+    for k, p in model.named_parameters():
+        st = opt.state[p]
+        assert O.rel_frobenius(st["exp_avg"].numpy(), z[f"exp_avg/{k}"]) < 1e-6
+        assert float(st["step"]) == float(z[f"step/{k}"])
+        assert st["step"].dtype == torch.float32 and st["step"].shape == ()
+
+
+def test_state_dict_layout_matches_reference(golden_dir):
+    z = _golden(golden_dir, "step_bf16.npz")
+    with open(os.path.join(golden_dir, "state_layout.json")) as f:
+        layout = json.load(f)
+    model, opt = _build(z, torch.bfloat16)
+    _set_grads(model, z, 0, torch.bfloat16)
+    opt.step()
+    sd = opt.state_dict()
+    assert len(sd["param_groups"]) == len(layout["param_groups"])
+    for got, ref in zip(sd["param_groups"], layout["param_groups"]):
+        assert got["params"] == ref["params"]
+        for key, value in ref.items():
+            if key in ("n_params", "params"):
+                continue
+            if value is None and key in ("muon_shapes", "muon_names"):
+                assert key not in got
+                continue
+            v = got[key]
+            v = [list(x) for x in v] if key == "muon_shapes" else (list(v) if isinstance(v, tuple) else v)
+            assert v == value, key
+        assert set(got) == {k for k, v in ref.items() if k not in ("n_params",) and
+                            not (v is None and k in ("muon_shapes", "muon_names"))}
+    assert set(sd["state"]) == {int(k) for k in layout["state"]}
+    for k, entry in layout["state"].items():
+        st = sd["state"][int(k)]
+        assert set(st) == set(entry)
+        for sk, (dt, shape) in entry.items():
+            assert str(st[sk].dtype) == dt and list(st[sk].shape) == shape
+
+
+def test_state_dict_round_trip_continues_identically(golden_dir):
+    z = _golden(golden_dir, "step_fp32.npz")
+    model_a, opt_a = _build(z, torch.float32)
+    _set_grads(model_a, z, 0, torch.float32)
+    opt_a.step()
+    sd = copy.deepcopy(opt_a.state_dict())  # as if saved to disk and loaded back
+    model_b, opt_b = _build(z, torch.float32)
+    with torch.no_grad():
+        for pa, pb in zip(model_a.parameters(), model_b.parameters()):
+            pb.copy_(pa)
+    opt_b.load_state_dict(sd)
+    for s in (1, 2):
+        _set_grads(model_a, z, s, torch.float32)
+        _set_grads(model_b, z, s, torch.float32)
+        opt_a.step()
+        opt_b.step()
+    for pa, pb in zip(model_a.parameters(), model_b.parameters()):
+        torch.testing.assert_close(pa, pb, rtol=0, atol=0)
+
+
+def test_load_legacy_state_forms(golden_dir):
+    z = _golden(golden_dir, "step_fp32.npz")
+    model, opt = _build(z, torch.float32)
+    _set_grads(model, z, 0, torch.float32)
+    opt.step()
+    sd = opt.state_dict()
+    legacy = {"state": {}, "param_groups": []}
+    for idx, st in sd["state"].items():
+        legacy["state"][idx] = {"momentum_buffer": st["exp_avg"].clone(), "exp_avg_sq": st["exp_avg_sq"].clone(),
+                                "step": float(st["step"])}
+    adam_g, muon_g = [dict(g) for g in sd["param_groups"]]
+    shapes = muon_g.pop("muon_shapes")
+    names = muon_g.pop("muon_names")
+    muon_g["muon_param_infos"] = [{"matrix_shape": s, "name": n} for s, n in zip(shapes, names)]
+    legacy["param_groups"] = [adam_g, muon_g]
+    model2, opt2 = _build(z, torch.float32)
+    opt2.load_state_dict(legacy)
+    g = opt2.param_groups[1]
+    assert g["muon_shapes"] == [tuple(s) for s in shapes] and g["muon_names"] == names
+    for p in g["params"]:
+        st = opt2.state[p]
+        assert "momentum_buffer" not in st and st["exp_avg"].dtype == torch.float32
+        assert torch.is_tensor(st["step"]) and st["step"].dtype == torch.float32
+    # tuple-form infos and muon_matrix_shapes
+    muon_g2 = dict(sd["param_groups"][1])
+    muon_g2["muon_matrix_shapes"] = muon_g2.pop("muon_shapes")
+    muon_g2.pop("muon_names")
+    model3, opt3 = _build(z, torch.float32)
+    opt3.load_state_dict({"state": sd["state"], "param_groups": [sd["param_groups"][0], muon_g2]})
+    assert opt3.param_groups[1]["muon_shapes"] == [tuple(s) for s in shapes]
+    assert opt3.param_groups[1]["muon_names"] == [None] * len(shapes)
+    infos_t = [(n, s) for s, n in zip(shapes, names)]
+    muon_g3 = dict(sd["param_groups"][1])
+    muon_g3.pop("muon_shapes")
+    muon_g3.pop("muon_names")
+    muon_g3["muon_param_infos"] = infos_t
+    model4, opt4 = _build(z, torch.float32)
+    opt4.load_state_dict({"state": sd["state"], "param_groups": [sd["param_groups"][0], muon_g3]})
+    assert opt4.param_groups[1]["muon_shapes"] == [tuple(s) for s in shapes]
+
+
+def test_bad_state_and_metadata_raise(golden_dir):
+    z = _golden(golden_dir, "step_fp32.npz")
+    model, opt = _build(z, torch.float32)
+    p = opt.param_groups[1]["params"][0]
+    with pytest.raises(RuntimeError, match="one value"):
+        opt._state_for_param(p, {"step": torch.zeros(2)})
+    opt.param_groups[1]["muon_shapes"] = opt.param_groups[1]["muon_shapes"][:-1]
+    with pytest.raises(RuntimeError, match="metadata does not match"):
+        opt._normalize_param_groups()
+    opt.param_groups[1]["muon_shapes"] = [(1, 1)] * len(opt.param_groups[1]["params"])
+    opt.param_groups[1]["muon_names"] = ["x"]
+    with pytest.raises(RuntimeError, match="names do not match"):
+        opt._normalize_param_groups()
+
+
+class Tiny(torch.nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.model = torch.nn.Module()
+        self.model.action_expert = torch.nn.Module()
+        self.model.action_expert.layers = torch.nn.ModuleList([torch.nn.Linear(8, 16, bias=True)])
+        self.model.action_expert.norm = torch.nn.LayerNorm(8)
+        self.model.embed_tokens = torch.nn.Embedding(10, 8)
+        self.head = torch.nn.Linear(8, 4)
+
+
+def test_default_selection_and_marking():
+    m = Tiny()
+    names = mark_muon_parameters(m)
+    assert names == ["model.action_expert.layers.0.weight"]
+    w = m.model.action_expert.layers[0].weight
+    assert w._opendm_muon_shape == (16, 8) and w._opendm_muon_name == names[0]
+    assert not hasattr(m.head.weight, "_opendm_muon_shape")
+    assert is_default_muon_parameter("module._fsdp_wrapped_module.model.action_expert.layers.3.mlp.up.weight",
+                                     torch.nn.Parameter(torch.zeros(2, 2)))
+    assert not is_default_muon_parameter("model.action_expert.layers.3.input_layernorm.weight",
+                                         torch.nn.Parameter(torch.zeros(2, 2)))
+    assert not is_default_muon_parameter("model.action_expert.layers.3.x.weight",
+                                         torch.nn.Parameter(torch.zeros(2, 2), requires_grad=False))
+    assert not is_default_muon_parameter("model.language.layers.3.x.weight", torch.nn.Parameter(torch.zeros(2, 2)))
+    assert _normalize_parameter_name("module._orig_mod.module.x") == "x"
+
+
+def test_marking_errors_and_missing_metadata():
+    m = Tiny()
+    with pytest.raises(RuntimeError, match="selected 0"):
+        mark_muon_parameters(m, predicate=lambda n, p: False)
+    with pytest.raises(RuntimeError, match="must be 2D"):
+        mark_muon_parameters(m, predicate=lambda n, p: n.endswith("bias"))
+    with pytest.raises(RuntimeError, match="metadata is missing"):
+        MuonAdamW(Tiny(), lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0, _engine=OracleEngine())
+    mark_muon_parameters(m)
+    for kw in ({"precision": "fp8"}, {"sharding": "zero3"}, {"scale_mode": "x"}):
+        with pytest.raises(ValueError):
+            MuonAdamW(m, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0, _engine=OracleEngine(), **kw)
+
+
+def test_sparse_and_mismatched_grads_raise():
+    m = Tiny()
+    mark_muon_parameters(m)
+    opt = MuonAdamW(m, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0, _engine=OracleEngine())
+    w = m.model.action_expert.layers[0].weight
+    w.grad = torch.zeros(16, 8)
+    w.grad.data = torch.zeros(3)  # a flat shard whose gradient does not match
+    with pytest.raises(RuntimeError, match="shape mismatch"):
+        opt.step()
+    w.grad = torch.zeros(16, 8).to_sparse()
+    with pytest.raises(RuntimeError, match="sparse"):
+        opt.step()
+    w.grad = None
+    m.head.weight.grad = torch.zeros(4, 8).to_sparse()
+    with pytest.raises(RuntimeError, match="sparse"):
+        opt.step()
+
+
+def test_param_groups_order_and_defaults():
+    m = Tiny()
+    mark_muon_parameters(m)
+    opt = MuonAdamW(m, lr=2e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, muon_ns_steps=3,
+                    _engine=OracleEngine())
+    g0, g1 = opt.param_groups
+    assert g0["use_muon"] is False and g1["use_muon"] is True
+    for g in (g0, g1):
+        for k in ("lr", "betas", "eps", "weight_decay", "muon_momentum", "muon_nesterov", "muon_ns_steps",
+                  "muon_lr_scale", "muon_moonlight_coefficient"):
+            assert k in g
+    assert g1["muon_shapes"] == [(16, 8)] and g1["muon_names"] == ["model.action_expert.layers.0.weight"]
+    assert g1["muon_ns_steps"] == 3
+
+
+def test_muon_group_inactive_without_grads():
+    m = Tiny()
+    mark_muon_parameters(m)
+    eng = OracleEngine()
+    opt = MuonAdamW(m, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0, _engine=eng)
+    before = m.model.action_expert.layers[0].weight.detach().clone()
+    opt.step()
+    assert eng.calls["muon"] == 0
+    assert torch.equal(before, m.model.action_expert.layers[0].weight)
+    assert opt.state == {} or all(not s for s in opt.state.values())
+
+
+def test_closure_and_lr_read_each_step():
+    m = Tiny()
+    mark_muon_parameters(m)
+    opt = MuonAdamW(m, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0, _engine=OracleEngine())
+    x = torch.randn(4, 8)
+
+    def closure():
+        opt.zero_grad()
+        loss = m.head(m.model.action_expert.layers[0].weight.t() @ torch.ones(16, 8) @ x.t()).sum() if False else \
+            (m.model.action_expert.layers[0](x).sum() + m.head(x).sum())
+        loss.backward()
+        return loss
+
+    loss = opt.step(closure)
+    assert torch.is_tensor(loss)
+    w = m.model.action_expert.layers[0].weight
+    before = w.detach().clone()
+    for g in opt.param_groups:
+        g["lr"] = 0.0
+    opt.step(closure)
+    assert torch.equal(before, w)  # lr is read from the group at every step
+
+
+def test_zeropower_cpu_has_no_fallback():
+    with pytest.raises(ValueError):
+        zeropower_via_newtonschulz5(torch.zeros(2, 3, 4))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        zeropower_via_newtonschulz5(torch.ones(4, 4))
+
+
+def test_shard_plan_dataclass_matches_reference_fields():
+    p = MuonShardPlan("local", 6, 6, (6,), (0,), 0)
+    assert p.process_group is None and p.kind == "local"
+    with pytest.raises(Exception):
+        p.kind = "x"  # frozen
+
+
+def test_lpt_assignment_balances_and_is_deterministic():
+    shapes = [(2048, 2048)] * 56 + [(256, 2048)] * 56 + [(8192, 2048)] * 56 + [(2048, 8192)] * 28
+    for world in (2, 4, 8):
+        owners = assign_owners(shapes, world)
+        assert owners == assign_owners(shapes, world)
+        assert set(owners) == set(range(world))
+        lb = load_balance(shapes, owners, world)
+        assert lb["max_over_mean"] < 1.02, lb
+    assert assign_owners(shapes, 1) == [0] * len(shapes)
+    assert ns_cost((8, 4)) == ns_cost((4, 8)) == 5 * (4 * 16 * 8 + 2 * 64)
