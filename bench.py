@@ -1,0 +1,437 @@
+"""Benchmark: one full MuonAdamW optimizer step (Muon + AdamW groups).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c4|c5]
+                    [--precision tf32|bf16] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
+
+Workloads (synthetic, seeded; shapes of the configurations the reference's
+metric is quoted on):
+  c2  2B-class decoder, 28 layers, hidden 2048, GQA q/o 2048x2048, k/v 256x2048,
+      SwiGLU gate/up 8192x2048, down 2048x8192 (196 Muon matrices) + norms and a
+      151936x2048 embedding on AdamW. Default; at N > 1 the same model is
+      sharded over the ranks (strong scaling).
+  c4  ~4B VLA stack: ViT 27x (1152, MLP 4304) + LM 36x (2560, kv 512, MLP 9728)
+      + action expert 18x (1024, MLP 4096), 540 Muon matrices + norms.
+  c5  7B-class decoder, 32 layers, hidden 4096, MLP 11008 (224 Muon matrices),
+      gradients with 1% heavy-tail entries.
+Parameters bf16 ~ N(0, 0.02), gradients bf16 ~ N(0, 1e-3), fp32 optimizer state.
+
+Rank 0 prints one JSON line. `value` is the device time of one optimizer step
+(max over ranks, CUDA events, K steps after W warm-up steps). `e2e` is the
+same step measured through the public API with the gradients copied in from
+pinned host memory every step and a slice of the updated parameters read
+back. `roofline` is the Newton-Schulz GEMMs' dense FLOP rate against the
+measured bf16 tensor peak. `cpu_baseline` (N = 1, rank 0) is the numpy oracle
+of the reference algorithm on the host cores, timed on one matrix of every
+shape class and extrapolated by multiplicity.
+
+--impl reference prints the same metric for the reference algorithm on the
+host CPU (the numpy oracle; the reference itself is PyTorch code that runs
+only from its own checkout), rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+LR, BETAS, EPS, WD = 0.02, (0.9, 0.95), 1e-8, 0.01
+MOMENTUM, NS_STEPS = 0.95, 5
+
+
+def decoder_layers(prefix, layers, hidden, q_out, kv_out, mlp, o_in=None):
+    """(name, shape) of one decoder-style stack; nn.Linear weights are [out, in]."""
+    o_in = o_in or q_out
+    out = []
+    for i in range(layers):
+        p = f"{prefix}.layers.{i}"
+        out += [(f"{p}.self_attn.q_proj.weight", (q_out, hidden)),
+                (f"{p}.self_attn.k_proj.weight", (kv_out, hidden)),
+                (f"{p}.self_attn.v_proj.weight", (kv_out, hidden)),
+                (f"{p}.self_attn.o_proj.weight", (hidden, o_in)),
+                (f"{p}.mlp.gate_proj.weight", (mlp, hidden)),
+                (f"{p}.mlp.up_proj.weight", (mlp, hidden)),
+                (f"{p}.mlp.down_proj.weight", (hidden, mlp)),
+                (f"{p}.input_layernorm.weight", (hidden,)),
+                (f"{p}.post_attention_layernorm.weight", (hidden,))]
+    return out
+
+
+def vit_layers(prefix, layers, hidden, mlp):
+    out = []
+    for i in range(layers):
+        p = f"{prefix}.layers.{i}"
+        out += [(f"{p}.self_attn.q_proj.weight", (hidden, hidden)),
+                (f"{p}.self_attn.k_proj.weight", (hidden, hidden)),
+                (f"{p}.self_attn.v_proj.weight", (hidden, hidden)),
+                (f"{p}.self_attn.out_proj.weight", (hidden, hidden)),
+                (f"{p}.mlp.fc1.weight", (mlp, hidden)),
+                (f"{p}.mlp.fc2.weight", (hidden, mlp)),
+                (f"{p}.layer_norm1.weight", (hidden,)),
+                (f"{p}.layer_norm2.weight", (hidden,))]
+    return out
+
+
+def config_params(name: str):
+    if name == "c2":
+        return (decoder_layers("model", 28, 2048, 2048, 256, 8192)
+                + [("model.embed_tokens.weight", (151936, 2048)), ("model.norm.weight", (2048,))])
+    if name == "c4":
+        return (vit_layers("vision", 27, 1152, 4304)
+                + decoder_layers("language", 36, 2560, 2560, 512, 9728)
+                + decoder_layers("action_expert", 18, 1024, 1024, 1024, 4096)
+                + [("language.norm.weight", (2560,)), ("action_expert.norm.weight", (1024,))])
+    if name == "c5":
+        return decoder_layers("model", 32, 4096, 4096, 4096, 11008) + [("model.norm.weight", (4096,))]
+    raise ValueError(f"unknown config {name!r}")
+
+
+def is_muon(name, shape):
+    return len(shape) == 2 and ".layers." in name
+
+
+DESCRIPTIONS = {
+    "c2": "2B-class decoder (28L, h2048, GQA kv256, SwiGLU 8192) + 151936x2048 embedding",
+    "c4": "~4B VLA (ViT 27L h1152/4304 + LM 36L h2560 kv512/9728 + AE 18L h1024/4096)",
+    "c5": "7B-class decoder (32L, h4096, MHA, SwiGLU 11008), 1% heavy-tail grads",
+}
+
+
+# ------------------------------------------------------------------ helpers
+def ns_flops(shape, steps=NS_STEPS):
+    m, n = min(shape), max(shape)
+    return steps * (4.0 * m * m * n + 2.0 * m ** 3)
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d["bf16_tflops_sustained"]), "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.gpus = {str(i) for i in gpu_indices}
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9 or f[0] not in self.gpus:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------ CPU oracle leg
+def cpu_sample(cfg: str, seed: int = 0):
+    """Time the numpy oracle on one matrix of every Muon shape class plus a
+    slice of every AdamW tensor, and extrapolate to the full step (ms)."""
+    import numpy as np
+
+    from oracle import muon_oracle as O
+
+    rng = np.random.default_rng(seed)
+    params = config_params(cfg)
+    classes: dict = {}
+    adam_elems = 0
+    for name, shape in params:
+        if is_muon(name, shape):
+            classes[shape] = classes.get(shape, 0) + 1
+        else:
+            adam_elems += math.prod(shape)
+    total = 0.0
+    for shape, count in classes.items():
+        p = O.bf16_round(rng.standard_normal(shape, dtype=np.float32) * 0.02)
+        g = O.bf16_round(rng.standard_normal(shape, dtype=np.float32) * 1e-3)
+        m = np.zeros(shape, np.float32)
+        t0 = time.perf_counter()
+        m, d = O.momentum_direction(g, m, MOMENTUM, True)
+        u = O.zeropower_via_newtonschulz5(d, NS_STEPS)
+        O.apply_update(p, u, lr=LR, weight_decay=WD, eff=O.effective_lr(LR, 1.0, 0.2, shape),
+                       param_dtype="bfloat16")
+        total += (time.perf_counter() - t0) * count
+    n_adam = min(adam_elems, 1 << 22)
+    p = O.bf16_round(rng.standard_normal(n_adam, dtype=np.float32) * 0.02)
+    g = O.bf16_round(rng.standard_normal(n_adam, dtype=np.float32) * 1e-3)
+    z = np.zeros(n_adam, np.float32)
+    t0 = time.perf_counter()
+    O.adamw_step(p, g, z, z, 0.0, lr=LR, beta1=BETAS[0], beta2=BETAS[1], eps=EPS, weight_decay=WD,
+                 param_dtype="bfloat16")
+    total += (time.perf_counter() - t0) * (adam_elems / n_adam)
+    sample = (f"numpy oracle: 1 matrix per Muon shape class ({len(classes)} classes) x multiplicity + AdamW on "
+              f"{n_adam} of {adam_elems} elements, extrapolated")
+    return total * 1e3, sample
+
+
+def cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg = args.config
+    for _ in range(args.warmup):
+        cpu_sample(cfg)
+    times = []
+    sample = ""
+    for _ in range(args.steps):
+        ms, sample = cpu_sample(cfg)
+        times.append(ms)
+    value = statistics.median(times)
+    line = {"metric": "muon_step_ms", "value": round(value, 3), "unit": "ms", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value, 3),
+            "higher_is_better": False, "scaling": "strong" if args.gpus > 1 else "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": cfg, "description": DESCRIPTIONS[cfg], "parallelism": "cpu",
+                       "precision": "fp32 (reference algorithm)"},
+            "cpu_baseline": {"value": round(value, 3), "unit": "ms", "cores": cores(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# -------------------------------------------------------------- GPU leg
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    from datetime import timedelta
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+
+    from opendm_b200.optimizer import MuonAdamW, mark_muon_parameters
+
+    cfg = args.config
+    spec = config_params(cfg)
+    gen = torch.Generator(device=device).manual_seed(0)
+
+    class Model(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.names = []
+            for name, shape in spec:
+                t = torch.randn(shape, generator=gen, device=device, dtype=torch.float32).mul_(0.02)
+                self.register_parameter(name.replace(".", "_"), torch.nn.Parameter(t.to(torch.bfloat16)))
+                self.names.append(name)
+
+    model = Model()
+    keymap = {name.replace(".", "_"): (name, shape) for name, shape in spec}
+    mark_muon_parameters(model, predicate=lambda n, p: is_muon(*keymap[n]))
+    opt = MuonAdamW(model, lr=LR, betas=BETAS, eps=EPS, weight_decay=WD, muon_momentum=MOMENTUM,
+                    muon_ns_steps=NS_STEPS, precision=args.precision, state_sharding=world > 1)
+    params = list(model.parameters())
+    ggen = torch.Generator(device=device).manual_seed(1)
+    grads = []
+    for p in params:
+        g = torch.randn(p.shape, generator=ggen, device=device, dtype=torch.float32).mul_(1e-3)
+        if cfg == "c5" and p.ndim == 2:
+            mask = torch.rand(p.shape, generator=ggen, device=device) < 0.01
+            g = torch.where(mask, torch.randn(p.shape, generator=ggen, device=device) * 1e-1, g)
+        grads.append(g.to(torch.bfloat16))
+    for p, g in zip(params, grads):
+        p.grad = g
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        opt.step()
+    engine = opt._engine
+    opt.check_device_errors()
+
+    # ---- device-timed region
+    peaks = load_peaks()
+    sampler = ClockSampler([local] if world == 1 else list(range(world))) if rank == 0 else None
+    launches0 = engine.kernel_launches
+    engine.profile_events = []
+    sync_all()
+    if sampler:
+        sampler.start()
+        time.sleep(0.5)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        opt.step()
+    end.record()
+    sync_all()
+    clocks = sampler.stop() if sampler else None
+    step_ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    launches = (engine.kernel_launches - launches0) // args.steps
+    events = engine.profile_events
+    engine.profile_events = None
+    opt.check_device_errors()
+    per = {}
+    for name, s, e in events:
+        per.setdefault(name, []).append(s.elapsed_time(e))
+    ns_ms = max_over_ranks(statistics.mean(per.get("ns", [0.0]))) if per.get("ns") else 0.0
+    mom_ms = statistics.mean(per.get("momentum", [0.0])) if per.get("momentum") else 0.0
+    adam_ms = statistics.mean(per.get("adamw", [0.0])) if per.get("adamw") else 0.0
+    upd_ms = statistics.mean(per.get("update", [0.0])) if per.get("update") else 0.0
+
+    muon_shapes = [s for n, s in spec if is_muon(n, s)]
+    total_flops = sum(ns_flops(s) for s in muon_shapes)
+    # FLOPs this rank ran (its owned matrices); the roofline uses the busiest rank.
+    owners = opt._owners.get(id(opt.param_groups[1]))
+    if owners is not None:
+        my_flops = sum(ns_flops(s) for s, o in zip(opt.param_groups[1]["muon_shapes"], owners) if o == rank)
+        my_elems = sum(math.prod(s) for s, o in zip(opt.param_groups[1]["muon_shapes"], owners) if o == rank)
+    else:
+        my_flops = total_flops
+        my_elems = sum(math.prod(s) for s in muon_shapes)
+    ns_tflops = my_flops / (ns_ms * 1e-3) / 1e12 if ns_ms > 0 else 0.0
+    ns_tflops = -max_over_ranks(-ns_tflops)  # slowest rank
+    # grad (bf16) + exp_avg read/write + direction write (+ the fp16 convert pass)
+    mom_bytes = my_elems * {"tf32": 2 + 4 + 4 + 4, "bf16": 2 + 4 + 4 + 2, "fp16": 2 + 8 + 4 + 4 + 2}[args.precision]
+    mom_gbs = mom_bytes / (mom_ms * 1e-3) / 1e9 if mom_ms > 0 else 0.0
+    adam_elems = sum(math.prod(s) for n, s in spec if not is_muon(n, s))
+    adam_gbs = adam_elems * (2 + 2 + 8 + 8 + 2) / (adam_ms * 1e-3) / 1e9 if adam_ms > 0 else 0.0
+
+    # ---- end-to-end through the public API with host-resident gradients
+    host_grads = [g.cpu().pin_memory() for g in grads]
+    probe = params[-1] if params[-1].ndim == 1 else params[0]
+    readback = torch.empty(min(probe.numel(), 4096), dtype=probe.dtype).pin_memory()
+    h2d = sum(g.numel() * g.element_size() for g in host_grads)
+    d2h = readback.numel() * readback.element_size()
+    e2e_steps = max(2, min(args.steps, 5))
+    sync_all()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for _ in range(e2e_steps):
+        for p, hg in zip(params, host_grads):
+            p.grad.copy_(hg, non_blocking=True)
+        opt.step()
+        readback.copy_(probe.detach().reshape(-1)[: readback.numel()], non_blocking=True)
+    e_end.record()
+    sync_all()
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_end) / e2e_steps)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        ms, sample = cpu_sample(cfg)
+        cpu = {"value": round(ms, 1), "unit": "ms", "cores": cores(), "kind": "port", "sample": sample}
+
+    if rank == 0:
+        peak = peaks["bf16_tflops_sustained"]
+        line = {
+            "metric": "muon_step_ms", "value": round(step_ms, 3), "unit": "ms", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3),
+            "higher_is_better": False, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "dtype": args.precision, "data": "synthetic",
+            "config": {"workload": cfg, "description": DESCRIPTIONS[cfg], "muon_matrices": len(muon_shapes),
+                       "ns_tflop_per_step": round(total_flops / 1e12, 2), "precision": args.precision,
+                       "parallelism": f"dp{world}" + (" (FLOP-balanced NS owners, bf16 param all-gather,"
+                                                      " owner-only momentum)" if world > 1 else ""),
+                       "l2": "inputs larger than L2 (params+grads+state >> 126 MB)"},
+            "e2e": {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": int(launches) * args.steps,
+            "roofline": {"bound": "tensor", "kernel": "ns_gemm (15 grouped launches per step)",
+                         "achieved": round(ns_tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(ns_tflops / peak, 4), "peak_source": f"{peaks['source']} bf16 sustained",
+                         "frac_of_tf32_peak": round(ns_tflops / (peak / 2), 4) if args.precision == "tf32" else None,
+                         "mma_kind": "kind::tf32" if args.precision == "tf32" else "kind::f16",
+                         "traffic": None, "ns_ms": round(ns_ms, 3)},
+            "elementwise": {"momentum_ms": round(mom_ms, 3), "momentum_gbs": round(mom_gbs, 1),
+                            "update_ms": round(upd_ms, 3),
+                            "update_gbs": round(my_elems * 6 / (upd_ms * 1e-3) / 1e9, 1) if upd_ms > 0 else 0.0,
+                            "adamw_ms": round(adam_ms, 3), "adamw_gbs": round(adam_gbs, 1),
+                            "hbm_peak_gbs": peaks["hbm_gbs"]},
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c2", choices=["c2", "c4", "c5"])
+    ap.add_argument("--precision", default="tf32", choices=["tf32", "fp16", "bf16"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -46,7 +46,8 @@ enum muon_status {
 enum muon_dtype {
   MUON_BF16 = 0, /* bfloat16 storage */
   MUON_F32 = 1,  /* float32 storage */
-  MUON_TF32 = 2  /* float32 storage holding values rounded to tf32 (NS operands) */
+  MUON_TF32 = 2, /* float32 storage holding values rounded to tf32 (NS operands) */
+  MUON_F16 = 3   /* float16 storage (NS operands, scaled by powers of two) */
 };
 
 /* ------------------------------------------------------------------ misc */
@@ -64,6 +65,12 @@ int muon_device_check(int device);
  * Returns MUON_ERR_KERNEL when the word is nonzero, and clears it. */
 int muon_read_error(int* err_dev, int* host_code, void* stream);
 
+/* Failure-detection self test (no counterpart in the reference): launches a
+ * kernel whose bounded wait on a barrier that nothing completes expires after
+ * `timeout_us` (1..1e6) and records code 0x1ff in *err_dev, leaving the
+ * context usable. Read the result with muon_read_error. */
+int muon_selftest_bounded_wait(int* err_dev, int timeout_us, void* stream);
+
 /* --------------------------------------------- (a) momentum + Nesterov
  * Replaces muon_adamw.py:381-394 (step += 1 is done by the host):
  *   g = grad.float() (zeros when grad is absent)
@@ -73,8 +80,10 @@ int muon_read_error(int* err_dev, int* host_code, void* stream);
  * sum of d^2 is reduced and turned into the Newton-Schulz input scale
  *   scale = 0                       if the norm is 0 or not finite
  *   scale = 1 / max(norm, eps)      otherwise.
- * d is written rounded to `dir_dtype` (MUON_BF16 or MUON_TF32) into
- * `direction` with row stride `ld` (the matrix keeps the parameter's layout).
+ * d is written rounded to `dir_dtype` into `direction` with row stride `ld`
+ * (the matrix keeps the parameter's layout): MUON_BF16 / MUON_TF32 write the
+ * Newton-Schulz operand directly; MUON_F32 writes d unrounded, for
+ * muon_convert_f16 to normalise and round afterwards.
  */
 typedef struct muon_momentum_seg {
   const void* grad;    /* [rows*cols] of grad_dtype, or NULL for an absent grad */
@@ -94,6 +103,33 @@ int muon_momentum(const muon_momentum_seg* segs_dev, int n_segs, int64_t total_c
                   float* partials_dev /* [total_chunks] scratch */,
                   float* scales_dev /* [n_segs] out */, void* stream);
 
+/* ------------------------------------------- fp16 operand preparation
+ * fp16 has tf32's 11-bit significand but a narrow exponent range, so the
+ * fp16 Newton-Schulz input is written after normalisation:
+ *   dst = 0                                  if scales[scale_index] == 0
+ *   dst = fp16(src * (scales[scale_index] * mul))   otherwise,
+ * with mul = muon_ns_operand_scale(rows, cols, 0, MUON_F16), a power of two
+ * that brings the entries of the unit-norm matrix to magnitude ~1.
+ */
+typedef struct muon_convert_seg {
+  const float* src;    /* [rows][ld_src] fp32 direction (muon_momentum, MUON_F32) */
+  void* dst;           /* [rows][ld_dst] fp16 (a class's x0 slot) */
+  int64_t rows;
+  int64_t cols;
+  int64_t ld_src;
+  int64_t ld_dst;
+  int64_t chunk_begin; /* prefix sum of muon_momentum_chunks() */
+  float mul;
+  int32_t scale_index;
+} muon_convert_seg;
+
+int muon_convert_f16(const muon_convert_seg* segs_dev, int n_segs, int64_t total_chunks,
+                     const float* scales_dev, void* stream);
+
+/* Power-of-two scale of the stored operand X at Newton-Schulz iteration
+ * `iteration` for op_dtype MUON_F16 (1.0 for the other types). */
+float muon_ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dtype);
+
 /* ------------------------------------ (b) Newton-Schulz orthogonalisation
  * Replaces zeropower_via_newtonschulz5 (muon_adamw.py:101-128) for a set of
  * same-shape matrices ("class"), and optionally the update of
@@ -101,73 +137,92 @@ int muon_momentum(const muon_momentum_seg* segs_dev, int n_segs, int64_t total_c
  *
  * The quintic iteration X <- a X + (b A + c A A) X, A = X X^T, is evaluated
  * in the algebraically identical form
- *   A' = X X^T - I,  M = alpha I + beta A' + gamma A' A',  X <- M X,
+ *   A' = X X^T - I,   B' = gamma A' + beta I,   M = alpha I + A' B',   X <- M X,
  *   alpha = a + b + c, beta = b + 2c, gamma = c,
  * which avoids cancellation between a X and (b A + c A A) X when the operands
- * are rounded (tf32 or bf16) for the tensor cores. A matrix with rows > cols
- * is orthogonalised through its transpose, as in the reference; here the
+ * are rounded (tf32, fp16 or bf16) for the tensor cores, and lets every
+ * epilogue work from its accumulator alone. A matrix with rows > cols is
+ * orthogonalised through its transpose, as in the reference; here the
  * transpose is expressed by operand majorness, so X keeps the parameter's
  * layout and no transposed copy is made.
  *
- * Each class owns four caller-provided buffers of op dtype (MUON_BF16:
- * 2 bytes, MUON_TF32: 4 bytes per element):
- *   x0, x1: [count][rows][ld_x]  (x0 holds the direction written by
- *           muon_momentum; x1 is the ping-pong partner)
- *   ap, mm: [count][m][ld_m]     m = min(rows, cols)
- * ld_x and ld_m must make rows 16-byte aligned (multiple of 8 for bf16, of 4
- * for tf32), and every buffer must be 16-byte aligned.
+ * Each class owns five caller-provided buffers of op dtype (MUON_BF16 and
+ * MUON_F16: 2 bytes, MUON_TF32: 4 bytes per element):
+ *   x0, x1:     [count][rows][ld_x]  (x0 holds the direction written by
+ *               muon_momentum, or by muon_convert_f16 for MUON_F16, which
+ *               stores it normalised; x1 is the ping-pong partner)
+ *   ap, bp, mm: [count][m][ld_m]     m = min(rows, cols)
+ * ld_x and ld_m must make rows 16-byte aligned (multiple of 8 for 2-byte,
+ * of 4 for 4-byte types), and every buffer must be 16-byte aligned.
  * `scales` holds the per-matrix input scale produced by muon_momentum.
  *
- * Output of the last iteration, per class:
- *   u_out != NULL: U = orthogonalised update, fp32 [count][rows][ld_u];
- *   params != NULL: in-place parameter update, for matrix i of the class
- *       p = p * wd_factor   (skipped when wd_factor == 1)
- *       p = p - eff * cast(U, param_dtype)
- *     with the reference's rounding order for bf16 parameters.
- *   Exactly one of u_out / params must be set.
+ * The last iteration writes U, the orthogonalised update, to u_out
+ * ([count][rows][ld_u], any alignment) rounded to u_dtype: MUON_F32 for the
+ * exact fp32 result, or the parameter dtype (MUON_BF16), which is the value
+ * the reference adds to a bf16 parameter (muon_adamw.py:414 casts the update
+ * to the parameter's dtype first). muon_apply_update then applies it.
  */
 typedef struct muon_ns_class {
   int32_t rows;
   int32_t cols;
   int32_t count;
-  int32_t param_dtype; /* MUON_BF16 or MUON_F32 (used when params != NULL) */
+  int32_t u_dtype; /* MUON_F32 or MUON_BF16 */
   void* x0;
   void* x1;
   int64_t ld_x;
   void* ap;
+  void* bp;
   void* mm;
   int64_t ld_m;
   const float* scales; /* [count] device */
-  float* u_out;        /* optional [count][rows][ld_u] fp32 */
+  void* u_out;         /* [count][rows][ld_u] of u_dtype */
   int64_t ld_u;
-  void* const* params; /* optional device array [count] of parameter pointers ([rows][cols]) */
 } muon_ns_class;
 
 typedef struct muon_ns_plan muon_ns_plan;
 
 /* Build launch descriptors (tensor maps, tile schedules) for `n_classes`
  * classes iterated `steps` times with operands of `op_dtype`
- * (MUON_TF32 or MUON_BF16). The plan stores pointers, not data: buffers must
+ * (MUON_TF32, MUON_F16 or MUON_BF16). The plan stores pointers, not data: buffers must
  * outlive it and stay at the same addresses. */
 int muon_ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, int steps,
                         muon_ns_plan** plan_out);
 
-/* Run the plan: 3 grouped GEMM launches per iteration. `eff` is a host array
- * [n_classes] of lr * lr_scale * coefficient * scale(shape) and wd_factor is
- * 1 - lr * weight_decay; both are read at launch time, so a scheduler may
- * change lr between steps. `err_dev` is a device int (0 before the call). */
-int muon_ns_plan_run(const muon_ns_plan* plan, const float* eff, float wd_factor, int* err_dev,
-                     void* stream);
+/* Run the plan: 3 grouped GEMM launches per iteration. `err_dev` is a device
+ * int (0 before the call). */
+int muon_ns_plan_run(const muon_ns_plan* plan, int* err_dev, void* stream);
 
 void muon_ns_plan_destroy(muon_ns_plan* plan);
 
-/* Bytes of one class's workspace when x0, x1, ap and mm are carved from a
+/* Bytes of one class's workspace when x0, x1, ap, bp and mm are carved from a
  * single buffer with muon_ns_class_layout (each part 256-byte aligned). */
 int64_t muon_ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype);
 
-/* Fill x0/x1/ap/mm/ld_x/ld_m of `cls` from one workspace buffer `base` of
+/* Fill x0/x1/ap/bp/mm/ld_x/ld_m of `cls` from one workspace buffer `base` of
  * muon_ns_class_workspace_bytes() bytes. */
 int muon_ns_class_layout(muon_ns_class* cls, void* base, int op_dtype);
+
+/* ------------------------------------------- (c) weight decay + update
+ * Replaces muon_adamw.py:395-398 and :407-414 for whole matrices, with the
+ * reference's rounding order:
+ *   p = p * wd_factor            rounded to the param dtype (skipped when 1)
+ *   p = p + (-eff) * u           one fused multiply-add, rounded to the param dtype
+ * where u is U already rounded to the param dtype (muon_ns_class.u_dtype) and
+ * eff = lr * lr_scale * coefficient * sqrt(max(rows, cols)) per matrix.
+ * wd_factor = 1 - lr * weight_decay and eff are read at launch time, so a
+ * learning-rate scheduler may change them between steps.
+ */
+typedef struct muon_update_seg {
+  void* param;         /* [numel] of param_dtype, updated in place */
+  const void* update;  /* [numel] of param_dtype */
+  int64_t numel;
+  int64_t chunk_begin; /* prefix sum of muon_momentum_chunks(1, numel) */
+  float eff;
+  int32_t param_dtype; /* MUON_BF16 or MUON_F32 */
+} muon_update_seg;
+
+int muon_apply_update(const muon_update_seg* segs_dev, int n_segs, int64_t total_chunks, float wd_factor,
+                      void* stream);
 
 /* ------------------------------------------------- AdamW fallback group
  * Replaces _adamw_step / _call_adamw_functional (muon_adamw.py:131-175,

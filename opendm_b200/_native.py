@@ -24,6 +24,7 @@ MUON_ERR_KERNEL = 5
 MUON_BF16 = 0
 MUON_F32 = 1
 MUON_TF32 = 2
+MUON_F16 = 3
 
 ABI_VERSION = 1
 
@@ -40,22 +41,47 @@ class MomentumSeg(Structure):
     ]
 
 
+class ConvertSeg(Structure):
+    _fields_ = [
+        ("src", c_void_p),
+        ("dst", c_void_p),
+        ("rows", c_int64),
+        ("cols", c_int64),
+        ("ld_src", c_int64),
+        ("ld_dst", c_int64),
+        ("chunk_begin", c_int64),
+        ("mul", c_float),
+        ("scale_index", c_int32),
+    ]
+
+
 class NsClass(Structure):
     _fields_ = [
         ("rows", c_int32),
         ("cols", c_int32),
         ("count", c_int32),
-        ("param_dtype", c_int32),
+        ("u_dtype", c_int32),
         ("x0", c_void_p),
         ("x1", c_void_p),
         ("ld_x", c_int64),
         ("ap", c_void_p),
+        ("bp", c_void_p),
         ("mm", c_void_p),
         ("ld_m", c_int64),
         ("scales", c_void_p),
         ("u_out", c_void_p),
         ("ld_u", c_int64),
-        ("params", c_void_p),
+    ]
+
+
+class UpdateSeg(Structure):
+    _fields_ = [
+        ("param", c_void_p),
+        ("update", c_void_p),
+        ("numel", c_int64),
+        ("chunk_begin", c_int64),
+        ("eff", c_float),
+        ("param_dtype", c_int32),
     ]
 
 
@@ -80,11 +106,15 @@ SIGNATURES = {
     "muon_last_error": (c_char_p, []),
     "muon_device_check": (c_int, [c_int]),
     "muon_read_error": (c_int, [c_void_p, POINTER(c_int), c_void_p]),
+    "muon_selftest_bounded_wait": (c_int, [c_void_p, c_int, c_void_p]),
     "muon_momentum_chunks": (c_int64, [c_int64, c_int64]),
     "muon_momentum": (c_int, [c_void_p, c_int, c_int64, c_int, c_int, c_float, c_int, c_float, c_void_p,
                               c_void_p, c_void_p]),
+    "muon_convert_f16": (c_int, [c_void_p, c_int, c_int64, c_void_p, c_void_p]),
+    "muon_ns_operand_scale": (c_float, [c_int32, c_int32, c_int, c_int]),
     "muon_ns_plan_create": (c_int, [POINTER(NsClass), c_int, c_int, c_int, POINTER(c_void_p)]),
-    "muon_ns_plan_run": (c_int, [c_void_p, POINTER(c_float), c_float, c_void_p, c_void_p]),
+    "muon_ns_plan_run": (c_int, [c_void_p, c_void_p, c_void_p]),
+    "muon_apply_update": (c_int, [c_void_p, c_int, c_int64, c_float, c_void_p]),
     "muon_ns_plan_destroy": (None, [c_void_p]),
     "muon_ns_class_workspace_bytes": (c_int64, [c_int32, c_int32, c_int32, c_int]),
     "muon_ns_class_layout": (c_int, [POINTER(NsClass), c_void_p, c_int]),

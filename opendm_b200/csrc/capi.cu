@@ -4,9 +4,22 @@
 #include <cstdio>
 #include <string>
 
+#include "common.cuh"
 #include "internal.h"
 
 namespace muon {
+
+// Waits on an mbarrier phase that nothing completes, with a caller-chosen
+// bound: exercises the timeout path of every pipeline wait in this library.
+__global__ void selftest_wait_kernel(int* err, unsigned long long timeout_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, err, kDevSelftest, timeout_ns);
+}
 
 static thread_local std::string g_last_error;
 
@@ -68,6 +81,14 @@ int muon_read_error(int* err_dev, int* host_code, void* stream) {
   return MUON_OK;
 }
 
+int muon_selftest_bounded_wait(int* err_dev, int timeout_us, void* stream) {
+  if (!err_dev) return set_error(MUON_ERR_ARG, "err_dev is null");
+  if (timeout_us < 1 || timeout_us > 1000000) return set_error(MUON_ERR_ARG, "timeout_us must be in [1, 1e6]");
+  muon::selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      err_dev, 1000ull * static_cast<unsigned long long>(timeout_us));
+  return muon::check_cuda(cudaGetLastError(), "selftest launch");
+}
+
 int64_t muon_momentum_chunks(int64_t rows, int64_t cols) { return muon::momentum_chunks(rows, cols); }
 
 int muon_momentum(const muon_momentum_seg* segs_dev, int n_segs, int64_t total_chunks, int grad_dtype,
@@ -77,15 +98,28 @@ int muon_momentum(const muon_momentum_seg* segs_dev, int n_segs, int64_t total_c
                                eps, partials_dev, scales_dev, static_cast<cudaStream_t>(stream));
 }
 
+int muon_convert_f16(const muon_convert_seg* segs_dev, int n_segs, int64_t total_chunks, const float* scales_dev,
+                     void* stream) {
+  return muon::launch_convert(segs_dev, n_segs, total_chunks, scales_dev, static_cast<cudaStream_t>(stream));
+}
+
+float muon_ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dtype) {
+  return muon::ns_operand_scale(rows, cols, iteration, op_dtype);
+}
+
 int muon_ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, int steps,
                         muon_ns_plan** plan_out) {
   if (!classes) return set_error(MUON_ERR_ARG, "classes is null");
   return muon::ns_plan_create(classes, n_classes, op_dtype, steps, plan_out);
 }
 
-int muon_ns_plan_run(const muon_ns_plan* plan, const float* eff, float wd_factor, int* err_dev,
-                     void* stream) {
-  return muon::ns_plan_run(plan, eff, wd_factor, err_dev, static_cast<cudaStream_t>(stream));
+int muon_ns_plan_run(const muon_ns_plan* plan, int* err_dev, void* stream) {
+  return muon::ns_plan_run(plan, err_dev, static_cast<cudaStream_t>(stream));
+}
+
+int muon_apply_update(const muon_update_seg* segs_dev, int n_segs, int64_t total_chunks, float wd_factor,
+                      void* stream) {
+  return muon::launch_apply_update(segs_dev, n_segs, total_chunks, wd_factor, static_cast<cudaStream_t>(stream));
 }
 
 void muon_ns_plan_destroy(muon_ns_plan* plan) { muon::ns_plan_destroy(plan); }

@@ -9,10 +9,16 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace muon {
+
+// Operand element types of the Newton-Schulz GEMMs (values match muon_dtype).
+constexpr int kOpBf16 = 0;  // MUON_BF16: kind::f16, bf16 operands
+constexpr int kOpTf32 = 2;  // MUON_TF32: kind::tf32, fp32 storage rounded to tf32
+constexpr int kOpF16 = 3;   // MUON_F16:  kind::f16, fp16 operands (power-of-two scaled)
 
 // 2 s per individual wait. A healthy pipeline stage completes in microseconds.
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;
@@ -24,6 +30,7 @@ enum DeviceError : int {
   kDevTimeoutTmemFull = 0x103, // epilogue waited for an accumulator
   kDevTimeoutTmemEmpty = 0x104,// MMA waited for a drained accumulator
   kDevTimeoutDrain = 0x105,    // final drain of in-flight work
+  kDevSelftest = 0x1ff,        // muon_selftest_bounded_wait
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -71,7 +78,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
 // Wait until the phase with the given parity completes. Returns false (and
 // records `code` in *err unless an error is already recorded) on timeout, or
 // when another thread of the grid has already recorded an error.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          unsigned long long timeout_ns = kWaitTimeoutNs) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
@@ -79,7 +87,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     if (mbar_try_wait(addr, parity)) return true;
     if ((i & 255u) == 0u) {
       if (*reinterpret_cast<volatile int*>(err) != 0) return false;
-      if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+      if (global_timer_ns() - t0 > timeout_ns) {
         atomicCAS(err, 0, code);
         return false;
       }
@@ -102,12 +110,64 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// 3-D tiled bulk tensor load for a CTA pair (tcgen05 cta_group::2): the data
+// lands in this CTA's shared memory; the transaction bytes are counted on the
+// mbarrier at `bar_cluster`, a shared::cluster address that may belong to the
+// peer CTA of the pair. No multicast.
+__device__ __forceinline__ void tma_load_3d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster,
+                                                 int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// ------------------------------------------------------------- clusters
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the object at CTA-local shared address `addr`
+// in the shared memory of cluster CTA `rank`.
+__device__ __forceinline__ uint32_t map_shared_rank(uint32_t addr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(addr), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Whole-warp TMEM allocation for a CTA pair: one warp with the same warp id
+// in each CTA of the pair issues it with the same smem slot offset.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(smem_slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
 }
 
 // Whole-warp TMEM allocation; the allocated base address is written to smem.
@@ -125,10 +185,10 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
 }
 
 // D[tmem] (+)= A[smem] * B[smem]^T for one UMMA instruction.
-template <bool kTf32>
+template <int kOp>
 __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                      uint32_t idesc, uint32_t accumulate) {
-  if constexpr (kTf32) {
+  if constexpr (kOp == kOpTf32) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
@@ -143,6 +203,38 @@ __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a_desc, uint64_t 
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
   }
+}
+
+// cta_group::2 MMA issued by the pair's leader CTA: A and B operands are
+// split across the two CTAs' shared memory at the same offsets; each CTA's
+// TMEM receives its 128 rows of D.
+template <int kOp>
+__device__ __forceinline__ void umma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  if constexpr (kOp == kOpTf32) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  }
+}
+
+// Arrive on the mbarrier at shared::cluster address `bar_cluster` (this CTA's
+// or its pair peer's) once every cta_group::2 MMA issued so far by this
+// thread has completed.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar_cluster)
+               : "memory");
 }
 
 // Arrive on an mbarrier once every previously issued tcgen05.mma of this
@@ -194,16 +286,17 @@ __device__ __forceinline__ uint64_t make_sw128_desc(uint32_t smem_addr, uint32_t
   return d;
 }
 
-// Instruction descriptor for kind::f16 (bf16 inputs) / kind::tf32, fp32 accumulate.
-__host__ __device__ constexpr uint32_t make_idesc(bool tf32, int m, int n, bool a_mn_major,
+// Instruction descriptor for kind::f16 (fp16 / bf16 inputs) or kind::tf32,
+// fp32 accumulate. A and B always share one format.
+__host__ __device__ constexpr uint32_t make_idesc(int op, int m, int n, bool a_mn_major,
                                                   bool b_mn_major) {
-  return (1u << 4)                                  // D format: f32
-         | ((tf32 ? 2u : 1u) << 7)                  // A format: bf16=1, tf32=2
-         | ((tf32 ? 2u : 1u) << 10)                 // B format
-         | ((a_mn_major ? 1u : 0u) << 15)           // A major
-         | ((b_mn_major ? 1u : 0u) << 16)           // B major
-         | (static_cast<uint32_t>(n >> 3) << 17)    // N >> 3
-         | (static_cast<uint32_t>(m >> 4) << 24);   // M >> 4
+  return (1u << 4)                                                       // D format: f32
+         | ((op == kOpTf32 ? 2u : op == kOpBf16 ? 1u : 0u) << 7)          // A: f16=0 bf16=1 tf32=2
+         | ((op == kOpTf32 ? 2u : op == kOpBf16 ? 1u : 0u) << 10)         // B format
+         | ((a_mn_major ? 1u : 0u) << 15)                                // A major
+         | ((b_mn_major ? 1u : 0u) << 16)                                // B major
+         | (static_cast<uint32_t>(n >> 3) << 17)                         // N >> 3
+         | (static_cast<uint32_t>(m >> 4) << 24);                        // M >> 4
 }
 
 // ---------------------------------------------------------------- rounding
@@ -219,5 +312,7 @@ __device__ __forceinline__ float round_tf32(float x) {
 __device__ __forceinline__ float bf16_round(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
+
+__device__ __forceinline__ float f16_round(float x) { return __half2float(__float2half_rn(x)); }
 
 }  // namespace muon

@@ -25,10 +25,15 @@ int64_t adamw_chunks(int64_t numel);
 
 int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, int steps,
                    muon_ns_plan** plan_out);
-int ns_plan_run(const muon_ns_plan* plan, const float* eff, float wd_factor, int* err_dev,
-                cudaStream_t stream);
+int ns_plan_run(const muon_ns_plan* plan, int* err_dev, cudaStream_t stream);
+int launch_apply_update(const muon_update_seg* segs_dev, int n_segs, int64_t total_chunks, float wd_factor,
+                        cudaStream_t stream);
 void ns_plan_destroy(muon_ns_plan* plan);
 int64_t ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype);
 int ns_class_layout(muon_ns_class* cls, void* base, int op_dtype);
+float ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dtype);
+
+int launch_convert(const muon_convert_seg* segs_dev, int n_segs, int64_t total_chunks,
+                   const float* scales_dev, cudaStream_t stream);
 
 }  // namespace muon

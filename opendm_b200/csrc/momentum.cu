@@ -72,7 +72,11 @@ __device__ __forceinline__ void load_grad8(const void* grad, int64_t e, float (&
 
 template <int kDirDt>
 __device__ __forceinline__ void store_dir8(void* dir, int64_t e, const float (&d)[8]) {
-  if constexpr (kDirDt == MUON_BF16) {
+  if constexpr (kDirDt == MUON_F32) {
+    float4* p = reinterpret_cast<float4*>(reinterpret_cast<float*>(dir) + e);
+    p[0] = make_float4(d[0], d[1], d[2], d[3]);
+    p[1] = make_float4(d[4], d[5], d[6], d[7]);
+  } else if constexpr (kDirDt == MUON_BF16) {
     uint4 raw;
     __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
 #pragma unroll
@@ -97,12 +101,9 @@ __global__ void __launch_bounds__(MOM_THREADS) momentum_kernel(const muon_moment
   const int64_t e0 = (chunk - sg.chunk_begin) * MOM_CHUNK;
   const int64_t e1 = min(e0 + MOM_CHUNK, numel);
   const bool nest = nesterov != 0;
-  const int gsz = kGradDt == MUON_BF16 ? 2 : 4;
-  const int dsz = kDirDt == MUON_BF16 ? 2 : 4;
   const bool vec_ok = sg.ld == sg.cols && (numel % 8) == 0 &&
                       ((reinterpret_cast<uintptr_t>(sg.grad) | reinterpret_cast<uintptr_t>(sg.exp_avg) |
-                        reinterpret_cast<uintptr_t>(sg.direction)) & 15u) == 0 &&
-                      gsz > 0 && dsz > 0;
+                        reinterpret_cast<uintptr_t>(sg.direction)) & 15u) == 0;
   float acc = 0.f;
   if (vec_ok) {
 #pragma unroll 2
@@ -143,6 +144,8 @@ __global__ void __launch_bounds__(MOM_THREADS) momentum_kernel(const muon_moment
       const int64_t di = r * sg.ld + c;
       if constexpr (kDirDt == MUON_BF16)
         reinterpret_cast<__nv_bfloat16*>(sg.direction)[di] = __float2bfloat16_rn(o.d);
+      else if constexpr (kDirDt == MUON_F32)
+        reinterpret_cast<float*>(sg.direction)[di] = o.d;
       else
         reinterpret_cast<float*>(sg.direction)[di] = round_tf32(o.d);
     }
@@ -187,19 +190,23 @@ int launch_momentum(const muon_momentum_seg* segs_dev, int n_segs, int64_t total
   if (!segs_dev || !partials_dev || !scales_dev) return set_error(MUON_ERR_ARG, "null momentum buffer");
   if (grad_dtype != MUON_BF16 && grad_dtype != MUON_F32)
     return set_error(MUON_ERR_ARG, "grad_dtype must be MUON_BF16 or MUON_F32");
-  if (dir_dtype != MUON_BF16 && dir_dtype != MUON_TF32)
-    return set_error(MUON_ERR_ARG, "dir_dtype must be MUON_BF16 or MUON_TF32");
+  if (dir_dtype != MUON_BF16 && dir_dtype != MUON_TF32 && dir_dtype != MUON_F32)
+    return set_error(MUON_ERR_ARG, "dir_dtype must be MUON_BF16, MUON_TF32 or MUON_F32");
   if (total_chunks > 0x7fffffffLL) return set_error(MUON_ERR_ARG, "too many momentum chunks");
   if (total_chunks > 0) {
     const dim3 grid(static_cast<unsigned>(total_chunks));
-    if (grad_dtype == MUON_BF16 && dir_dtype == MUON_BF16)
-      momentum_kernel<MUON_BF16, MUON_BF16><<<grid, MOM_THREADS, 0, stream>>>(segs_dev, n_segs, momentum, nesterov, partials_dev);
-    else if (grad_dtype == MUON_BF16)
-      momentum_kernel<MUON_BF16, MUON_TF32><<<grid, MOM_THREADS, 0, stream>>>(segs_dev, n_segs, momentum, nesterov, partials_dev);
-    else if (dir_dtype == MUON_BF16)
-      momentum_kernel<MUON_F32, MUON_BF16><<<grid, MOM_THREADS, 0, stream>>>(segs_dev, n_segs, momentum, nesterov, partials_dev);
-    else
-      momentum_kernel<MUON_F32, MUON_TF32><<<grid, MOM_THREADS, 0, stream>>>(segs_dev, n_segs, momentum, nesterov, partials_dev);
+#define MUON_MOM_LAUNCH(G, D) \
+  momentum_kernel<G, D><<<grid, MOM_THREADS, 0, stream>>>(segs_dev, n_segs, momentum, nesterov, partials_dev)
+    if (grad_dtype == MUON_BF16) {
+      if (dir_dtype == MUON_BF16) MUON_MOM_LAUNCH(MUON_BF16, MUON_BF16);
+      else if (dir_dtype == MUON_TF32) MUON_MOM_LAUNCH(MUON_BF16, MUON_TF32);
+      else MUON_MOM_LAUNCH(MUON_BF16, MUON_F32);
+    } else {
+      if (dir_dtype == MUON_BF16) MUON_MOM_LAUNCH(MUON_F32, MUON_BF16);
+      else if (dir_dtype == MUON_TF32) MUON_MOM_LAUNCH(MUON_F32, MUON_TF32);
+      else MUON_MOM_LAUNCH(MUON_F32, MUON_F32);
+    }
+#undef MUON_MOM_LAUNCH
     if (check_cuda(cudaGetLastError(), "momentum launch")) return MUON_ERR_CUDA;
   }
   const int warps_per_block = 8;
@@ -207,6 +214,70 @@ int launch_momentum(const muon_momentum_seg* segs_dev, int n_segs, int64_t total
   momentum_scale_kernel<<<blocks, warps_per_block * 32, 0, stream>>>(segs_dev, n_segs, total_chunks, partials_dev,
                                                                       eps, scales_dev);
   if (check_cuda(cudaGetLastError(), "momentum scale launch")) return MUON_ERR_CUDA;
+  return MUON_OK;
+}
+
+// fp16 Newton-Schulz input: normalise, scale by a power of two, round.
+__device__ __forceinline__ int find_convert_segment(const muon_convert_seg* segs, int n_segs, int64_t chunk) {
+  int lo = 0, hi = n_segs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (segs[mid].chunk_begin <= chunk)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(MOM_THREADS) convert_f16_kernel(const muon_convert_seg* __restrict__ segs,
+                                                                  int n_segs, const float* __restrict__ scales) {
+  const int64_t chunk = blockIdx.x;
+  const muon_convert_seg sg = segs[find_convert_segment(segs, n_segs, chunk)];
+  const int64_t numel = sg.rows * sg.cols;
+  const int64_t e0 = (chunk - sg.chunk_begin) * MOM_CHUNK;
+  const int64_t e1 = min(e0 + MOM_CHUNK, numel);
+  const float s = scales[sg.scale_index];
+  const bool zero = !(s != 0.f);
+  const float f = s * sg.mul;
+  __half* dst = reinterpret_cast<__half*>(sg.dst);
+  const bool vec_ok = sg.ld_src == sg.cols && sg.ld_dst == sg.cols && (numel % 8) == 0 &&
+                      ((reinterpret_cast<uintptr_t>(sg.src) | reinterpret_cast<uintptr_t>(sg.dst)) & 15u) == 0;
+  if (vec_ok) {
+    for (int it = 0; it < MOM_ITERS; ++it) {
+      const int64_t e = e0 + (int64_t(it) * MOM_THREADS + threadIdx.x) * MOM_VEC;
+      if (e >= e1) break;
+      const float4* sp = reinterpret_cast<const float4*>(sg.src + e);
+      const float4 a = __ldg(sp), b = __ldg(sp + 1);
+      uint4 raw;
+      __half2* h = reinterpret_cast<__half2*>(&raw);
+      if (zero) {
+        h[0] = h[1] = h[2] = h[3] = __floats2half2_rn(0.f, 0.f);
+      } else {
+        h[0] = __floats2half2_rn(a.x * f, a.y * f);
+        h[1] = __floats2half2_rn(a.z * f, a.w * f);
+        h[2] = __floats2half2_rn(b.x * f, b.y * f);
+        h[3] = __floats2half2_rn(b.z * f, b.w * f);
+      }
+      *reinterpret_cast<uint4*>(dst + e) = raw;
+    }
+  } else {
+    for (int64_t e = e0 + threadIdx.x; e < e1; e += MOM_THREADS) {
+      const int64_t r = e / sg.cols, c = e - r * sg.cols;
+      const float v = zero ? 0.f : sg.src[r * sg.ld_src + c] * f;
+      dst[r * sg.ld_dst + c] = __float2half_rn(v);
+    }
+  }
+}
+
+int launch_convert(const muon_convert_seg* segs_dev, int n_segs, int64_t total_chunks, const float* scales_dev,
+                   cudaStream_t stream) {
+  if (n_segs <= 0 || total_chunks <= 0) return MUON_OK;
+  if (!segs_dev || !scales_dev) return set_error(MUON_ERR_ARG, "null convert buffer");
+  if (total_chunks > 0x7fffffffLL) return set_error(MUON_ERR_ARG, "too many convert chunks");
+  convert_f16_kernel<<<static_cast<unsigned>(total_chunks), MOM_THREADS, 0, stream>>>(segs_dev, n_segs,
+                                                                                       scales_dev);
+  if (check_cuda(cudaGetLastError(), "convert launch")) return MUON_ERR_CUDA;
   return MUON_OK;
 }
 

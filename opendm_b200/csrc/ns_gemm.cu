@@ -3,26 +3,34 @@
 //
 // One launch evaluates one phase of one Newton-Schulz iteration for every
 // matrix of every shape class:
-//   phase 0 (gram):  A' = s^2 X X^T - I               symmetric m x m, K = n
-//   phase 1 (poly):  M  = alpha I + beta A' + gamma A'A'  symmetric m x m, K = m
+//   phase 0 (gram):  A' = s^2 X X^T - I and B' = gamma A' + beta I
+//                                                     symmetric m x m, K = n
+//   phase 1 (poly):  M  = alpha I + A' B'            symmetric m x m, K = m
 //   phase 2 (apply): X  = s M X   (wide)  |  X = s X M  (tall: X kept as the
 //                    parameter's n x m layout, which is the transpose)
-// s is the per-matrix Frobenius scale on the first iteration and 1 after it.
-// The last apply either writes the fp32 update U or applies the fused
-// weight-decay + scaled update to the parameters
-// (reference: muon_adamw.py:395-398, :407-414).
+// s is the per-matrix Frobenius scale on the first iteration and 1 after it
+// (fp16 operands are stored pre-normalised and power-of-two scaled instead).
+// The last apply writes the update U in fp32 or in the parameter dtype.
 //
-// Kernel structure (one CTA per SM, persistent, static round-robin tiles):
-//   warp 0      TMA producer: 128B-swizzled operand tiles into a 4-stage ring
-//   warp 1      TMEM owner and single-thread tcgen05.mma issuer
-//   warps 2..5  epilogue: tcgen05.ld -> registers -> smem transpose ->
-//               coalesced global stores (+ mirrored stores for symmetric C)
-// Accumulators: two 128 x 256 fp32 buffers in TMEM (all 512 columns), so the
-// epilogue of tile i overlaps the main loop of tile i+1.
+// Kernel structure: clusters of 2 CTAs (one per SM), persistent, static
+// round-robin over 256 x 256 tiles. The pair issues cta_group::2 MMAs: CTA r
+// holds rows [128 r, 128 r + 128) of the tile's A operand and of its B
+// operand, and receives rows [128 r, 128 r + 128) of D in its own TMEM, so
+// each SM loads half of B (32 KB per 64-deep K stage instead of 48 KB).
+//   warp 0      TMA producer (both CTAs): a 6-stage ring; the bytes of both
+//               CTAs complete on the leader CTA's full barrier
+//   warp 1      TMEM allocation (both CTAs); single-thread MMA issuer (leader)
+//   warps 2..5  epilogue (both CTAs): tcgen05.ld -> registers -> smem
+//               transpose -> coalesced global stores (+ mirrored stores for
+//               symmetric C)
+// Accumulators: two 128 x 256 fp32 buffers per CTA in TMEM (all 512 columns),
+// so the epilogue of tile i overlaps the main loop of tile i+1. No TMA
+// multicast is used: each CTA loads its own operand halves.
 // Operands are bf16 (kind::f16) or tf32 (kind::tf32); either way a stage
 // holds 128 bytes of K per row, so the byte geometry is identical.
 
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <vector>
@@ -32,22 +40,24 @@
 
 namespace muon {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
-constexpr int STAGES = 4;
+constexpr int BM = 128;          // rows of D per CTA
+constexpr int PAIR_M = 2 * BM;   // rows of D per CTA pair (one tile)
+constexpr int BN = 256;          // columns of D per tile
+constexpr int BN_CTA = BN / 2;   // rows of the B operand each CTA of the pair holds
+constexpr int STAGES = 6;
 constexpr int A_STAGE_BYTES = BM * 128;
-constexpr int B_STAGE_BYTES = BN * 128;
+constexpr int B_STAGE_BYTES = BN_CTA * 128;
 constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int EPI_WARPS = 4;
 constexpr int NUM_THREADS = 64 + EPI_WARPS * 32;
 constexpr int EPI_PITCH = 33;  // floats per staged row (conflict-free transpose)
-constexpr int EPI_BYTES = EPI_WARPS * 32 * EPI_PITCH * 4;
+constexpr int EPI_BYTES = 2 * EPI_WARPS * 32 * EPI_PITCH * 4;  // two staging buffers per warp
 constexpr int BAR_BYTES = 256;
 constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int kMaxProblems = 16;
 
-enum EpiKind : int { EPI_GRAM = 0, EPI_POLY = 1, EPI_APPLY = 2, EPI_APPLY_F32 = 3, EPI_UPDATE = 4 };
+enum EpiKind : int { EPI_GRAM = 0, EPI_POLY = 1, EPI_APPLY = 2, EPI_U_F32 = 3, EPI_U_BF16 = 4 };
 
 // Newton-Schulz quintic coefficients of the reference (muon_adamw.py:123) and
 // the shifted-form coefficients derived from them.
@@ -63,15 +73,11 @@ struct GemmProblem {
   int symmetric;   // compute upper-triangle tiles and mirror them
   int epi;
   int first;       // apply the per-matrix input scale
-  int param_dtype;
-  float eff;
-  float wd_factor;
+  float mul;       // constant multiplier of the accumulator (power of two)
   void* out;
   long long out_ld, out_bs;
-  const void* side;
-  long long side_ld, side_bs;
+  void* out2;      // gram: B' (same geometry as out)
   const float* scale;
-  void* const* params;
 };
 
 struct GemmParams {
@@ -101,13 +107,13 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmParams& P, int t) {
     c.ti = lt / pr.tiles_n;
     c.tj = lt - c.ti * pr.tiles_n;
   } else {
-    // Row block ti holds column blocks [ti/2, tiles_n): exactly the tiles that
-    // contain an element with col >= row.
+    // Square tiles: row block ti holds column blocks [ti, tiles_n), exactly
+    // the tiles that contain an element with col >= row.
     int ti = 0;
     while (true) {
-      const int cnt = pr.tiles_n - (ti >> 1);
+      const int cnt = pr.tiles_n - ti;
       if (lt < cnt) {
-        c.tj = (ti >> 1) + lt;
+        c.tj = ti + lt;
         break;
       }
       lt -= cnt;
@@ -118,40 +124,48 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmParams& P, int t) {
   return c;
 }
 
-template <bool kTf32>
+template <int kOp>
 __device__ __forceinline__ void store_op(void* base, long long idx, float v) {
-  if constexpr (kTf32) {
+  if constexpr (kOp == kOpTf32) {
     reinterpret_cast<float*>(base)[idx] = v;
-  } else {
+  } else if constexpr (kOp == kOpBf16) {
     reinterpret_cast<__nv_bfloat16*>(base)[idx] = __float2bfloat16_rn(v);
+  } else {
+    reinterpret_cast<__half*>(base)[idx] = __float2half_rn(v);
   }
 }
 
-template <bool kTf32>
+template <int kOp>
 __device__ __forceinline__ float round_op(float v) {
-  if constexpr (kTf32) {
+  if constexpr (kOp == kOpTf32) {
     return round_tf32(v);
-  } else {
+  } else if constexpr (kOp == kOpBf16) {
     return bf16_round(v);
-  }
-}
-
-template <bool kTf32>
-__device__ __forceinline__ float load_op(const void* base, long long idx) {
-  if constexpr (kTf32) {
-    return reinterpret_cast<const float*>(base)[idx];
   } else {
-    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[idx]);
+    return f16_round(v);
   }
 }
 
-template <bool kTf32>
-__global__ void __launch_bounds__(NUM_THREADS, 1) ns_gemm_kernel(const __grid_constant__ GemmParams P) {
+template <int kOp>
+__device__ __forceinline__ float load_op(const void* base, long long idx) {
+  if constexpr (kOp == kOpTf32) {
+    return reinterpret_cast<const float*>(base)[idx];
+  } else if constexpr (kOp == kOpBf16) {
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[idx]);
+  } else {
+    return __half2float(reinterpret_cast<const __half*>(base)[idx]);
+  }
+}
+
+template <int kOp>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    ns_gemm_kernel(const __grid_constant__ GemmParams P) {
+  constexpr bool kTf32 = kOp == kOpTf32;
   constexpr int ES = kTf32 ? 4 : 2;
   constexpr int BKE = 128 / ES;     // K elements per stage == MN elements per swizzle atom
   constexpr int UMMA_K = 32 / ES;   // K elements per tcgen05.mma
   constexpr int KSTEPS = BKE / UMMA_K;
-  // MN-major operands: bf16 uses the 128B swizzle (8-row K groups, SBO 1024);
+  // MN-major operands: 16-bit types use the 128B swizzle (8-row K groups, SBO 1024);
   // tf32 must use the 32-byte-atom 128B swizzle (4-row K groups, SBO 512).
   constexpr uint32_t kMnLayout = kTf32 ? kLayoutSw128Base32 : kLayoutSw128;
   constexpr uint32_t kMnSbo = kTf32 ? 512 : 1024;
@@ -172,6 +186,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ns_gemm_kernel(const __grid_co
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0: leader (issues the MMAs)
+  const int cluster_id = blockIdx.x >> 1;
+  const int n_clusters = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -180,7 +197,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ns_gemm_kernel(const __grid_co
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], EPI_WARPS);
+      mbar_init(&tempty[a], 2 * EPI_WARPS);  // epilogue warps of both CTAs (leader's copy is used)
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -191,9 +208,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ns_gemm_kernel(const __grid_co
       tma_prefetch_desc(&P.map_b[p]);
     }
   }
-  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+  if (warp == 1) tmem_alloc_pair(tmem_slot, TMEM_COLS);
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // peer barriers initialised and TMEM allocated in both CTAs
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -206,33 +224,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ns_gemm_kernel(const __grid_co
       uint32_t issued_phase[STAGES];
       for (int s = 0; s < STAGES; ++s) issued[s] = 0, issued_phase[s] = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < P.total_tiles; t += gridDim.x) {
+      for (int t = cluster_id; ok && t < P.total_tiles; t += n_clusters) {
         const TileCoord tc = decode_tile(P, t);
         const GemmProblem& pr = P.prob[tc.p];
         const int kb_count = (pr.K + BKE - 1) / BKE;
-        const int m0 = tc.ti * BM, n0 = tc.tj * BN;
+        const int m0 = tc.ti * PAIR_M + static_cast<int>(rank) * BM;
+        const int n0 = tc.tj * BN + static_cast<int>(rank) * BN_CTA;
         for (int kb = 0; kb < kb_count; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, P.err, kDevTimeoutEmpty)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
+          const uint32_t bar = map_shared_rank(smem_u32(&full[stage]), 0);
           uint8_t* sa = stage_a + stage * A_STAGE_BYTES;
           uint8_t* sb = stage_b + stage * B_STAGE_BYTES;
           const int k0 = kb * BKE;
           if (!pr.a_mn) {
-            tma_load_3d(sa, &P.map_a[tc.p], &full[stage], k0, m0, tc.g);
+            tma_load_3d_pair(sa, &P.map_a[tc.p], bar, k0, m0, tc.g);
           } else {
 #pragma unroll
             for (int j = 0; j < BM / BKE; ++j)
-              tma_load_3d(sa + j * BKE * 128, &P.map_a[tc.p], &full[stage], m0 + j * BKE, k0, tc.g);
+              tma_load_3d_pair(sa + j * BKE * 128, &P.map_a[tc.p], bar, m0 + j * BKE, k0, tc.g);
           }
           if (!pr.b_mn) {
-            tma_load_3d(sb, &P.map_b[tc.p], &full[stage], k0, n0, tc.g);
+            tma_load_3d_pair(sb, &P.map_b[tc.p], bar, k0, n0, tc.g);
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / BKE; ++j)
-              tma_load_3d(sb + j * BKE * 128, &P.map_b[tc.p], &full[stage], n0 + j * BKE, k0, tc.g);
+            for (int j = 0; j < BN_CTA / BKE; ++j)
+              tma_load_3d_pair(sb + j * BKE * 128, &P.map_b[tc.p], bar, n0 + j * BKE, k0, tc.g);
           }
           issued[stage] = 1;
           issued_phase[stage] = phase;
@@ -242,18 +262,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ns_gemm_kernel(const __grid_co
           }
         }
       }
-      // Drain: every issued TMA load must have landed before the CTA exits.
+      // Drain: a stage is released (empty) only after the MMAs that read it
+      // completed, which implies its loads landed.
       for (int s = 0; s < STAGES; ++s)
-        if (issued[s]) mbar_wait(&full[s], issued_phase[s], P.err, kDevTimeoutDrain);
+        if (issued[s]) mbar_wait(&empty[s], issued_phase[s], P.err, kDevTimeoutDrain);
     }
   } else if (warp == 1) {
-    // ----------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------- MMA issuer (leader)
+    if (lane == 0 && rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int local_t = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < P.total_tiles; t += gridDim.x, ++local_t) {
+      for (int t = cluster_id; ok && t < P.total_tiles; t += n_clusters, ++local_t) {
         const TileCoord tc = decode_tile(P, t);
         const GemmProblem& pr = P.prob[tc.p];
         const int kb_count = (pr.K + BKE - 1) / BKE;
@@ -265,7 +286,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ns_gemm_kernel(const __grid_co
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        const uint32_t idesc = make_idesc(kTf32, BM, BN, pr.a_mn != 0, pr.b_mn != 0);
+        const uint32_t idesc = make_idesc(kOp, PAIR_M, BN, pr.a_mn != 0, pr.b_mn != 0);
         for (int kb = 0; kb < kb_count; ++kb) {
           if (!mbar_wait(&full[stage], phase, P.err, kDevTimeoutFull)) {
             ok = false;
@@ -280,27 +301,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ns_gemm_kernel(const __grid_co
                                         : make_sw128_desc(a_addr + kk * 32, 16, 1024);
             const uint64_t bd = pr.b_mn ? make_sw128_desc(b_addr + kk * UMMA_K * 128, BKE * 128, kMnSbo, kMnLayout)
                                         : make_sw128_desc(b_addr + kk * 32, 16, 1024);
-            umma<kTf32>(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+            umma_pair<kOp>(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
-          umma_commit(&empty[stage]);
+          // Release the stage in both CTAs once these MMAs have read it.
+          umma_commit_pair(smem_u32(&empty[stage]));
+          umma_commit_pair(map_shared_rank(smem_u32(&empty[stage]), 1));
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull[acc]);
+        umma_commit_pair(smem_u32(&tfull[acc]));
+        umma_commit_pair(map_shared_rank(smem_u32(&tfull[acc]), 1));
       }
       // Drain: all issued MMAs complete before TMEM is released.
-      umma_commit(drain);
+      umma_commit_pair(smem_u32(drain));
       mbar_wait(drain, 0, P.err, kDevTimeoutDrain);
     }
   } else {
     // ------------------------------------------------------------- epilogue
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     float* buf = epi_buf + (warp - 2) * 32 * EPI_PITCH;
+    const uint32_t leader_tempty0 = map_shared_rank(smem_u32(&tempty[0]), 0);
+    const uint32_t leader_tempty1 = map_shared_rank(smem_u32(&tempty[1]), 0);
     int local_t = 0;
-    for (int t = blockIdx.x; t < P.total_tiles; t += gridDim.x, ++local_t) {
+    for (int t = cluster_id; t < P.total_tiles; t += n_clusters, ++local_t) {
       const TileCoord tc = decode_tile(P, t);
       const GemmProblem& pr = P.prob[tc.p];
       const int acc = local_t & 1;
@@ -317,102 +343,95 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) ns_gemm_kernel(const __grid_co
         sc = pr.scale[tc.g];
         zero = !(sc != 0.f);
       }
-      const int row0 = tc.ti * BM + quad * 32;
+      const float mul = pr.mul;
+      const int row0 = tc.ti * PAIR_M + static_cast<int>(rank) * BM + quad * 32;
       const long long out_off = static_cast<long long>(tc.g) * pr.out_bs;
-      const long long side_off = static_cast<long long>(tc.g) * pr.side_bs;
-      void* param_ptr = (pr.epi == EPI_UPDATE) ? pr.params[tc.g] : nullptr;
+      const float f = pr.first ? sc * sc * mul : mul;  // gram: s^2 * mul
+      const float fa = pr.first ? sc * mul : mul;      // apply: s * mul
+      const bool sym = pr.symmetric != 0;
+      float* buf2 = buf + 32 * EPI_PITCH * EPI_WARPS;   // second staging buffer (gram B')
 
       for (int ch = 0; ch < BN / 32; ++ch) {
         const int col0 = tc.tj * BN + ch * 32;
         float v[32];
         tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + ch * 32, v);
         if (row0 >= pr.M || col0 >= pr.N) continue;
-        if (pr.symmetric && col0 + 31 < row0) continue;  // chunk entirely below the diagonal
+        if (sym && col0 + 31 < row0) continue;  // chunk entirely below the diagonal
+        // Row mode (lane = row): epilogue arithmetic on the accumulator row.
+        const int myrow = row0 + lane;
+        if (pr.epi == EPI_GRAM) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) buf[lane * EPI_PITCH + i] = v[i];
-        __syncwarp();
-        // Column mode: lane = column, walk the 32 rows (coalesced I/O).
-        const int col = col0 + lane;
-        for (int r = 0; r < 32; ++r) {
-          const int row = row0 + r;
-          if (row >= pr.M || col >= pr.N) continue;
-          if (pr.symmetric && col < row) continue;
-          const float a = buf[r * EPI_PITCH + lane];
-          const long long idx = static_cast<long long>(row) * pr.out_ld + col;
-          float res;
-          switch (pr.epi) {
-            case EPI_GRAM: {
-              float x = zero ? 0.f : (pr.first ? (sc * sc) * a : a);
-              if (row == col) x -= 1.f;
-              res = round_op<kTf32>(x);
-              store_op<kTf32>(pr.out, out_off + idx, res);
-              break;
-            }
-            case EPI_POLY: {
-              const float s = load_op<kTf32>(pr.side, side_off + static_cast<long long>(row) * pr.side_ld + col);
-              float x = fmaf(P.gamma, a, P.beta * s);
-              if (row == col) x += P.alpha;
-              res = round_op<kTf32>(x);
-              store_op<kTf32>(pr.out, out_off + idx, res);
-              break;
-            }
-            case EPI_APPLY: {
-              const float x = zero ? 0.f : (pr.first ? sc * a : a);
-              res = round_op<kTf32>(x);
-              store_op<kTf32>(pr.out, out_off + idx, res);
-              break;
-            }
-            case EPI_APPLY_F32: {
-              res = zero ? 0.f : (pr.first ? sc * a : a);
-              reinterpret_cast<float*>(pr.out)[out_off + idx] = res;
-              break;
-            }
-            default: {  // EPI_UPDATE: parameters are dense [M][N]
-              const float u = zero ? 0.f : (pr.first ? sc * a : a);
-              const long long pidx = static_cast<long long>(row) * pr.N + col;
-              if (pr.param_dtype == MUON_BF16) {
-                __nv_bfloat16* pp = reinterpret_cast<__nv_bfloat16*>(param_ptr);
-                float p = __bfloat162float(pp[pidx]);
-                if (pr.wd_factor != 1.f) p = bf16_round(p * pr.wd_factor);
-                pp[pidx] = __float2bfloat16_rn(fmaf(-pr.eff, bf16_round(u), p));
-              } else {
-                float* pp = reinterpret_cast<float*>(param_ptr);
-                float p = pp[pidx];
-                if (pr.wd_factor != 1.f) p = p * pr.wd_factor;
-                pp[pidx] = fmaf(-pr.eff, u, p);
-              }
-              res = u;
-              break;
-            }
+          for (int i = 0; i < 32; ++i) {
+            const float a = zero ? 0.f : v[i] * f;
+            const float ap = (myrow == col0 + i) ? a - 1.f : a;
+            buf[lane * EPI_PITCH + i] = round_op<kOp>(ap);
+            buf2[lane * EPI_PITCH + i] = round_op<kOp>(fmaf(P.gamma, ap, (myrow == col0 + i) ? P.beta : 0.f));
           }
-          buf[r * EPI_PITCH + lane] = res;
+        } else if (pr.epi == EPI_POLY) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            buf[lane * EPI_PITCH + i] = round_op<kOp>((myrow == col0 + i) ? v[i] + P.alpha : v[i]);
+        } else if (pr.epi == EPI_APPLY) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) buf[lane * EPI_PITCH + i] = round_op<kOp>(zero ? 0.f : v[i] * fa);
+        } else if (pr.epi == EPI_U_BF16) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) buf[lane * EPI_PITCH + i] = bf16_round(zero ? 0.f : v[i] * fa);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) buf[lane * EPI_PITCH + i] = zero ? 0.f : v[i] * fa;
         }
         __syncwarp();
-        if (pr.symmetric) {
-          // Row mode: lane = row; store the strict upper part mirrored (coalesced).
-          const int row = row0 + lane;
-          if (row < pr.M) {
+        // Column mode (lane = column): coalesced stores of the 32 rows.
+        const int col = col0 + lane;
+        if (col < pr.N) {
+          const int rmax = min(32, pr.M - row0);
+          if (pr.epi == EPI_U_F32) {
+            float* o = reinterpret_cast<float*>(pr.out) + out_off + static_cast<long long>(row0) * pr.out_ld + col;
+            for (int r = 0; r < rmax; ++r) o[static_cast<long long>(r) * pr.out_ld] = buf[r * EPI_PITCH + lane];
+          } else if (pr.epi == EPI_U_BF16) {
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(pr.out) + out_off +
+                               static_cast<long long>(row0) * pr.out_ld + col;
+            for (int r = 0; r < rmax; ++r)
+              o[static_cast<long long>(r) * pr.out_ld] = __float2bfloat16_rn(buf[r * EPI_PITCH + lane]);
+          } else {
+            const long long base = out_off + static_cast<long long>(row0) * pr.out_ld + col;
+            for (int r = 0; r < rmax; ++r) {
+              if (sym && col < row0 + r) continue;
+              store_op<kOp>(pr.out, base + static_cast<long long>(r) * pr.out_ld, buf[r * EPI_PITCH + lane]);
+              if (pr.epi == EPI_GRAM)
+                store_op<kOp>(pr.out2, base + static_cast<long long>(r) * pr.out_ld, buf2[r * EPI_PITCH + lane]);
+            }
+          }
+        }
+        if (sym) {
+          // Row mode again: the strict upper part, mirrored (coalesced).
+          if (myrow < pr.M) {
+            const long long base = out_off + myrow;
             for (int j = 0; j < 32; ++j) {
               const int c2 = col0 + j;
-              if (c2 > row && c2 < pr.N)
-                store_op<kTf32>(pr.out, out_off + static_cast<long long>(c2) * pr.out_ld + row,
-                                buf[lane * EPI_PITCH + j]);
+              if (c2 > myrow && c2 < pr.N) {
+                store_op<kOp>(pr.out, base + static_cast<long long>(c2) * pr.out_ld, buf[lane * EPI_PITCH + j]);
+                if (pr.epi == EPI_GRAM)
+                  store_op<kOp>(pr.out2, base + static_cast<long long>(c2) * pr.out_ld, buf2[lane * EPI_PITCH + j]);
+              }
             }
           }
-          __syncwarp();
         }
+        __syncwarp();
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (lane == 0) mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // both CTAs done with TMEM and with each other's barriers
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 
@@ -439,9 +458,12 @@ static EncodeTiledFn get_encode_fn() {
 // A 3-D operand view [batch][outer][inner] with element strides ld (outer)
 // and bs (batch). `box_outer` rows are loaded per TMA request, 128 bytes of
 // the inner dimension each.
-static int encode_operand(CUtensorMap* map, const void* base, int es, long long inner,
+static int op_bytes(int op) { return op == MUON_TF32 ? 4 : 2; }
+
+static int encode_operand(CUtensorMap* map, const void* base, int op, long long inner,
                           long long outer, long long batch, long long ld, long long bs,
                           int box_outer, bool mn_major = false) {
+  const int es = op_bytes(op);
   EncodeTiledFn fn = get_encode_fn();
   if (!fn) return set_error(MUON_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
@@ -453,7 +475,10 @@ static int encode_operand(CUtensorMap* map, const void* base, int es, long long 
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld * es), static_cast<cuuint64_t>(bs * es)};
   cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / es), static_cast<cuuint32_t>(box_outer), 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, es == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+  const CUtensorMapDataType dt = op == MUON_TF32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : op == MUON_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, dt, 3,
                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   (mn_major && es == 4) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -475,36 +500,48 @@ struct muon_ns_plan {
   int n_classes;
   int num_sms;
   std::vector<muon::GemmParams> launches;  // 3 * steps
-  std::vector<int> last_class_of_problem;  // final-apply launch: problem -> class
 };
 
 namespace muon {
 
+// Power-of-two scale S_it of the stored Newton-Schulz operand X at iteration
+// `it` in fp16 mode, chosen so the entries have magnitude about 1: the input
+// X0 has unit Frobenius norm (entries ~ 1/sqrt(rows*cols)), later iterates
+// have singular values ~1 (entries ~ 1/sqrt(max(rows, cols))). Powers of two
+// keep every rescaling exact. Other modes store X unscaled (1.0).
+float ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dtype) {
+  if (op_dtype != MUON_F16 || rows <= 0 || cols <= 0) return 1.0f;
+  const double target = iteration == 0 ? std::sqrt(double(rows) * double(cols))
+                                        : std::sqrt(double(std::max(rows, cols)));
+  return std::ldexp(1.0f, static_cast<int>(std::lround(std::log2(target))));
+}
+
 static int tiles_per_matrix(int M, int N, bool symmetric, int* tm, int* tn) {
-  *tm = (M + BM - 1) / BM;
+  *tm = (M + PAIR_M - 1) / PAIR_M;
   *tn = (N + BN - 1) / BN;
   if (!symmetric) return (*tm) * (*tn);
   int total = 0;
-  for (int ti = 0; ti < *tm; ++ti) total += *tn - (ti >> 1);
+  for (int ti = 0; ti < *tm; ++ti) total += *tn - ti;  // square tiles: tj in [ti, tn)
   return total;
 }
 
 int64_t ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype) {
   if (rows <= 0 || cols <= 0 || count <= 0) return 0;
-  const int es = op_dtype == MUON_BF16 ? 2 : 4;
+  if (op_dtype != MUON_TF32 && op_dtype != MUON_BF16 && op_dtype != MUON_F16) return 0;
+  const int es = op_bytes(op_dtype);
   const int align_el = 16 / es;
   const int64_t m = std::min(rows, cols);
   const int64_t ld_x = (cols + align_el - 1) / align_el * align_el;
   const int64_t ld_m = (m + align_el - 1) / align_el * align_el;
   auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
-  return 2 * up(int64_t(count) * rows * ld_x * es) + 2 * up(int64_t(count) * m * ld_m * es);
+  return 2 * up(int64_t(count) * rows * ld_x * es) + 3 * up(int64_t(count) * m * ld_m * es);
 }
 
 int ns_class_layout(muon_ns_class* cls, void* base, int op_dtype) {
   if (!cls || !base) return set_error(MUON_ERR_ARG, "null class or workspace");
   if ((reinterpret_cast<uintptr_t>(base) & 255u) != 0)
     return set_error(MUON_ERR_ARG, "NS workspace must be 256-byte aligned");
-  const int es = op_dtype == MUON_BF16 ? 2 : 4;
+  const int es = op_bytes(op_dtype);
   const int align_el = 16 / es;
   const int64_t rows = cls->rows, cols = cls->cols, count = cls->count;
   const int64_t m = std::min(rows, cols);
@@ -517,7 +554,8 @@ int ns_class_layout(muon_ns_class* cls, void* base, int op_dtype) {
   cls->x0 = p;
   cls->x1 = p + xb;
   cls->ap = p + 2 * xb;
-  cls->mm = p + 2 * xb + mb;
+  cls->bp = p + 2 * xb + mb;
+  cls->mm = p + 2 * xb + 2 * mb;
   return MUON_OK;
 }
 
@@ -525,25 +563,23 @@ int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, in
                    muon_ns_plan** plan_out) {
   if (!plan_out) return set_error(MUON_ERR_ARG, "plan_out is null");
   *plan_out = nullptr;
-  if (op_dtype != MUON_TF32 && op_dtype != MUON_BF16)
-    return set_error(MUON_ERR_ARG, "op_dtype must be MUON_TF32 or MUON_BF16");
+  if (op_dtype != MUON_TF32 && op_dtype != MUON_BF16 && op_dtype != MUON_F16)
+    return set_error(MUON_ERR_ARG, "op_dtype must be MUON_TF32, MUON_BF16 or MUON_F16");
   if (steps < 1) return set_error(MUON_ERR_UNSUPPORTED, "Newton-Schulz plans need steps >= 1");
   if (n_classes < 1 || n_classes > kMaxProblems)
     return set_error(MUON_ERR_ARG, "n_classes must be in [1, 16]");
-  const int es = op_dtype == MUON_BF16 ? 2 : 4;
+  const int es = op_bytes(op_dtype);
   for (int c = 0; c < n_classes; ++c) {
     const muon_ns_class& k = classes[c];
     if (k.rows <= 0 || k.cols <= 0 || k.count <= 0)
       return set_error(MUON_ERR_ARG, "class with an empty shape or count");
-    if (!k.x0 || !k.x1 || !k.ap || !k.mm || !k.scales)
+    if (!k.x0 || !k.x1 || !k.ap || !k.bp || !k.mm || !k.scales || !k.u_out)
       return set_error(MUON_ERR_ARG, "class buffer pointer is null");
-    if ((k.u_out == nullptr) == (k.params == nullptr))
-      return set_error(MUON_ERR_ARG, "exactly one of u_out / params must be set per class");
-    if (k.params && k.param_dtype != MUON_BF16 && k.param_dtype != MUON_F32)
-      return set_error(MUON_ERR_ARG, "param_dtype must be MUON_BF16 or MUON_F32");
+    if (k.u_dtype != MUON_BF16 && k.u_dtype != MUON_F32)
+      return set_error(MUON_ERR_ARG, "u_dtype must be MUON_BF16 or MUON_F32");
     const int m = std::min(k.rows, k.cols);
     if (k.ld_x < k.cols || k.ld_m < m) return set_error(MUON_ERR_ARG, "leading dimension too small");
-    if (k.u_out && k.ld_u < k.cols) return set_error(MUON_ERR_ARG, "ld_u too small");
+    if (k.ld_u < k.cols) return set_error(MUON_ERR_ARG, "ld_u too small");
   }
   int dev = 0, sms = 0;
   if (check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return MUON_ERR_CUDA;
@@ -557,6 +593,7 @@ int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, in
   plan->num_sms = sms;
   plan->launches.resize(3 * steps);
 
+  const bool f16 = op_dtype == MUON_F16;
   const float alpha = float(kNsA + kNsB + kNsC);
   const float beta = float(kNsB + 2.0 * kNsC);
   const float gamma = float(kNsC);
@@ -585,7 +622,6 @@ int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, in
         if (kdim(x) != kdim(y)) return kdim(x) > kdim(y);
         return work(x) > work(y);
       });
-      if (phase == 2 && it == steps - 1) plan->last_class_of_problem = order;
       int tile_begin = 0;
       for (int pi = 0; pi < n_classes; ++pi) {
         const int c = order[pi];
@@ -607,68 +643,73 @@ int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, in
           pr.K = n;
           pr.symmetric = 1;
           pr.epi = EPI_GRAM;
-          pr.first = it == 0;
+          // fp16: X is stored pre-normalised and scaled by S_it, so A = acc / S_it^2.
+          pr.first = f16 ? 0 : it == 0;
+          {
+            const float S = ns_operand_scale(k.rows, k.cols, it, op_dtype);
+            pr.mul = 1.0f / (S * S);
+          }
           pr.a_mn = pr.b_mn = wide ? 0 : 1;
           pr.out = k.ap;
+          pr.out2 = k.bp;
           pr.out_ld = k.ld_m;
           pr.out_bs = mbs;
           if (wide) {
-            rc = encode_operand(&L.map_a[pi], xin, es, k.cols, k.rows, k.count, k.ld_x, xbs, BM);
-            if (!rc) rc = encode_operand(&L.map_b[pi], xin, es, k.cols, k.rows, k.count, k.ld_x, xbs, BN);
+            rc = encode_operand(&L.map_a[pi], xin, op_dtype, k.cols, k.rows, k.count, k.ld_x, xbs, BM);
+            if (!rc) rc = encode_operand(&L.map_b[pi], xin, op_dtype, k.cols, k.rows, k.count, k.ld_x, xbs, BN_CTA);
           } else {
-            rc = encode_operand(&L.map_a[pi], xin, es, k.cols, k.rows, k.count, k.ld_x, xbs, 128 / es, true);
-            if (!rc) rc = encode_operand(&L.map_b[pi], xin, es, k.cols, k.rows, k.count, k.ld_x, xbs, 128 / es, true);
+            rc = encode_operand(&L.map_a[pi], xin, op_dtype, k.cols, k.rows, k.count, k.ld_x, xbs, 128 / es, true);
+            if (!rc) rc = encode_operand(&L.map_b[pi], xin, op_dtype, k.cols, k.rows, k.count, k.ld_x, xbs, 128 / es, true);
           }
         } else if (phase == 1) {
-          // M = alpha I + beta A' + gamma A'A' (A' symmetric: both operands K-major).
+          // M = alpha I + A' B' (A', B' symmetric: both operands K-major).
           pr.M = pr.N = pr.K = m;
           pr.symmetric = 1;
           pr.epi = EPI_POLY;
           pr.first = 0;
+          pr.mul = 1.0f;
           pr.a_mn = pr.b_mn = 0;
           pr.out = k.mm;
           pr.out_ld = k.ld_m;
           pr.out_bs = mbs;
-          pr.side = k.ap;
-          pr.side_ld = k.ld_m;
-          pr.side_bs = mbs;
-          rc = encode_operand(&L.map_a[pi], k.ap, es, m, m, k.count, k.ld_m, mbs, BM);
-          if (!rc) rc = encode_operand(&L.map_b[pi], k.ap, es, m, m, k.count, k.ld_m, mbs, BN);
+          rc = encode_operand(&L.map_a[pi], k.ap, op_dtype, m, m, k.count, k.ld_m, mbs, BM);
+          if (!rc) rc = encode_operand(&L.map_b[pi], k.bp, op_dtype, m, m, k.count, k.ld_m, mbs, BN_CTA);
         } else {
           // Wide: X' = M X (B operand MN-major). Tall: X' = X M (both K-major).
           pr.M = k.rows;
           pr.N = k.cols;
           pr.K = m;
           pr.symmetric = 0;
-          pr.first = it == 0;
+          pr.first = f16 ? 0 : it == 0;
           const bool last = it == steps - 1;
+          {
+            // acc = M (S_it X): rescale to S_{it+1} X' for the next iteration,
+            // or to X' itself for the output.
+            const float S = ns_operand_scale(k.rows, k.cols, it, op_dtype);
+            const float Sn = last ? 1.0f : ns_operand_scale(k.rows, k.cols, it + 1, op_dtype);
+            pr.mul = Sn / S;
+          }
           if (wide) {
             pr.a_mn = 0;
             pr.b_mn = 1;
-            rc = encode_operand(&L.map_a[pi], k.mm, es, m, m, k.count, k.ld_m, mbs, BM);
-            if (!rc) rc = encode_operand(&L.map_b[pi], xin, es, k.cols, k.rows, k.count, k.ld_x, xbs, 128 / es, true);
+            rc = encode_operand(&L.map_a[pi], k.mm, op_dtype, m, m, k.count, k.ld_m, mbs, BM);
+            if (!rc) rc = encode_operand(&L.map_b[pi], xin, op_dtype, k.cols, k.rows, k.count, k.ld_x, xbs, 128 / es, true);
           } else {
             pr.a_mn = 0;
             pr.b_mn = 0;
-            rc = encode_operand(&L.map_a[pi], xin, es, k.cols, k.rows, k.count, k.ld_x, xbs, BM);
-            if (!rc) rc = encode_operand(&L.map_b[pi], k.mm, es, m, m, k.count, k.ld_m, mbs, BN);
+            rc = encode_operand(&L.map_a[pi], xin, op_dtype, k.cols, k.rows, k.count, k.ld_x, xbs, BM);
+            if (!rc) rc = encode_operand(&L.map_b[pi], k.mm, op_dtype, m, m, k.count, k.ld_m, mbs, BN_CTA);
           }
           if (!last) {
             pr.epi = EPI_APPLY;
             pr.out = xout;
             pr.out_ld = k.ld_x;
             pr.out_bs = xbs;
-          } else if (k.u_out) {
-            pr.epi = EPI_APPLY_F32;
+          } else {
+            pr.epi = k.u_dtype == MUON_BF16 ? EPI_U_BF16 : EPI_U_F32;
             pr.out = k.u_out;
             pr.out_ld = k.ld_u;
             pr.out_bs = static_cast<long long>(k.rows) * k.ld_u;
-          } else {
-            pr.epi = EPI_UPDATE;
-            pr.params = k.params;
-            pr.param_dtype = k.param_dtype;
-            pr.eff = 0.f;
-            pr.wd_factor = 1.f;
           }
         }
         if (rc != MUON_OK) {
@@ -687,39 +728,50 @@ int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, in
   return MUON_OK;
 }
 
-int ns_plan_run(const muon_ns_plan* plan, const float* eff, float wd_factor, int* err_dev,
-                cudaStream_t stream) {
+int ns_plan_run(const muon_ns_plan* plan, int* err_dev, cudaStream_t stream) {
   if (!plan) return set_error(MUON_ERR_ARG, "plan is null");
   if (!err_dev) return set_error(MUON_ERR_ARG, "err_dev is null");
-  static bool attr_set[2] = {false, false};
-  const bool tf32 = plan->op_dtype == MUON_TF32;
-  const void* fn = tf32 ? reinterpret_cast<const void*>(&ns_gemm_kernel<true>)
-                        : reinterpret_cast<const void*>(&ns_gemm_kernel<false>);
-  if (!attr_set[tf32]) {
+  static bool attr_set[4] = {false, false, false, false};
+  const int op = plan->op_dtype;
+  const void* fn = op == MUON_TF32   ? reinterpret_cast<const void*>(&ns_gemm_kernel<kOpTf32>)
+                   : op == MUON_BF16 ? reinterpret_cast<const void*>(&ns_gemm_kernel<kOpBf16>)
+                                     : reinterpret_cast<const void*>(&ns_gemm_kernel<kOpF16>);
+  static int max_clusters[4] = {0, 0, 0, 0};
+  if (!attr_set[op]) {
     if (check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
                    "cudaFuncSetAttribute(ns_gemm)"))
       return MUON_ERR_CUDA;
-    attr_set[tf32] = true;
+    // Persistent schedule: launch only as many CTA pairs as can be resident
+    // at once (a GPC with an odd number of free SMs leaves one unused).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (plan->num_sms / 2));
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (check_cuda(cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg), "cudaOccupancyMaxActiveClusters"))
+      return MUON_ERR_CUDA;
+    max_clusters[op] = std::max(1, std::min(clusters, plan->num_sms / 2));
+    attr_set[op] = true;
   }
   const int n = static_cast<int>(plan->launches.size());
   for (int i = 0; i < n; ++i) {
     GemmParams L = plan->launches[i];
     L.err = err_dev;
-    if (i == n - 1) {
-      for (int pi = 0; pi < L.n_problems; ++pi) {
-        if (L.prob[pi].epi == EPI_UPDATE) {
-          if (!eff) return set_error(MUON_ERR_ARG, "eff is required for in-place parameter updates");
-          L.prob[pi].eff = eff[plan->last_class_of_problem[pi]];
-          L.prob[pi].wd_factor = wd_factor;
-        }
-      }
-    }
     if (L.total_tiles == 0) continue;
-    const int grid = std::min(L.total_tiles, plan->num_sms);
-    if (tf32)
-      ns_gemm_kernel<true><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(L);
+    const int grid = 2 * std::min(L.total_tiles, max_clusters[op]);  // CTA pairs
+    if (op == MUON_TF32)
+      ns_gemm_kernel<kOpTf32><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(L);
+    else if (op == MUON_BF16)
+      ns_gemm_kernel<kOpBf16><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(L);
     else
-      ns_gemm_kernel<false><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(L);
+      ns_gemm_kernel<kOpF16><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(L);
     if (check_cuda(cudaGetLastError(), "ns_gemm launch")) return MUON_ERR_CUDA;
   }
   return MUON_OK;

@@ -28,7 +28,8 @@ import torch
 from . import _native as N
 
 _DTYPE_CODE = {torch.bfloat16: N.MUON_BF16, torch.float32: N.MUON_F32}
-PRECISIONS = {"tf32": N.MUON_TF32, "bf16": N.MUON_BF16}
+PRECISIONS = {"tf32": N.MUON_TF32, "fp16": N.MUON_F16, "bf16": N.MUON_BF16}
+_OP_TORCH = {N.MUON_TF32: torch.float32, N.MUON_F16: torch.float16, N.MUON_BF16: torch.bfloat16}
 
 
 @dataclass
@@ -79,8 +80,18 @@ class _ClassState:
         self.cls.rows, self.cls.cols, self.cls.count = rows, cols, count
         N.check(lib.muon_ns_class_layout(byref(self.cls), c_void_p(self.workspace.data_ptr()), op_dtype),
                 "muon_ns_class_layout")
-        self.es = 2 if op_dtype == N.MUON_BF16 else 4
+        self.op_dtype = op_dtype
+        self.es = 4 if op_dtype == N.MUON_TF32 else 2
         self.x_stride = rows * int(self.cls.ld_x) * self.es  # bytes per matrix in x0
+        # fp16 stores X0 normalised and scaled by this power of two.
+        self.x0_scale = float(lib.muon_ns_operand_scale(rows, cols, 0, op_dtype))
+
+    def x0_view(self, slot: int) -> torch.Tensor:
+        """The stored Newton-Schulz input of matrix `slot` as a [rows, cols] tensor."""
+        ld = int(self.cls.ld_x)
+        off = (int(self.cls.x0) - self.workspace.data_ptr()) // self.es + slot * self.rows * ld
+        return torch.empty(0, dtype=_OP_TORCH[self.op_dtype], device=self.workspace.device).set_(
+            self.workspace.untyped_storage(), off, (self.rows, self.cols), (ld, 1))
 
 
 class CudaMuonEngine:
@@ -106,6 +117,21 @@ class CudaMuonEngine:
         self._err_host = torch.zeros(1, dtype=torch.int32).pin_memory()
         self._err_event = None
         self.kernel_launches = 0  # launches issued by this engine (for benchmarks)
+        # When a list, (name, start, end) CUDA events are appended around the
+        # momentum, Newton-Schulz and AdamW launches (benchmark instrumentation).
+        self.profile_events: list | None = None
+
+    def _event_pair(self, name: str):
+        if self.profile_events is None:
+            return None
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        return name, start, end
+
+    def _event_end(self, pair) -> None:
+        if pair is not None:
+            pair[2].record()
+            self.profile_events.append(pair)
 
     # ------------------------------------------------------------- errors
     def _record_error_check(self) -> None:
@@ -145,19 +171,16 @@ class CudaMuonEngine:
         self._classes = []
         self._order = [(0, 0)] * len(items)
         self._seg_order: list[int] = []
-        ptr_tables = []
         for ci, ((r, c, dt), idxs) in enumerate(groups.items()):
             cs = _ClassState(r, c, dt, len(idxs), self.op_dtype, self.device)
             for slot, i in enumerate(idxs):
                 self._order[i] = (ci, slot)
                 self._seg_order.append(i)
-            ptrs = torch.tensor([items[i].param.data_ptr() for i in idxs], dtype=torch.int64)
-            cs.param_ptrs = ptrs.to(self.device)
-            ptr_tables.append(cs.param_ptrs)
-            cs.cls.param_dtype = _dtype_code(items[idxs[0]].param)
-            cs.cls.params = c_void_p(cs.param_ptrs.data_ptr())
-            cs.cls.u_out = None
-            cs.cls.ld_u = 0
+            # U, rounded to the parameter dtype, for muon_apply_update.
+            cs.u_buf = torch.empty((len(idxs), r, c), dtype=dt, device=self.device)
+            cs.cls.u_dtype = _dtype_code(items[idxs[0]].param)
+            cs.cls.u_out = c_void_p(cs.u_buf.data_ptr())
+            cs.cls.ld_u = c
             self._classes.append(cs)
         self._scales = torch.zeros(max(len(items), 1), dtype=torch.float32, device=self.device)
         first = 0
@@ -165,6 +188,30 @@ class CudaMuonEngine:
             cs.first_seg = first
             cs.cls.scales = c_void_p(self._scales.data_ptr() + 4 * first)
             first += cs.count
+        self._staging = None
+        self._staging_off: dict[int, int] = {}
+        self._convert_table = None
+        if self.op_dtype == N.MUON_F16:
+            # fp32 directions, normalised into fp16 x0 by muon_convert_f16.
+            total = sum(cs.rows * cs.cols * cs.count for cs in self._classes)
+            self._staging = torch.empty(max(total, 1), dtype=torch.float32, device=self.device)
+            segs, off, chunks = [], 0, 0
+            for i in self._seg_order:
+                ci, slot = self._order[i]
+                cs = self._classes[ci]
+                self._staging_off[i] = off
+                cv = N.ConvertSeg()
+                cv.src = self._staging.data_ptr() + 4 * off
+                cv.dst = cs.cls.x0 + slot * cs.x_stride
+                cv.rows, cv.cols, cv.ld_src, cv.ld_dst = cs.rows, cs.cols, cs.cols, int(cs.cls.ld_x)
+                cv.chunk_begin = chunks
+                cv.mul = cs.x0_scale
+                cv.scale_index = cs.first_seg + slot
+                segs.append(cv)
+                off += cs.rows * cs.cols
+                chunks += int(self.lib.muon_momentum_chunks(cs.rows, cs.cols))
+            self._convert_table = _upload(N.struct_bytes(segs), self.device)
+            self._convert_n, self._convert_chunks = len(segs), chunks
         if ns_steps >= 1:
             arr = (N.NsClass * len(self._classes))(*[cs.cls for cs in self._classes])
             plan = c_void_p()
@@ -175,7 +222,7 @@ class CudaMuonEngine:
 
     # --------------------------------------------------------------- launches
     def _momentum(self, segs: list, grad_dtype: int, momentum: float, nesterov: bool, scales_ptr: int,
-                  eps: float = 1e-7) -> None:
+                  eps: float = 1e-7, dir_dtype: int | None = None) -> None:
         if not segs:
             return
         total = 0
@@ -184,7 +231,9 @@ class CudaMuonEngine:
             total += int(self.lib.muon_momentum_chunks(s.rows, s.cols))
         table = _upload(N.struct_bytes(segs), self.device)
         partials = torch.empty(max(total, 1), dtype=torch.float32, device=self.device)
-        N.check(self.lib.muon_momentum(c_void_p(table.data_ptr()), len(segs), total, grad_dtype, self.op_dtype,
+        if dir_dtype is None:
+            dir_dtype = N.MUON_F32 if self.op_dtype == N.MUON_F16 else self.op_dtype
+        N.check(self.lib.muon_momentum(c_void_p(table.data_ptr()), len(segs), total, grad_dtype, dir_dtype,
                                        c_float(momentum), int(bool(nesterov)), c_float(eps),
                                        c_void_p(partials.data_ptr()), c_void_p(scales_ptr), _stream_handle()),
                 "muon_momentum")
@@ -216,10 +265,15 @@ class CudaMuonEngine:
                 g = g.contiguous()
             seg.grad = g.data_ptr() if g is not None else None
             seg.exp_avg = it.exp_avg.data_ptr()
-            seg.direction = cs.cls.x0 + slot * cs.x_stride
-            seg.rows, seg.cols, seg.ld = cs.rows, cs.cols, int(cs.cls.ld_x)
+            if self._staging is not None:
+                seg.direction = self._staging.data_ptr() + 4 * self._staging_off[i]
+                seg.rows, seg.cols, seg.ld = cs.rows, cs.cols, cs.cols
+            else:
+                seg.direction = cs.cls.x0 + slot * cs.x_stride
+                seg.rows, seg.cols, seg.ld = cs.rows, cs.cols, int(cs.cls.ld_x)
             code = _dtype_code(g) if g is not None else next(iter(gdt))
             by_dtype.setdefault(code, []).append((cs.first_seg + slot, seg))
+        ev = self._event_pair("momentum")
         for code, lst in by_dtype.items():
             # Each launch writes scales for a contiguous run; split into runs.
             lst.sort(key=lambda x: x[0])
@@ -234,28 +288,59 @@ class CudaMuonEngine:
                 run.append(seg)
             if run:
                 self._momentum(run, code, momentum, nesterov, self._scales.data_ptr() + 4 * start)
+        if self._convert_table is not None:
+            N.check(self.lib.muon_convert_f16(c_void_p(self._convert_table.data_ptr()), self._convert_n,
+                                              self._convert_chunks, c_void_p(self._scales.data_ptr()),
+                                              _stream_handle()), "muon_convert_f16")
+            self.kernel_launches += 1
+        self._event_end(ev)
         if ns_steps >= 1:
-            eff = (c_float * len(self._classes))(*[items[self._seg_order[cs.first_seg]].eff for cs in self._classes])
-            N.check(self.lib.muon_ns_plan_run(self._plan, eff, c_float(weight_decay_factor),
-                                              c_void_p(self._err.data_ptr()), _stream_handle()),
+            ev = self._event_pair("ns")
+            N.check(self.lib.muon_ns_plan_run(self._plan, c_void_p(self._err.data_ptr()), _stream_handle()),
                     "muon_ns_plan_run")
+            self._event_end(ev)
             self.kernel_launches += 3 * ns_steps
             self._record_error_check()
+            self._apply_updates(items, weight_decay_factor)
         else:
             self._zero_step_update(items, weight_decay_factor)
+
+    def _apply_updates(self, items: list[MatrixItem], wd_factor: float) -> None:
+        """Weight decay + p -= eff * U for every matrix (muon_apply_update)."""
+        segs, total = [], 0
+        for i in self._seg_order:
+            it = items[i]
+            ci, slot = self._order[i]
+            cs = self._classes[ci]
+            sg = N.UpdateSeg()
+            sg.param = it.param.data_ptr()
+            sg.update = cs.u_buf[slot].data_ptr()
+            sg.numel = cs.rows * cs.cols
+            sg.chunk_begin = total
+            sg.eff = it.eff
+            sg.param_dtype = cs.cls.u_dtype
+            segs.append(sg)
+            total += int(self.lib.muon_momentum_chunks(1, sg.numel))
+        table = _upload(N.struct_bytes(segs), self.device)
+        ev = self._event_pair("update")
+        N.check(self.lib.muon_apply_update(c_void_p(table.data_ptr()), len(segs), total, c_float(wd_factor),
+                                           _stream_handle()), "muon_apply_update")
+        self._event_end(ev)
+        self.kernel_launches += 1
+
+    def _normalized_input(self, cs: _ClassState, slot: int) -> torch.Tensor:
+        """The unit-norm Newton-Schulz input of one matrix, fp32 (ns_steps == 0 result)."""
+        x = cs.x0_view(slot).float()
+        if self.op_dtype == N.MUON_F16:
+            return x / cs.x0_scale
+        return x * self._scales[cs.first_seg + slot]
 
     def _zero_step_update(self, items: list[MatrixItem], wd_factor: float) -> None:
         # ns_steps == 0: the reference's update is the normalised direction itself.
         for i in self._seg_order:
             it = items[i]
             ci, slot = self._order[i]
-            cs = self._classes[ci]
-            dtype = torch.bfloat16 if self.op_dtype == N.MUON_BF16 else torch.float32
-            ld = int(cs.cls.ld_x)
-            x = torch.empty(0, dtype=dtype, device=self.device).set_(
-                cs.workspace.untyped_storage(), (cs.cls.x0 - cs.workspace.data_ptr()) // cs.es + slot * cs.rows * ld,
-                (cs.rows, cs.cols), (ld, 1))
-            u = x.float() * self._scales[cs.first_seg + slot]
+            u = self._normalized_input(self._classes[ci], slot)
             if wd_factor != 1.0:
                 it.param.mul_(wd_factor)
             it.param.add_(u.to(it.param.dtype), alpha=-it.eff)
@@ -293,13 +378,8 @@ class CudaMuonEngine:
         seg.direction = out.data_ptr()
         seg.rows, seg.cols, seg.ld = 1, n, n
         scratch = torch.empty(1, dtype=torch.float32, device=self.device)
-        saved = self.op_dtype
-        self.op_dtype = N.MUON_TF32  # fp32 storage; values rounded to tf32 like the NS input
-        try:
-            self._momentum([seg], _dtype_code(g) if g is not None else N.MUON_F32, momentum, nesterov,
-                           scratch.data_ptr())
-        finally:
-            self.op_dtype = saved
+        self._momentum([seg], _dtype_code(g) if g is not None else N.MUON_F32, momentum, nesterov,
+                       scratch.data_ptr(), dir_dtype=N.MUON_F32)
         return out
 
     def orthogonalize(self, matrix: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch.Tensor:
@@ -320,27 +400,38 @@ class CudaMuonEngine:
         seg = N.MomentumSeg()
         seg.grad = src.data_ptr()
         seg.exp_avg = exp_avg.data_ptr()
-        seg.direction = cs.cls.x0
-        seg.rows, seg.cols, seg.ld = rows, cols, int(cs.cls.ld_x)
-        # momentum 0, no Nesterov: exp_avg = g and d = g, i.e. a rounded copy plus the norm.
+        seg.rows, seg.cols = rows, cols
+        f16 = self.op_dtype == N.MUON_F16
+        staging = torch.empty((rows, cols), dtype=torch.float32, device=self.device) if f16 else None
+        if f16:
+            seg.direction, seg.ld = staging.data_ptr(), cols
+        else:
+            seg.direction, seg.ld = cs.cls.x0, int(cs.cls.ld_x)
+        # momentum 0, no Nesterov: exp_avg = g and d = g, i.e. a copy plus the norm.
         self._momentum([seg], _dtype_code(src), 0.0, False, scales.data_ptr(), eps=eps)
+        if f16:
+            cv = N.ConvertSeg()
+            cv.src, cv.dst = staging.data_ptr(), cs.cls.x0
+            cv.rows, cv.cols, cv.ld_src, cv.ld_dst = rows, cols, cols, int(cs.cls.ld_x)
+            cv.chunk_begin, cv.mul, cv.scale_index = 0, cs.x0_scale, 0
+            table = _upload(N.struct_bytes([cv]), self.device)
+            N.check(self.lib.muon_convert_f16(c_void_p(table.data_ptr()), 1,
+                                              int(self.lib.muon_momentum_chunks(rows, cols)),
+                                              c_void_p(scales.data_ptr()), _stream_handle()), "muon_convert_f16")
         if steps < 1:
-            dtype = torch.bfloat16 if self.op_dtype == N.MUON_BF16 else torch.float32
-            ld = int(cs.cls.ld_x)
-            x = torch.empty(0, dtype=dtype, device=self.device).set_(
-                cs.workspace.untyped_storage(), 0, (rows, cols), (ld, 1))
-            return x.float() * scales[0]
+            if f16:
+                return staging * scales[0]
+            return cs.x0_view(0).float() * scales[0]
         cs.cls.scales = c_void_p(scales.data_ptr())
         cs.cls.u_out = c_void_p(out.data_ptr())
         cs.cls.ld_u = cols
-        cs.cls.params = None
-        cs.cls.param_dtype = N.MUON_F32
+        cs.cls.u_dtype = N.MUON_F32
         plan = c_void_p()
         N.check(self.lib.muon_ns_plan_create(byref(cs.cls), 1, self.op_dtype, int(steps), byref(plan)),
                 "muon_ns_plan_create")
         try:
-            N.check(self.lib.muon_ns_plan_run(plan, None, c_float(1.0), c_void_p(self._err.data_ptr()),
-                                              _stream_handle()), "muon_ns_plan_run")
+            N.check(self.lib.muon_ns_plan_run(plan, c_void_p(self._err.data_ptr()), _stream_handle()),
+                    "muon_ns_plan_run")
         finally:
             self.lib.muon_ns_plan_destroy(plan)
         self.kernel_launches += 3 * int(steps)
@@ -378,8 +469,10 @@ class CudaMuonEngine:
             segs.append(s)
         table = _upload(N.struct_bytes(segs), self.device)
         wd_factor = 1.0 - lr * weight_decay if weight_decay != 0 else 1.0
+        ev = self._event_pair("adamw")
         N.check(self.lib.muon_adamw(c_void_p(table.data_ptr()), len(segs), total, float(beta1), float(beta2),
                                     c_float(eps), c_float(wd_factor), _stream_handle()), "muon_adamw")
+        self._event_end(ev)
         self.kernel_launches += 1
 
     def close(self) -> None:

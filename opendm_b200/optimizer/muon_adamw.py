@@ -14,8 +14,11 @@ The arithmetic runs in the sm_100a kernels of ``libopendm_muon.so`` through
 ``opendm_b200.engine``; there is no CPU path. Optional keyword arguments
 (defaults reproduce the reference):
 
-* ``precision``: "tf32" (default; Newton-Schulz operands rounded to tf32,
-  fp32 accumulation) or "bf16" (faster, ~1e-2 relative update error).
+* ``precision``: Newton-Schulz operand type, fp32 accumulation throughout.
+  "tf32" (default): operands rounded to tf32. "fp16": operands in fp16
+  (the same 11-bit significand as tf32, twice the tensor-core rate), each
+  stored matrix scaled by a power of two to stay in fp16's range; accuracy
+  equal to "tf32". "bf16": fastest storage, ~1e-2 relative update error.
 * ``scale_mode``: "reference" (lr * lr_scale * coefficient * sqrt(max(r, c)))
   or "shape" (lr * lr_scale * max(1, r / c) ** 0.5).
 * ``sharding``: "auto" (default: with world size > 1 and replicated
@@ -180,8 +183,8 @@ class MuonAdamW(torch.optim.Optimizer):
             raise RuntimeError("MuonAdamW metadata is missing; mark parameters before FSDP wrapping.")
         if sharding not in ("auto", "off"):
             raise ValueError(f"sharding must be 'auto' or 'off', got {sharding!r}")
-        if precision not in ("tf32", "bf16"):
-            raise ValueError(f"precision must be 'tf32' or 'bf16', got {precision!r}")
+        if precision not in ("tf32", "fp16", "bf16"):
+            raise ValueError(f"precision must be 'tf32', 'fp16' or 'bf16', got {precision!r}")
         effective_lr(1.0, 1.0, 1.0, (1, 1), scale_mode)  # validates scale_mode
         groups = [
             {"params": adamw_params, "use_muon": False},

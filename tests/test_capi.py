@@ -1,0 +1,73 @@
+"""The C-ABI library loads and exports every function declared in
+include/opendm_muon.h (no compute calls: these run without a GPU)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from opendm_b200 import _native as N
+from opendm_b200.build import build
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    text = open(os.path.join(ROOT, "include", "opendm_muon.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(muon_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build()
+    return N.lib()
+
+
+def test_every_declared_symbol_is_exported_and_bound(lib):
+    names = _declared()
+    assert len(names) >= 12
+    raw = ctypes.CDLL(str(N.LIB_PATH))
+    for name in names:
+        assert hasattr(raw, name), name
+        assert name in N.SIGNATURES, name
+    assert set(N.SIGNATURES) == set(names)
+
+
+def test_host_only_entry_points(lib):
+    assert lib.muon_version() == N.ABI_VERSION
+    assert lib.muon_momentum_chunks(2048, 8192) == (2048 * 8192 + 16383) // 16384
+    assert lib.muon_momentum_chunks(0, 5) == 0
+    assert lib.muon_adamw_chunks(8193) == 2
+    # two x buffers (ld padded to 16 bytes) + three m x m buffers, 256-byte aligned parts
+    assert lib.muon_ns_class_workspace_bytes(3, 5, 2, N.MUON_TF32) == 2 * 256 + 3 * 256
+    assert lib.muon_ns_class_workspace_bytes(256, 2048, 1, N.MUON_BF16) == 2 * 256 * 2048 * 2 + 3 * 256 * 256 * 2
+    assert lib.muon_ns_class_workspace_bytes(256, 2048, 1, N.MUON_F16) == 2 * 256 * 2048 * 2 + 3 * 256 * 256 * 2
+    assert lib.muon_ns_class_workspace_bytes(4, 4, 1, N.MUON_F32) == 0  # not an operand type
+    # fp16 operand scales: powers of two bringing entries to magnitude ~1
+    assert lib.muon_ns_operand_scale(2048, 8192, 0, N.MUON_F16) == 4096.0
+    assert lib.muon_ns_operand_scale(2048, 8192, 1, N.MUON_F16) == 128.0
+    assert lib.muon_ns_operand_scale(2048, 8192, 0, N.MUON_TF32) == 1.0
+
+
+def test_argument_validation_reports_errors(lib):
+    plan = ctypes.c_void_p()
+    cls = N.NsClass()
+    status = lib.muon_ns_plan_create(ctypes.byref(cls), 1, N.MUON_TF32, 5, ctypes.byref(plan))
+    assert status == N.MUON_ERR_ARG
+    assert "empty" in N.last_error()
+    assert lib.muon_ns_plan_create(ctypes.byref(cls), 1, N.MUON_F32, 5, ctypes.byref(plan)) == N.MUON_ERR_ARG
+    assert lib.muon_ns_plan_create(ctypes.byref(cls), 1, N.MUON_TF32, 0, ctypes.byref(plan)) == N.MUON_ERR_UNSUPPORTED
+    assert lib.muon_momentum(None, 2, 4, N.MUON_BF16, N.MUON_TF32, 0.9, 1, 1e-7, None, None, None) == N.MUON_ERR_ARG
+    assert lib.muon_apply_update(None, 2, 4, 1.0, None) == N.MUON_ERR_ARG
+    assert lib.muon_convert_f16(None, 2, 4, None, None) == N.MUON_ERR_ARG
+    with pytest.raises(RuntimeError, match="failed"):
+        N.check(N.MUON_ERR_ARG, "probe")
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(N, "_LIB", None)
+    monkeypatch.setenv("OPENDM_MUON_LIB", str(tmp_path / "absent.so"))
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        N.lib()

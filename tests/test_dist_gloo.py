@@ -1,0 +1,192 @@
+"""Multi-rank host logic over gloo (world size 2, CPU): the FLOP-balanced
+Newton-Schulz sharding with the parameter all-gather, owner-only momentum with
+consolidation, FSDP-style flat shards (the reference's owner_only / partial
+plans), and a rank that fails mid-step. Arithmetic: the CPU oracle through
+tests/oracle_engine.py; every rank must end with the single-process oracle's
+result."""
+
+import os
+import socket
+import traceback
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import muon_oracle as O
+
+WORLD = 2
+# 8 fp32 matrices + 4 fp32 vectors of length 512 on AdamW.
+C1_MUON = [(512, 512), (512, 2048), (2048, 512), (1024, 1024)] * 2
+C1_ADAM = [(512,)] * 4
+SMALL_MUON = [(64, 64), (64, 160), (160, 64), (96, 96), (48, 200), (33, 70)]
+SMALL_ADAM = [(64,), (10,)]
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _data(muon, adam, steps, seed=0):
+    rng = np.random.default_rng(seed)
+    params = [(rng.standard_normal(s) * 0.02).astype(np.float32) for s in muon + adam]
+    grads = [[(rng.standard_normal(s) * 1e-3).astype(np.float32) for s in muon + adam] for _ in range(steps)]
+    return params, grads
+
+
+def _oracle(muon, adam, steps):
+    params, grads = _data(muon, adam, steps)
+    opt = O.OracleMuonAdamW(lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01)
+    mp_ = {str(i): params[i].copy() for i in range(len(muon))}
+    ap_ = {str(i): params[i].copy() for i in range(len(muon), len(params))}
+    for s in range(steps):
+        g = grads[s]
+        opt.step(mp_, {str(i): g[i] for i in range(len(muon))}, ap_,
+                 {str(i): g[i] for i in range(len(muon), len(params))})
+    final = [mp_[str(i)] for i in range(len(muon))] + [ap_[str(i)] for i in range(len(muon), len(params))]
+    exp_avg = [opt.muon_state[str(i)].exp_avg for i in range(len(muon))]
+    return final, exp_avg
+
+
+def _worker(rank, port, scenario, muon, adam, steps, outdir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.set_num_threads(2)
+    from datetime import timedelta
+
+    from opendm_b200.optimizer import MuonAdamW
+    from tests.oracle_engine import OracleEngine
+
+    result = {"rank": rank}
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=WORLD, timeout=timedelta(seconds=20))
+        params, grads = _data(muon, adam, steps)
+        model = torch.nn.Module()
+        n_muon = len(muon)
+        if scenario in ("replicated", "state_sharding", "fail"):
+            for i, p in enumerate(params):
+                t = torch.nn.Parameter(torch.from_numpy(p.copy()))
+                if i < n_muon:
+                    t._opendm_muon_shape = tuple(p.shape)
+                    t._opendm_muon_name = f"m{i}"
+                model.register_parameter(f"p{i}", t)
+            slices = None
+        else:  # flat shards: concatenate the Muon matrices, split evenly over the ranks
+            sizes = [int(np.prod(s)) for s in muon]
+            total = sum(sizes)
+            per = (total + WORLD - 1) // WORLD
+            lo, hi = rank * per, min((rank + 1) * per, total)
+            slices = []
+            off = 0
+            for i, n in enumerate(sizes):
+                a, b = max(lo, off), min(hi, off + n)
+                a, b = (a - off, b - off) if b > a else (0, 0)
+                slices.append((a, b))
+                flat = params[i].reshape(-1)[a:b].copy()
+                t = torch.nn.Parameter(torch.from_numpy(flat))
+                t._opendm_muon_shape = tuple(muon[i])
+                t._opendm_muon_name = f"m{i}"
+                model.register_parameter(f"p{i}", t)
+                off += n
+            for i in range(n_muon, len(params)):
+                model.register_parameter(f"p{i}", torch.nn.Parameter(torch.from_numpy(params[i].copy())))
+        engine = OracleEngine()
+        opt = MuonAdamW(model, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, _engine=engine,
+                        state_sharding=(scenario == "state_sharding"))
+        plist = list(model.parameters())
+        for s in range(steps):
+            if scenario == "fail" and rank == 1 and s == 1:
+                raise SystemExit(3)  # this rank dies between steps
+            for i, p in enumerate(plist):
+                g = grads[s][i]
+                if slices is not None and i < n_muon:
+                    a, b = slices[i]
+                    g = g.reshape(-1)[a:b]
+                p.grad = torch.from_numpy(g.copy())
+            opt.step()
+        if scenario == "state_sharding":
+            opt.consolidate_state_dict()
+        result["params"] = [p.detach().numpy().copy() for p in plist]
+        result["exp_avg"] = [opt.state[p]["exp_avg"].numpy().copy() if "exp_avg" in opt.state[p]
+                             else np.zeros(0, np.float32) for p in plist[:n_muon]]
+        result["slices"] = slices
+        result["muon_calls"] = engine.matrices_seen
+        result["kinds"] = [pl.kind for pl in opt._get_muon_shard_plans(opt.param_groups[1])]
+        dist.barrier()
+        dist.destroy_process_group()
+    except SystemExit:
+        result["exited"] = True
+    except Exception as exc:  # reported to the parent
+        result["error"] = f"{type(exc).__name__}: {exc}"
+        result["trace"] = traceback.format_exc()
+    torch.save(result, os.path.join(outdir, f"rank{rank}.pt"))
+
+
+def _run(scenario, muon, adam, steps, tmp_path):
+    ctx = mp.get_context("spawn")
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, port, scenario, muon, adam, steps, str(tmp_path)))
+             for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("rank did not finish")
+    return [torch.load(os.path.join(tmp_path, f"rank{r}.pt"), weights_only=False) for r in range(WORLD)]
+
+
+def _check(res, muon, adam, steps, check_exp_avg=True):
+    final, exp_avg = _oracle(muon, adam, steps)
+    for r in res:
+        assert "error" not in r, r.get("trace")
+        for i, got in enumerate(r["params"]):
+            want = final[i]
+            if r["slices"] is not None and i < len(muon):
+                a, b = r["slices"][i]
+                want = want.reshape(-1)[a:b]
+            assert O.rel_frobenius(got, want) < 1e-5, (r["rank"], i, O.rel_frobenius(got, want))
+        if check_exp_avg:
+            for i, got in enumerate(r["exp_avg"]):
+                want = exp_avg[i]
+                if r["slices"] is not None:
+                    a, b = r["slices"][i]
+                    want = want.reshape(-1)[a:b]
+                assert O.rel_frobenius(got.reshape(-1), want.reshape(-1)) < 1e-6, (r["rank"], i)
+
+
+def test_c1_sharded_two_ranks(tmp_path):
+    """BASELINE config 1 on gloo world size 2: each matrix orthogonalised by one
+    owner, parameters all-gathered; both ranks equal the single-process oracle."""
+    res = _run("replicated", C1_MUON, C1_ADAM, 2, tmp_path)
+    _check(res, C1_MUON, C1_ADAM, 2)
+    assert all(k == "replicated" for k in res[0]["kinds"])
+    assert res[0]["muon_calls"] + res[1]["muon_calls"] == 2 * len(C1_MUON)  # no redundant NS
+    assert 0 < res[0]["muon_calls"] < 2 * len(C1_MUON)
+
+
+def test_owner_only_momentum_consolidates(tmp_path):
+    res = _run("state_sharding", SMALL_MUON, SMALL_ADAM, 3, tmp_path)
+    _check(res, SMALL_MUON, SMALL_ADAM, 3)
+
+
+def test_flat_shards_partial_and_owner_only(tmp_path):
+    res = _run("flat", SMALL_MUON, SMALL_ADAM, 2, tmp_path)
+    kinds = set(res[0]["kinds"]) | set(res[1]["kinds"])
+    assert "partial" in kinds and ("owner_only" in kinds or "empty" in kinds)
+    _check(res, SMALL_MUON, SMALL_ADAM, 2)
+
+
+def test_rank_failure_surfaces_as_error(tmp_path):
+    """A rank that exits between steps: the surviving rank's next collective
+    raises instead of hanging (host-side failure detection)."""
+    res = _run("fail", SMALL_MUON, SMALL_ADAM, 3, tmp_path)
+    assert res[1].get("exited")
+    assert "error" in res[0], "surviving rank should report a collective error"
