@@ -12,9 +12,11 @@ differs from the reference's by ~1e-3 relative (tf32-level Newton-Schulz)
 moves p - eff*U by a few hundredths of a bf16 ulp, so a few percent of the
 elements round to the neighbouring bf16 value, each flip being a whole ulp
 (~0.4%). For bf16 parameters the checks are therefore: the parameter change
-p_new - p_old*(1-lr*wd) within the 1e-2 update bar, the parameters within
-2e-3 relative, and fewer than 1% of the elements more than one bf16 ulp
-(at the parameter's scale) from the reference.
+p_new - p_old*(1-lr*wd) within the 1e-2 update bar at every step, the
+parameters within 2e-3 relative after one step (growing as sqrt(steps) over
+several steps, as the flips accumulate), and, after one step, fewer than 1%
+of the elements more than one bf16 ulp (at the parameter's scale) from the
+reference.
 """
 
 import copy
@@ -34,9 +36,11 @@ UPDATE_TOL = 5e-3
 BF16_PARAM_TOL = 2e-3
 
 
-def _check_params(got, want, before_got, before_want, wd_factor, dtype, what, max_beyond=None):
+def _check_params(got, want, before_got, before_want, wd_factor, dtype, what, max_beyond=None, step=0):
     """Parity of updated parameters (see the module docstring for bf16).
-    ``before_*`` are each side's parameters before this step."""
+    ``before_*`` are each side's parameters before this step; ``step`` is the
+    0-based step index (bf16 rounding flips accumulate like a random walk, so
+    the bf16 bound grows as sqrt(step + 1))."""
     err = O.rel_frobenius(got, want)
     if dtype != torch.bfloat16:
         assert err < PARAM_TOL, (what, err)
@@ -54,7 +58,7 @@ def _check_params(got, want, before_got, before_want, wd_factor, dtype, what, ma
 
     if np.any(want != base(before_want)):
         assert O.rel_frobenius(got - base(before_got), want - base(before_want)) < 1e-2, (what, "update")
-    assert err < BF16_PARAM_TOL, (what, err)
+    assert err < BF16_PARAM_TOL * np.sqrt(step + 1), (what, err)
 
 
 def _dev():
@@ -98,7 +102,7 @@ def test_dropin_matches_reference_golden(golden_dir, name, dtype):
             # systematic difference of up to 0.4% in eff for bf16 parameters.
             _check_params(p.detach().float().cpu().numpy(), z[f"param{s}/{k}"], before[k], want_before,
                           factor, dtype if k in muon_keys else torch.float32, (s, k),
-                          max_beyond=3e-2 if s == 0 else None)
+                          max_beyond=3e-2 if s == 0 else None, step=s)
     for k, p in model.named_parameters():
         st = opt.state[p]
         got = st["exp_avg"].cpu().numpy()
@@ -149,7 +153,7 @@ def _run_config(shapes_muon, shapes_adam, dtype, steps, seed=0):
         if i < n:
             # element-level flips compound over steps; checked for one-step runs only
             _check_params(got, want, before_got[i], before_want[i], 1.0 - 0.02 * 0.01, dtype, i,
-                          max_beyond=1e-2 if steps == 1 else None)
+                          max_beyond=1e-2 if steps == 1 else None, step=steps - 1)
         else:
             assert O.rel_frobenius(got, want) < (BF16_PARAM_TOL if dtype == torch.bfloat16 else 1e-5), i
     for i in range(n):
