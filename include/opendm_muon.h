@@ -103,6 +103,26 @@ int muon_momentum(const muon_momentum_seg* segs_dev, int n_segs, int64_t total_c
                   float* partials_dev /* [total_chunks] scratch */,
                   float* scales_dev /* [n_segs] out */, void* stream);
 
+/* Allocation-free variant of muon_momentum for one matrix. It has no
+ * counterpart in the reference. It exists for callers that cannot allocate
+ * device memory: code that runs inside a host framework whose memory pool
+ * owns every allocation, or inside a region where cudaMalloc is not allowed.
+ * The caller passes only inputs and outputs (grad may be NULL; scale_out is
+ * one device float); the per-chunk scratch is a 64 KiB array inside the
+ * library that every GPU which loads the library keeps until the process
+ * exits. Limit: rows * cols <= MUON_NOALLOC_MAX_ELEMENTS; larger matrices are
+ * rejected with MUON_ERR_ARG. The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress), so make that first call
+ * before any stream capture. All calls on one device share its copy of the
+ * array, which keeps the last call's contents: calls that overlap on that GPU
+ * (for example on two streams) race with each other. Each call writes every
+ * scratch value it reads, so nothing needs clearing between calls. Results
+ * equal muon_momentum's for the same matrix. */
+#define MUON_NOALLOC_MAX_ELEMENTS (16384LL * 16384LL)
+int muon_momentum_single_noalloc(const void* grad, float* exp_avg, void* direction, int64_t rows, int64_t cols,
+                                 int64_t ld, int grad_dtype, int dir_dtype, float momentum, int nesterov,
+                                 float eps, float* scale_out, void* stream);
+
 /* ------------------------------------------- fp16 operand preparation
  * fp16 has tf32's 11-bit significand but a narrow exponent range, so the
  * fp16 Newton-Schulz input is written after normalisation:

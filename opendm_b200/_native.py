@@ -110,6 +110,8 @@ SIGNATURES = {
     "muon_momentum_chunks": (c_int64, [c_int64, c_int64]),
     "muon_momentum": (c_int, [c_void_p, c_int, c_int64, c_int, c_int, c_float, c_int, c_float, c_void_p,
                               c_void_p, c_void_p]),
+    "muon_momentum_single_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_int,
+                                             c_float, c_int, c_float, c_void_p, c_void_p]),
     "muon_convert_f16": (c_int, [c_void_p, c_int, c_int64, c_void_p, c_void_p]),
     "muon_ns_operand_scale": (c_float, [c_int32, c_int32, c_int, c_int]),
     "muon_ns_plan_create": (c_int, [POINTER(NsClass), c_int, c_int, c_int, POINTER(c_void_p)]),

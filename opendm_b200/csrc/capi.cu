@@ -98,6 +98,13 @@ int muon_momentum(const muon_momentum_seg* segs_dev, int n_segs, int64_t total_c
                                eps, partials_dev, scales_dev, static_cast<cudaStream_t>(stream));
 }
 
+int muon_momentum_single_noalloc(const void* grad, float* exp_avg, void* direction, int64_t rows, int64_t cols,
+                                 int64_t ld, int grad_dtype, int dir_dtype, float momentum, int nesterov, float eps,
+                                 float* scale_out, void* stream) {
+  return muon::launch_momentum_single_noalloc(grad, exp_avg, direction, rows, cols, ld, grad_dtype, dir_dtype,
+                                              momentum, nesterov, eps, scale_out, static_cast<cudaStream_t>(stream));
+}
+
 int muon_convert_f16(const muon_convert_seg* segs_dev, int n_segs, int64_t total_chunks, const float* scales_dev,
                      void* stream) {
   return muon::launch_convert(segs_dev, n_segs, total_chunks, scales_dev, static_cast<cudaStream_t>(stream));

@@ -9,6 +9,9 @@
 // of each matrix in a fixed order (deterministic) and produces the input scale
 // 1 / max(||d||_F, eps), or 0 for a zero or non-finite norm.
 
+#include <cstdio>
+#include <mutex>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -278,6 +281,174 @@ int launch_convert(const muon_convert_seg* segs_dev, int n_segs, int64_t total_c
   convert_f16_kernel<<<static_cast<unsigned>(total_chunks), MOM_THREADS, 0, stream>>>(segs_dev, n_segs,
                                                                                        scales_dev);
   if (check_cuda(cudaGetLastError(), "convert launch")) return MUON_ERR_CUDA;
+  return MUON_OK;
+}
+
+// ===========================================================================
+// Allocation-free variant for one matrix (muon_momentum_single_noalloc).
+//
+// Some callers cannot allocate device memory at all: code that runs inside a
+// host framework whose memory pool owns every allocation, or inside a region
+// where cudaMalloc is forbidden. This variant takes only the caller's inputs
+// and outputs; its scratch (one partial sum of d^2 per 16 Ki-element chunk) is
+// this file-scope device array, which every GPU that loads the library keeps
+// until the process exits. Calls that overlap on the GPU share the array and
+// race; each call writes every partial it later reads, so nothing needs to be
+// cleared between calls.
+constexpr int64_t kNoAllocMaxChunks = 16384;  // 64 KiB: up to 16384 * 16384 elements
+constexpr int kMaxNoAllocDevices = 64;
+
+static __device__ __align__(256) float g_noalloc_partials[kNoAllocMaxChunks];
+
+template <int kGradDt, int kDirDt>
+__global__ void __launch_bounds__(MOM_THREADS) momentum_single_noalloc_kernel(muon_momentum_seg sg, float mu,
+                                                                              int nesterov,
+                                                                              float* __restrict__ partials) {
+  __shared__ float red[MOM_THREADS / 32];
+  const int64_t chunk = blockIdx.x;
+  const int64_t numel = sg.rows * sg.cols;
+  const int64_t e0 = chunk * MOM_CHUNK;
+  const int64_t e1 = min(e0 + MOM_CHUNK, numel);
+  const bool nest = nesterov != 0;
+  const bool vec_ok = sg.ld == sg.cols && (numel % 8) == 0 &&
+                      ((reinterpret_cast<uintptr_t>(sg.grad) | reinterpret_cast<uintptr_t>(sg.exp_avg) |
+                        reinterpret_cast<uintptr_t>(sg.direction)) & 15u) == 0;
+  float acc = 0.f;
+  if (vec_ok) {
+    for (int it = 0; it < MOM_ITERS; ++it) {
+      const int64_t e = e0 + (int64_t(it) * MOM_THREADS + threadIdx.x) * MOM_VEC;
+      if (e >= e1) break;
+      float g[8];
+      load_grad8<kGradDt, kDirDt>(sg.grad, e, g);
+      float4* mp = reinterpret_cast<float4*>(sg.exp_avg + e);
+      const float4 m0 = mp[0], m1 = mp[1];
+      const float mo[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+      float mn[8], d[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const MomOut o = mom_op(g[i], mo[i], mu, nest);
+        mn[i] = o.m;
+        d[i] = o.d;
+        acc = fmaf(o.d, o.d, acc);
+      }
+      mp[0] = make_float4(mn[0], mn[1], mn[2], mn[3]);
+      mp[1] = make_float4(mn[4], mn[5], mn[6], mn[7]);
+      store_dir8<kDirDt>(sg.direction, e, d);
+    }
+  } else {
+    for (int64_t e = e0 + threadIdx.x; e < e1; e += MOM_THREADS) {
+      float g = 0.f;
+      if (sg.grad) {
+        if constexpr (kGradDt == MUON_BF16)
+          g = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sg.grad)[e]);
+        else
+          g = reinterpret_cast<const float*>(sg.grad)[e];
+      }
+      const MomOut o = mom_op(g, sg.exp_avg[e], mu, nest);
+      sg.exp_avg[e] = o.m;
+      acc = fmaf(o.d, o.d, acc);
+      const int64_t r = e / sg.cols, c = e - r * sg.cols;
+      const int64_t di = r * sg.ld + c;
+      if constexpr (kDirDt == MUON_BF16)
+        reinterpret_cast<__nv_bfloat16*>(sg.direction)[di] = __float2bfloat16_rn(o.d);
+      else if constexpr (kDirDt == MUON_F32)
+        reinterpret_cast<float*>(sg.direction)[di] = o.d;
+      else
+        reinterpret_cast<float*>(sg.direction)[di] = round_tf32(o.d);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < MOM_THREADS / 32 ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if (threadIdx.x == 0) partials[chunk] = v;
+  }
+}
+
+// Same fixed-order reduction as momentum_scale_kernel, for one matrix.
+__global__ void momentum_single_scale_kernel(const float* __restrict__ partials, int64_t n_chunks, float eps,
+                                             float* __restrict__ scale_out) {
+  const int lane = threadIdx.x & 31;
+  float acc = 0.f;
+  for (int64_t c = lane; c < n_chunks; c += 32) acc += partials[c];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    const float norm = sqrtf(acc);
+    *scale_out = (isfinite(norm) && norm > 0.f) ? 1.0f / fmaxf(norm, eps) : 0.f;
+  }
+}
+
+// Device address of g_noalloc_partials, resolved once per device (with that
+// device current) on the first call made on it.
+static std::mutex g_noalloc_mutex;
+static float* g_noalloc_ptr[kMaxNoAllocDevices] = {};
+
+static int noalloc_scratch(float** out) {
+  int dev = 0;
+  if (check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return MUON_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxNoAllocDevices) return set_error(MUON_ERR_DEVICE, "device ordinal out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (check_cuda(cudaGetSymbolAddress(&p, g_noalloc_partials), "cudaGetSymbolAddress(g_noalloc_partials)"))
+      return MUON_ERR_CUDA;
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return MUON_OK;
+}
+
+int launch_momentum_single_noalloc(const void* grad, float* exp_avg, void* direction, int64_t rows, int64_t cols,
+                                   int64_t ld, int grad_dtype, int dir_dtype, float momentum, int nesterov,
+                                   float eps, float* scale_out, cudaStream_t stream) {
+  if (!exp_avg || !direction || !scale_out) return set_error(MUON_ERR_ARG, "null exp_avg, direction or scale_out");
+  if (rows < 0 || cols < 0 || ld < cols) return set_error(MUON_ERR_ARG, "invalid matrix shape or leading dimension");
+  if (grad_dtype != MUON_BF16 && grad_dtype != MUON_F32)
+    return set_error(MUON_ERR_ARG, "grad_dtype must be MUON_BF16 or MUON_F32");
+  if (dir_dtype != MUON_BF16 && dir_dtype != MUON_TF32 && dir_dtype != MUON_F32)
+    return set_error(MUON_ERR_ARG, "dir_dtype must be MUON_BF16, MUON_TF32 or MUON_F32");
+  const int64_t chunks = momentum_chunks(rows, cols);
+  if (chunks > kNoAllocMaxChunks) {
+    char msg[160];
+    snprintf(msg, sizeof(msg),
+             "matrix of %lld elements exceeds the allocation-free limit of %lld elements; use muon_momentum",
+             static_cast<long long>(rows * cols), static_cast<long long>(kNoAllocMaxChunks * MOM_CHUNK));
+    return set_error(MUON_ERR_ARG, msg);
+  }
+  float* partials = nullptr;
+  const int rc = noalloc_scratch(&partials);
+  if (rc != MUON_OK) return rc;
+  muon_momentum_seg sg;
+  sg.grad = grad;
+  sg.exp_avg = exp_avg;
+  sg.direction = direction;
+  sg.rows = rows;
+  sg.cols = cols;
+  sg.ld = ld;
+  sg.chunk_begin = 0;
+  if (chunks > 0) {
+    const dim3 grid(static_cast<unsigned>(chunks));
+#define MUON_NOALLOC_LAUNCH(G, D) \
+  momentum_single_noalloc_kernel<G, D><<<grid, MOM_THREADS, 0, stream>>>(sg, momentum, nesterov, partials)
+    if (grad_dtype == MUON_BF16) {
+      if (dir_dtype == MUON_BF16) MUON_NOALLOC_LAUNCH(MUON_BF16, MUON_BF16);
+      else if (dir_dtype == MUON_TF32) MUON_NOALLOC_LAUNCH(MUON_BF16, MUON_TF32);
+      else MUON_NOALLOC_LAUNCH(MUON_BF16, MUON_F32);
+    } else {
+      if (dir_dtype == MUON_BF16) MUON_NOALLOC_LAUNCH(MUON_F32, MUON_BF16);
+      else if (dir_dtype == MUON_TF32) MUON_NOALLOC_LAUNCH(MUON_F32, MUON_TF32);
+      else MUON_NOALLOC_LAUNCH(MUON_F32, MUON_F32);
+    }
+#undef MUON_NOALLOC_LAUNCH
+    if (check_cuda(cudaGetLastError(), "momentum (no-alloc) launch")) return MUON_ERR_CUDA;
+  }
+  momentum_single_scale_kernel<<<1, 32, 0, stream>>>(partials, chunks, eps, scale_out);
+  if (check_cuda(cudaGetLastError(), "momentum scale (no-alloc) launch")) return MUON_ERR_CUDA;
   return MUON_OK;
 }
 
