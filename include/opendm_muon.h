@@ -177,7 +177,8 @@ float muon_ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dt
  * `scales` holds the per-matrix input scale produced by muon_momentum.
  *
  * The last iteration writes U, the orthogonalised update, to u_out
- * ([count][rows][ld_u], any alignment) rounded to u_dtype: MUON_F32 for the
+ * ([count][rows][ld_u], 16-byte aligned, ld_u * element size a multiple of
+ * 16 bytes) rounded to u_dtype: MUON_F32 for the
  * exact fp32 result, or the parameter dtype (MUON_BF16), which is the value
  * the reference adds to a bf16 parameter (muon_adamw.py:414 casts the update
  * to the parameter's dtype first). muon_apply_update then applies it.
@@ -233,10 +234,12 @@ int muon_ns_class_layout(muon_ns_class* cls, void* base, int op_dtype);
  * learning-rate scheduler may change them between steps.
  */
 typedef struct muon_update_seg {
-  void* param;         /* [numel] of param_dtype, updated in place */
-  const void* update;  /* [numel] of param_dtype */
-  int64_t numel;
-  int64_t chunk_begin; /* prefix sum of muon_momentum_chunks(1, numel) */
+  void* param;         /* [rows][cols] of param_dtype, updated in place */
+  const void* update;  /* [rows][ld] of param_dtype */
+  int64_t rows;
+  int64_t cols;
+  int64_t ld;          /* >= cols */
+  int64_t chunk_begin; /* prefix sum of muon_momentum_chunks(rows, cols) */
   float eff;
   int32_t param_dtype; /* MUON_BF16 or MUON_F32 */
 } muon_update_seg;

@@ -78,7 +78,9 @@ class UpdateSeg(Structure):
     _fields_ = [
         ("param", c_void_p),
         ("update", c_void_p),
-        ("numel", c_int64),
+        ("rows", c_int64),
+        ("cols", c_int64),
+        ("ld", c_int64),
         ("chunk_begin", c_int64),
         ("eff", c_float),
         ("param_dtype", c_int32),

@@ -50,8 +50,8 @@ constexpr int B_STAGE_BYTES = BN_CTA * 128;
 constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int EPI_WARPS = 4;
 constexpr int NUM_THREADS = 64 + EPI_WARPS * 32;
-constexpr int EPI_PITCH = 33;  // floats per staged row (conflict-free transpose)
-constexpr int EPI_BYTES = 2 * EPI_WARPS * 32 * EPI_PITCH * 4;  // two staging buffers per warp
+constexpr int EPI_WARP_BYTES = 8192;  // per epilogue warp: ring of TMA-store staging buffers
+constexpr int EPI_BYTES = EPI_WARPS * EPI_WARP_BYTES;
 constexpr int BAR_BYTES = 256;
 constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
 constexpr int TMEM_COLS = 2 * BN;
@@ -83,6 +83,8 @@ struct GemmProblem {
 struct GemmParams {
   CUtensorMap map_a[kMaxProblems];
   CUtensorMap map_b[kMaxProblems];
+  CUtensorMap map_out[kMaxProblems];   // D (A', M, X or U): 32 x 32 store boxes
+  CUtensorMap map_out2[kMaxProblems];  // gram: B' 
   GemmProblem prob[kMaxProblems];
   int n_problems;
   int total_tiles;
@@ -157,6 +159,118 @@ __device__ __forceinline__ float load_op(const void* base, long long idx) {
   }
 }
 
+// ------------------------------------------------------------ epilogue I/O
+// A warp stores its 32 x 32 chunk of D through a ring of shared-memory
+// buffers with one TMA store per chunk. The buffers use the layout of the
+// output tensor map's swizzle (64B for 2-byte outputs, 128B for 4-byte ones),
+// which also makes the 16-byte shared stores below bank-conflict free.
+
+// Row-major staging: lane = row, `w` holds the row packed (2-byte: 16 words).
+__device__ __forceinline__ void stage_rows_16(uint8_t* buf, int lane, const uint32_t (&w)[16]) {
+  const uint32_t base = smem_u32(buf) + lane * 64;
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    st_shared_v4(base + ((k ^ sw) << 4), w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+}
+
+__device__ __forceinline__ void stage_rows_32(uint8_t* buf, int lane, const uint32_t (&w)[32]) {
+  const uint32_t base = smem_u32(buf) + lane * 128;
+  const int sw = lane & 7;
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    st_shared_v4(base + ((k ^ sw) << 4), w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+}
+
+// Transposed staging: element (row = lane, col = i) goes to row i, column lane.
+__device__ __forceinline__ void stage_cols_16(uint8_t* buf, int lane, const uint32_t (&w)[16]) {
+  const uint32_t base = smem_u32(buf) + (lane & 7) * 2;
+  const int unit = lane >> 3;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const uint16_t h = static_cast<uint16_t>((i & 1) ? (w[i >> 1] >> 16) : (w[i >> 1] & 0xffffu));
+    st_shared_b16(base + i * 64 + ((unit ^ ((i >> 1) & 3)) << 4), h);
+  }
+}
+
+__device__ __forceinline__ void stage_cols_32(uint8_t* buf, int lane, const uint32_t (&w)[32]) {
+  const uint32_t base = smem_u32(buf) + (lane & 3) * 4;
+  const int unit = lane >> 2;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) st_shared_b32(base + i * 128 + ((unit ^ (i & 7)) << 4), w[i]);
+}
+
+// Rounds 32 fp32 values of one row into output words.
+// kind: 0 = fp32 (raw), 1 = tf32 (rna), 2 = fp16, 3 = bf16.
+template <int kWords>
+__device__ __forceinline__ void pack_row(const float (&x)[32], int kind, uint32_t (&w)[kWords]) {
+  if constexpr (kWords == 32) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(kind == 1 ? round_tf32(x[i]) : x[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (kind == 2) {
+        const __half2 h = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+        w[i] = *reinterpret_cast<const uint32_t*>(&h);
+      } else {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+        w[i] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+    }
+  }
+}
+
+// Per-warp ring of staging buffers: 4 x 2 KB (2-byte outputs) or 2 x 4 KB.
+struct StoreRing {
+  uint8_t* base;
+  int issued;
+  int out_bytes;
+};
+
+template <int kOutBytes>
+__device__ __forceinline__ uint8_t* ring_acquire(StoreRing& ring, int lane) {
+  constexpr int kBuf = kOutBytes == 2 ? 2048 : 4096;
+  constexpr int kN = EPI_WARP_BYTES / kBuf;
+  if (ring.out_bytes != kOutBytes) {  // buffer size changes: let every store finish reading
+    if (lane == 0) bulk_wait_group_read<0>();
+    __syncwarp();
+    ring.issued = 0;
+    ring.out_bytes = kOutBytes;
+  } else if (ring.issued >= kN) {
+    if (lane == 0) bulk_wait_group_read<kN - 1>();  // the store that used this buffer is done
+    __syncwarp();
+  }
+  return ring.base + (ring.issued % kN) * kBuf;
+}
+
+__device__ __forceinline__ void ring_store(StoreRing& ring, uint8_t* buf, const CUtensorMap* map, int lane, int x,
+                                           int y, int z) {
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_3d(map, buf, x, y, z);
+    bulk_commit_group();
+  }
+  ++ring.issued;
+}
+
+// Store one chunk (row-major words of this lane's row) at (x = col0, y = row0)
+// and, when `mirror`, its transpose at (x = row0, y = col0).
+template <int kWords>
+__device__ __forceinline__ void store_chunk(StoreRing& ring, const CUtensorMap* map, int lane, const uint32_t (&w)[kWords],
+                                            int col0, int row0, int g, bool mirror) {
+  constexpr int kOutBytes = kWords == 32 ? 4 : 2;
+  uint8_t* buf = ring_acquire<kOutBytes>(ring, lane);
+  if constexpr (kWords == 32) stage_rows_32(buf, lane, w); else stage_rows_16(buf, lane, w);
+  ring_store(ring, buf, map, lane, col0, row0, g);
+  if (mirror) {
+    buf = ring_acquire<kOutBytes>(ring, lane);
+    if constexpr (kWords == 32) stage_cols_32(buf, lane, w); else stage_cols_16(buf, lane, w);
+    ring_store(ring, buf, map, lane, row0, col0, g);
+  }
+}
+
 template <int kOp>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     ns_gemm_kernel(const __grid_constant__ GemmParams P) {
@@ -175,7 +289,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* stage_a = smem;
   uint8_t* stage_b = smem + STAGES * A_STAGE_BYTES;
-  float* epi_buf = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* epi_buf = smem + STAGES * STAGE_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES + EPI_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
@@ -322,9 +436,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ------------------------------------------------------------- epilogue
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
-    float* buf = epi_buf + (warp - 2) * 32 * EPI_PITCH;
+    StoreRing ring{epi_buf + (warp - 2) * EPI_WARP_BYTES, 0, 0};
     const uint32_t leader_tempty0 = map_shared_rank(smem_u32(&tempty[0]), 0);
     const uint32_t leader_tempty1 = map_shared_rank(smem_u32(&tempty[1]), 0);
+    // Output word kinds: 0 fp32, 1 tf32, 2 fp16, 3 bf16.
+    constexpr int kOpKind = kOp == kOpTf32 ? 1 : kOp == kOpF16 ? 2 : 3;
+    constexpr int kOpWords = kOp == kOpTf32 ? 32 : 16;
     int local_t = 0;
     for (int t = cluster_id; t < P.total_tiles; t += n_clusters, ++local_t) {
       const TileCoord tc = decode_tile(P, t);
@@ -345,85 +462,66 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       }
       const float mul = pr.mul;
       const int row0 = tc.ti * PAIR_M + static_cast<int>(rank) * BM + quad * 32;
-      const long long out_off = static_cast<long long>(tc.g) * pr.out_bs;
       const float f = pr.first ? sc * sc * mul : mul;  // gram: s^2 * mul
       const float fa = pr.first ? sc * mul : mul;      // apply: s * mul
       const bool sym = pr.symmetric != 0;
-      float* buf2 = buf + 32 * EPI_PITCH * EPI_WARPS;   // second staging buffer (gram B')
+      const int myrow = row0 + lane;
+      const CUtensorMap* map1 = &P.map_out[tc.p];
+      const CUtensorMap* map2 = &P.map_out2[tc.p];
 
       for (int ch = 0; ch < BN / 32; ++ch) {
         const int col0 = tc.tj * BN + ch * 32;
         float v[32];
         tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + ch * 32, v);
         if (row0 >= pr.M || col0 >= pr.N) continue;
-        if (sym && col0 + 31 < row0) continue;  // chunk entirely below the diagonal
-        // Row mode (lane = row): epilogue arithmetic on the accumulator row.
-        const int myrow = row0 + lane;
+        // Symmetric outputs: chunks below the diagonal are the mirror of chunks
+        // above it; a diagonal chunk is stored whole, without a mirror.
+        if (sym && col0 + 32 <= row0) continue;
+        const bool mirror = sym && col0 >= row0 + 32;
+        float x[32];
         if (pr.epi == EPI_GRAM) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const float a = zero ? 0.f : v[i] * f;
-            const float ap = (myrow == col0 + i) ? a - 1.f : a;
-            buf[lane * EPI_PITCH + i] = round_op<kOp>(ap);
-            buf2[lane * EPI_PITCH + i] = round_op<kOp>(fmaf(P.gamma, ap, (myrow == col0 + i) ? P.beta : 0.f));
+            x[i] = (myrow == col0 + i) ? a - 1.f : a;  // A'
           }
+          uint32_t w[kOpWords];
+          pack_row<kOpWords>(x, kOpKind, w);
+          store_chunk<kOpWords>(ring, map1, lane, w, col0, row0, tc.g, mirror);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) x[i] = fmaf(P.gamma, x[i], (myrow == col0 + i) ? P.beta : 0.f);  // B'
+          pack_row<kOpWords>(x, kOpKind, w);
+          store_chunk<kOpWords>(ring, map2, lane, w, col0, row0, tc.g, mirror);
         } else if (pr.epi == EPI_POLY) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            buf[lane * EPI_PITCH + i] = round_op<kOp>((myrow == col0 + i) ? v[i] + P.alpha : v[i]);
-        } else if (pr.epi == EPI_APPLY) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) buf[lane * EPI_PITCH + i] = round_op<kOp>(zero ? 0.f : v[i] * fa);
-        } else if (pr.epi == EPI_U_BF16) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) buf[lane * EPI_PITCH + i] = bf16_round(zero ? 0.f : v[i] * fa);
+          for (int i = 0; i < 32; ++i) x[i] = (myrow == col0 + i) ? v[i] + P.alpha : v[i];
+          uint32_t w[kOpWords];
+          pack_row<kOpWords>(x, kOpKind, w);
+          store_chunk<kOpWords>(ring, map1, lane, w, col0, row0, tc.g, mirror);
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) buf[lane * EPI_PITCH + i] = zero ? 0.f : v[i] * fa;
-        }
-        __syncwarp();
-        // Column mode (lane = column): coalesced stores of the 32 rows.
-        const int col = col0 + lane;
-        if (col < pr.N) {
-          const int rmax = min(32, pr.M - row0);
-          if (pr.epi == EPI_U_F32) {
-            float* o = reinterpret_cast<float*>(pr.out) + out_off + static_cast<long long>(row0) * pr.out_ld + col;
-            for (int r = 0; r < rmax; ++r) o[static_cast<long long>(r) * pr.out_ld] = buf[r * EPI_PITCH + lane];
+          for (int i = 0; i < 32; ++i) x[i] = zero ? 0.f : v[i] * fa;
+          if (pr.epi == EPI_APPLY) {
+            uint32_t w[kOpWords];
+            pack_row<kOpWords>(x, kOpKind, w);
+            store_chunk<kOpWords>(ring, map1, lane, w, col0, row0, tc.g, false);
           } else if (pr.epi == EPI_U_BF16) {
-            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(pr.out) + out_off +
-                               static_cast<long long>(row0) * pr.out_ld + col;
-            for (int r = 0; r < rmax; ++r)
-              o[static_cast<long long>(r) * pr.out_ld] = __float2bfloat16_rn(buf[r * EPI_PITCH + lane]);
+            uint32_t w[16];
+            pack_row<16>(x, 3, w);
+            store_chunk<16>(ring, map1, lane, w, col0, row0, tc.g, false);
           } else {
-            const long long base = out_off + static_cast<long long>(row0) * pr.out_ld + col;
-            for (int r = 0; r < rmax; ++r) {
-              if (sym && col < row0 + r) continue;
-              store_op<kOp>(pr.out, base + static_cast<long long>(r) * pr.out_ld, buf[r * EPI_PITCH + lane]);
-              if (pr.epi == EPI_GRAM)
-                store_op<kOp>(pr.out2, base + static_cast<long long>(r) * pr.out_ld, buf2[r * EPI_PITCH + lane]);
-            }
+            uint32_t w[32];
+            pack_row<32>(x, 0, w);
+            store_chunk<32>(ring, map1, lane, w, col0, row0, tc.g, false);
           }
         }
-        if (sym) {
-          // Row mode again: the strict upper part, mirrored (coalesced).
-          if (myrow < pr.M) {
-            const long long base = out_off + myrow;
-            for (int j = 0; j < 32; ++j) {
-              const int c2 = col0 + j;
-              if (c2 > myrow && c2 < pr.N) {
-                store_op<kOp>(pr.out, base + static_cast<long long>(c2) * pr.out_ld, buf[lane * EPI_PITCH + j]);
-                if (pr.epi == EPI_GRAM)
-                  store_op<kOp>(pr.out2, base + static_cast<long long>(c2) * pr.out_ld, buf2[lane * EPI_PITCH + j]);
-              }
-            }
-          }
-        }
-        __syncwarp();
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
     }
+    if (lane == 0) bulk_wait_group_all();  // every TMA store of this warp has completed
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -523,6 +621,37 @@ static int tiles_per_matrix(int M, int N, bool symmetric, int* tm, int* tn) {
   int total = 0;
   for (int ti = 0; ti < *tm; ++ti) total += *tn - ti;  // square tiles: tj in [ti, tn)
   return total;
+}
+
+// Output view [batch][outer][inner] of element type `dtype` (MUON_*) for
+// 32 x 32 TMA stores, swizzled like the epilogue's staging buffers.
+static int encode_output(CUtensorMap* map, const void* base, int dtype, long long inner, long long outer,
+                         long long batch, long long ld, long long bs) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return set_error(MUON_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const int es = (dtype == MUON_F32 || dtype == MUON_TF32) ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    return set_error(MUON_ERR_ARG, "NS output buffer is not 16-byte aligned");
+  if (((ld * es) & 15) != 0 || ((bs * es) & 15) != 0)
+    return set_error(MUON_ERR_ARG, "NS output leading dimension is not a multiple of 16 bytes");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer),
+                        static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld * es), static_cast<cuuint64_t>(bs * es)};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType dt = es == 4             ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == MUON_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                     : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  es == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char msg[160];
+    snprintf(msg, sizeof(msg), "cuTensorMapEncodeTiled (output) failed (%d) for %lldx%lldx%lld ld=%lld", int(r),
+             batch, outer, inner, ld);
+    return set_error(MUON_ERR_CUDA, msg);
+  }
+  return MUON_OK;
 }
 
 int64_t ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype) {
@@ -710,6 +839,19 @@ int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, in
             pr.out = k.u_out;
             pr.out_ld = k.ld_u;
             pr.out_bs = static_cast<long long>(k.rows) * k.ld_u;
+          }
+        }
+        if (rc == MUON_OK) {
+          if (phase == 0) {
+            rc = encode_output(&L.map_out[pi], k.ap, op_dtype, m, m, k.count, k.ld_m, mbs);
+            if (!rc) rc = encode_output(&L.map_out2[pi], k.bp, op_dtype, m, m, k.count, k.ld_m, mbs);
+          } else if (phase == 1) {
+            rc = encode_output(&L.map_out[pi], k.mm, op_dtype, m, m, k.count, k.ld_m, mbs);
+          } else if (pr.epi == EPI_APPLY) {
+            rc = encode_output(&L.map_out[pi], pr.out, op_dtype, k.cols, k.rows, k.count, k.ld_x, xbs);
+          } else {
+            rc = encode_output(&L.map_out[pi], k.u_out, k.u_dtype, k.cols, k.rows, k.count, k.ld_u,
+                               static_cast<long long>(k.rows) * k.ld_u);
           }
         }
         if (rc != MUON_OK) {

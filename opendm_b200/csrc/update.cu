@@ -37,7 +37,8 @@ __device__ __forceinline__ float upd_elem(float p, float u, float neg_eff, float
 template <bool kBf16>
 __device__ __forceinline__ void update_chunk(const muon_update_seg& sg, int64_t e0, int64_t e1, float wd_factor) {
   const float neg_eff = -sg.eff;
-  const bool vec_ok = (sg.numel % 8) == 0 &&
+  const int64_t numel = sg.rows * sg.cols;
+  const bool vec_ok = sg.ld == sg.cols && (numel % 8) == 0 &&
                       ((reinterpret_cast<uintptr_t>(sg.param) | reinterpret_cast<uintptr_t>(sg.update)) & 15u) == 0;
   if (vec_ok) {
     for (int it = 0; it < UPD_ITERS; ++it) {
@@ -76,13 +77,15 @@ __device__ __forceinline__ void update_chunk(const muon_update_seg& sg, int64_t 
     }
   } else {
     for (int64_t e = e0 + threadIdx.x; e < e1; e += UPD_THREADS) {
+      const int64_t r = e / sg.cols, c = e - r * sg.cols;
+      const int64_t ui = r * sg.ld + c;
       if constexpr (kBf16) {
         __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(sg.param) + e;
-        const float u = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sg.update)[e]);
+        const float u = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sg.update)[ui]);
         *p = __float2bfloat16_rn(upd_elem<true>(__bfloat162float(*p), u, neg_eff, wd_factor));
       } else {
         float* p = reinterpret_cast<float*>(sg.param) + e;
-        *p = upd_elem<false>(*p, reinterpret_cast<const float*>(sg.update)[e], neg_eff, wd_factor);
+        *p = upd_elem<false>(*p, reinterpret_cast<const float*>(sg.update)[ui], neg_eff, wd_factor);
       }
     }
   }
@@ -93,7 +96,7 @@ __global__ void __launch_bounds__(UPD_THREADS) apply_update_kernel(const muon_up
   const int64_t chunk = blockIdx.x;
   const muon_update_seg sg = segs[find_update_segment(segs, n_segs, chunk)];
   const int64_t e0 = (chunk - sg.chunk_begin) * UPD_CHUNK;
-  const int64_t e1 = min(e0 + UPD_CHUNK, sg.numel);
+  const int64_t e1 = min(e0 + UPD_CHUNK, sg.rows * sg.cols);
   if (sg.param_dtype == MUON_BF16)
     update_chunk<true>(sg, e0, e1, wd_factor);
   else

@@ -58,6 +58,12 @@ def _dtype_code(t: torch.Tensor) -> int:
         raise RuntimeError(f"unsupported dtype {t.dtype}: the kernels take bfloat16 or float32") from None
 
 
+def _pad16(cols: int, dtype: torch.dtype) -> int:
+    """Row length padded so a row is a multiple of 16 bytes."""
+    per = 16 // torch.empty((), dtype=dtype).element_size()
+    return (cols + per - 1) // per * per
+
+
 def _stream_handle() -> c_void_p:
     return c_void_p(torch.cuda.current_stream().cuda_stream)
 
@@ -176,11 +182,13 @@ class CudaMuonEngine:
             for slot, i in enumerate(idxs):
                 self._order[i] = (ci, slot)
                 self._seg_order.append(i)
-            # U, rounded to the parameter dtype, for muon_apply_update.
-            cs.u_buf = torch.empty((len(idxs), r, c), dtype=dt, device=self.device)
+            # U, rounded to the parameter dtype, for muon_apply_update; rows padded
+            # to 16 bytes for the epilogue's TMA stores.
+            ld_u = _pad16(c, dt)
+            cs.u_buf = torch.empty((len(idxs), r, ld_u), dtype=dt, device=self.device)
             cs.cls.u_dtype = _dtype_code(items[idxs[0]].param)
             cs.cls.u_out = c_void_p(cs.u_buf.data_ptr())
-            cs.cls.ld_u = c
+            cs.cls.ld_u = ld_u
             self._classes.append(cs)
         self._scales = torch.zeros(max(len(items), 1), dtype=torch.float32, device=self.device)
         first = 0
@@ -315,12 +323,12 @@ class CudaMuonEngine:
             sg = N.UpdateSeg()
             sg.param = it.param.data_ptr()
             sg.update = cs.u_buf[slot].data_ptr()
-            sg.numel = cs.rows * cs.cols
+            sg.rows, sg.cols, sg.ld = cs.rows, cs.cols, int(cs.cls.ld_u)
             sg.chunk_begin = total
             sg.eff = it.eff
             sg.param_dtype = cs.cls.u_dtype
             segs.append(sg)
-            total += int(self.lib.muon_momentum_chunks(1, sg.numel))
+            total += int(self.lib.muon_momentum_chunks(cs.rows, cs.cols))
         table = _upload(N.struct_bytes(segs), self.device)
         ev = self._event_pair("update")
         N.check(self.lib.muon_apply_update(c_void_p(table.data_ptr()), len(segs), total, c_float(wd_factor),
@@ -389,9 +397,11 @@ class CudaMuonEngine:
         if matrix.device != self.device:
             raise RuntimeError("matrix is not on the engine's device")
         rows, cols = (int(s) for s in matrix.shape)
-        out = torch.zeros((rows, cols), dtype=torch.float32, device=self.device)
         if matrix.numel() == 0:
-            return out
+            return torch.zeros((rows, cols), dtype=torch.float32, device=self.device)
+        ld_out = _pad16(cols, torch.float32)
+        out_buf = torch.zeros((rows, ld_out), dtype=torch.float32, device=self.device)
+        out = out_buf[:, :cols]
         src = matrix if matrix.dtype in (torch.float32, torch.bfloat16) else matrix.float()
         src = src.contiguous()
         cs = _ClassState(rows, cols, torch.float32, 1, self.op_dtype, self.device)
@@ -423,8 +433,8 @@ class CudaMuonEngine:
                 return staging * scales[0]
             return cs.x0_view(0).float() * scales[0]
         cs.cls.scales = c_void_p(scales.data_ptr())
-        cs.cls.u_out = c_void_p(out.data_ptr())
-        cs.cls.ld_u = cols
+        cs.cls.u_out = c_void_p(out_buf.data_ptr())
+        cs.cls.ld_u = ld_out
         cs.cls.u_dtype = N.MUON_F32
         plan = c_void_p()
         N.check(self.lib.muon_ns_plan_create(byref(cs.cls), 1, self.op_dtype, int(steps), byref(plan)),
