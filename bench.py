@@ -1,7 +1,7 @@
 """Benchmark: one full MuonAdamW optimizer step (Muon + AdamW groups).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c4|c5]
-                    [--precision tf32|bf16] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c2s|c4|c5]
+                    [--precision fp16|tf32|bf16] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
 
 Workloads (synthetic, seeded; shapes of the configurations the reference's
@@ -14,6 +14,8 @@ metric is quoted on):
       + action expert 18x (1024, MLP 4096), 540 Muon matrices + norms.
   c5  7B-class decoder, 32 layers, hidden 4096, MLP 11008 (224 Muon matrices),
       gradients with 1% heavy-tail entries.
+  c2s the first 4 layers of c2 (28 Muon matrices, no embedding): the small
+      case for profiler captures, not a bench line.
 Parameters bf16 ~ N(0, 0.02), gradients bf16 ~ N(0, 1e-3), fp32 optimizer state.
 
 Rank 0 prints one JSON line. `value` is the device time of one optimizer step
@@ -21,7 +23,10 @@ Rank 0 prints one JSON line. `value` is the device time of one optimizer step
 same step measured through the public API with the gradients copied in from
 pinned host memory every step and a slice of the updated parameters read
 back. `roofline` is the Newton-Schulz GEMMs' dense FLOP rate against the
-measured bf16 tensor peak. `cpu_baseline` (N = 1, rank 0) is the numpy oracle
+measured bf16 tensor peak (plus the FLOPs the tiles actually execute:
+256 x 256 tiles, upper triangle of symmetric products). The timed steps sit
+inside a CUDA profiler range (ncu --profile-from-start off captures only
+them). `cpu_baseline` (N = 1, rank 0) is the numpy oracle
 of the reference algorithm on the host cores, timed on one matrix of every
 shape class and extrapolated by multiplicity.
 
@@ -93,6 +98,8 @@ def config_params(name: str):
                 + [("language.norm.weight", (2560,)), ("action_expert.norm.weight", (1024,))])
     if name == "c5":
         return decoder_layers("model", 32, 4096, 4096, 4096, 11008) + [("model.norm.weight", (4096,))]
+    if name == "c2s":
+        return decoder_layers("model", 4, 2048, 2048, 256, 8192) + [("model.norm.weight", (2048,))]
     raise ValueError(f"unknown config {name!r}")
 
 
@@ -104,6 +111,7 @@ DESCRIPTIONS = {
     "c2": "2B-class decoder (28L, h2048, GQA kv256, SwiGLU 8192) + 151936x2048 embedding",
     "c4": "~4B VLA (ViT 27L h1152/4304 + LM 36L h2560 kv512/9728 + AE 18L h1024/4096)",
     "c5": "7B-class decoder (32L, h4096, MHA, SwiGLU 11008), 1% heavy-tail grads",
+    "c2s": "first 4 layers of the 2B-class decoder (profiling case)",
 }
 
 
@@ -111,6 +119,24 @@ DESCRIPTIONS = {
 def ns_flops(shape, steps=NS_STEPS):
     m, n = min(shape), max(shape)
     return steps * (4.0 * m * m * n + 2.0 * m ** 3)
+
+
+def ns_executed_flops(shape, steps=NS_STEPS):
+    """FLOPs the Newton-Schulz launches execute for one matrix: 256 x 256
+    output tiles, K rounded up to the 64-deep stage, upper-triangle tiles only
+    for the two symmetric m x m products (gram, poly)."""
+    rows, cols = shape
+    m, n = min(shape), max(shape)
+
+    def kpad(k):
+        return (k + 63) // 64 * 64
+
+    t = (m + 255) // 256
+    sym_tiles = t * (t + 1) // 2
+    gram = sym_tiles * 256 * 256 * 2 * kpad(n)
+    poly = sym_tiles * 256 * 256 * 2 * kpad(m)
+    apply = ((rows + 255) // 256) * ((cols + 255) // 256) * 256 * 256 * 2 * kpad(m)
+    return steps * float(gram + poly + apply)
 
 
 def load_peaks():
@@ -315,15 +341,17 @@ def run_ours(args):
     sampler = ClockSampler([local] if world == 1 else list(range(world))) if rank == 0 else None
     launches0 = engine.kernel_launches
     engine.profile_events = []
-    sync_all()
     if sampler:
         sampler.start()
-        time.sleep(0.5)
+        time.sleep(0.5)  # first samples land before the timed region
+    sync_all()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.profiler.start()
     start.record()
     for _ in range(args.steps):
         opt.step()
     end.record()
+    torch.cuda.profiler.stop()
     sync_all()
     clocks = sampler.stop() if sampler else None
     step_ms = max_over_ranks(start.elapsed_time(end) / args.steps)
@@ -338,19 +366,26 @@ def run_ours(args):
     mom_ms = statistics.mean(per.get("momentum", [0.0])) if per.get("momentum") else 0.0
     adam_ms = statistics.mean(per.get("adamw", [0.0])) if per.get("adamw") else 0.0
     upd_ms = statistics.mean(per.get("update", [0.0])) if per.get("update") else 0.0
+    ag_ms = max_over_ranks(statistics.mean(per["allgather"])) if per.get("allgather") else 0.0
 
     muon_shapes = [s for n, s in spec if is_muon(n, s)]
     total_flops = sum(ns_flops(s) for s in muon_shapes)
     # FLOPs this rank ran (its owned matrices); the roofline uses the busiest rank.
     owners = opt._owners.get(id(opt.param_groups[1]))
     if owners is not None:
-        my_flops = sum(ns_flops(s) for s, o in zip(opt.param_groups[1]["muon_shapes"], owners) if o == rank)
-        my_elems = sum(math.prod(s) for s, o in zip(opt.param_groups[1]["muon_shapes"], owners) if o == rank)
+        mine = [s for s, o in zip(opt.param_groups[1]["muon_shapes"], owners) if o == rank]
     else:
-        my_flops = total_flops
-        my_elems = sum(math.prod(s) for s in muon_shapes)
-    ns_tflops = my_flops / (ns_ms * 1e-3) / 1e12 if ns_ms > 0 else 0.0
+        mine = muon_shapes
+    my_flops = sum(ns_flops(s) for s in mine)
+    my_exec = sum(ns_executed_flops(s) for s in mine)
+    my_elems = sum(math.prod(s) for s in mine)
+    my_ns_ms = statistics.mean(per["ns"]) if per.get("ns") else 0.0
+    ns_tflops = my_flops / (my_ns_ms * 1e-3) / 1e12 if my_ns_ms > 0 else 0.0
+    ns_exec_tflops = my_exec / (my_ns_ms * 1e-3) / 1e12 if my_ns_ms > 0 else 0.0
     ns_tflops = -max_over_ranks(-ns_tflops)  # slowest rank
+    ns_exec_tflops = -max_over_ranks(-ns_exec_tflops)
+    bucket = opt._buckets.get(id(opt.param_groups[1]))
+    ag_bytes = bucket.nbytes_received() if bucket is not None else 0
     # grad (bf16) + exp_avg read/write + direction write (+ the fp16 convert pass)
     mom_bytes = my_elems * {"tf32": 2 + 4 + 4 + 4, "bf16": 2 + 4 + 4 + 2, "fp16": 2 + 8 + 4 + 4 + 2}[args.precision]
     mom_gbs = mom_bytes / (mom_ms * 1e-3) / 1e9 if mom_ms > 0 else 0.0
@@ -358,18 +393,25 @@ def run_ours(args):
     adam_gbs = adam_elems * (2 + 2 + 8 + 8 + 2) / (adam_ms * 1e-3) / 1e9 if adam_ms > 0 else 0.0
 
     # ---- end-to-end through the public API with host-resident gradients
-    host_grads = [g.cpu().pin_memory() for g in grads]
+    # The gradients this rank's step reads: with owner-only momentum a rank
+    # never reads the gradients of matrices another rank owns.
+    needed = list(range(len(params)))
+    if owners is not None and opt.state_sharding:
+        owned_ids = {id(p) for p, o in zip(opt.param_groups[1]["params"], owners) if o == rank}
+        muon_ids = {id(p) for p in opt.param_groups[1]["params"]}
+        needed = [i for i, p in enumerate(params) if id(p) not in muon_ids or id(p) in owned_ids]
+    host_grads = {i: grads[i].cpu().pin_memory() for i in needed}
     probe = params[-1] if params[-1].ndim == 1 else params[0]
     readback = torch.empty(min(probe.numel(), 4096), dtype=probe.dtype).pin_memory()
-    h2d = sum(g.numel() * g.element_size() for g in host_grads)
+    h2d = sum(g.numel() * g.element_size() for g in host_grads.values())
     d2h = readback.numel() * readback.element_size()
     e2e_steps = max(2, min(args.steps, 5))
     sync_all()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record()
     for _ in range(e2e_steps):
-        for p, hg in zip(params, host_grads):
-            p.grad.copy_(hg, non_blocking=True)
+        for i, hg in host_grads.items():
+            params[i].grad.copy_(hg, non_blocking=True)
         opt.step()
         readback.copy_(probe.detach().reshape(-1)[: readback.numel()], non_blocking=True)
     e_end.record()
@@ -398,6 +440,9 @@ def run_ours(args):
             "roofline": {"bound": "tensor", "kernel": "ns_gemm (15 grouped launches per step)",
                          "achieved": round(ns_tflops, 1), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(ns_tflops / peak, 4), "peak_source": f"{peaks['source']} bf16 sustained",
+                         "flops": "dense: steps*(4 m^2 n + 2 m^3) per matrix",
+                         "executed_tflops": round(ns_exec_tflops, 1),
+                         "executed_frac": round(ns_exec_tflops / peak, 4),
                          "frac_of_tf32_peak": round(ns_tflops / (peak / 2), 4) if args.precision == "tf32" else None,
                          "mma_kind": "kind::tf32" if args.precision == "tf32" else "kind::f16",
                          "traffic": None, "ns_ms": round(ns_ms, 3)},
@@ -406,6 +451,9 @@ def run_ours(args):
                             "update_gbs": round(my_elems * 6 / (upd_ms * 1e-3) / 1e9, 1) if upd_ms > 0 else 0.0,
                             "adamw_ms": round(adam_ms, 3), "adamw_gbs": round(adam_gbs, 1),
                             "hbm_peak_gbs": peaks["hbm_gbs"]},
+            "collective": ({"allgather_ms": round(ag_ms, 3), "allgather_bytes_received": ag_bytes,
+                            "allgather_gbs": round(ag_bytes / (ag_ms * 1e-3) / 1e9, 1) if ag_ms > 0 else 0.0}
+                           if world > 1 else None),
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
@@ -420,8 +468,8 @@ def main(argv=None):
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="c2", choices=["c2", "c4", "c5"])
-    ap.add_argument("--precision", default="tf32", choices=["tf32", "fp16", "bf16"])
+    ap.add_argument("--config", default="c2", choices=["c2", "c2s", "c4", "c5"])
+    ap.add_argument("--precision", default="fp16", choices=["fp16", "tf32", "bf16"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)

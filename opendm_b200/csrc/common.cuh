@@ -100,7 +100,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 3-D tiled bulk tensor load (no multicast) completing on an mbarrier.
+// 3-D tiled bulk tensor load into this CTA's shared memory, completing on an mbarrier.
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
                                             int x, int y, int z) {
   asm volatile(
@@ -113,7 +113,7 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
 // 3-D tiled bulk tensor load for a CTA pair (tcgen05 cta_group::2): the data
 // lands in this CTA's shared memory; the transaction bytes are counted on the
 // mbarrier at `bar_cluster`, a shared::cluster address that may belong to the
-// peer CTA of the pair. No multicast.
+// peer CTA of the pair. Each CTA fetches only its own tile.
 __device__ __forceinline__ void tma_load_3d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster,
                                                  int x, int y, int z) {
   asm volatile(

@@ -20,12 +20,12 @@
 //   warp 0      TMA producer (both CTAs): a 6-stage ring; the bytes of both
 //               CTAs complete on the leader CTA's full barrier
 //   warp 1      TMEM allocation (both CTAs); single-thread MMA issuer (leader)
-//   warps 2..5  epilogue (both CTAs): tcgen05.ld -> registers -> smem
-//               transpose -> coalesced global stores (+ mirrored stores for
-//               symmetric C)
+//   warps 2..5  epilogue (both CTAs): tcgen05.ld -> registers -> swizzled
+//               shared-memory staging -> one TMA tensor store per 32 x 32
+//               chunk (+ a transposed mirror store for symmetric C)
 // Accumulators: two 128 x 256 fp32 buffers per CTA in TMEM (all 512 columns),
-// so the epilogue of tile i overlaps the main loop of tile i+1. No TMA
-// multicast is used: each CTA loads its own operand halves.
+// so the epilogue of tile i overlaps the main loop of tile i+1. Each CTA
+// loads its own operand halves with plain (single-destination) TMA loads.
 // Operands are bf16 (kind::f16) or tf32 (kind::tf32); either way a stage
 // holds 128 bytes of K per row, so the byte geometry is identical.
 

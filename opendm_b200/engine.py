@@ -103,7 +103,7 @@ class _ClassState:
 class CudaMuonEngine:
     """Runs the Muon and AdamW kernels on one CUDA device."""
 
-    def __init__(self, device: torch.device | str | int, precision: str = "tf32"):
+    def __init__(self, device: torch.device | str | int, precision: str = "fp16"):
         if precision not in PRECISIONS:
             raise ValueError(f"precision must be one of {sorted(PRECISIONS)}, got {precision!r}")
         self.device = torch.device(device) if not isinstance(device, int) else torch.device("cuda", device)

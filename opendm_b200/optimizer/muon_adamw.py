@@ -15,10 +15,10 @@ The arithmetic runs in the sm_100a kernels of ``libopendm_muon.so`` through
 (defaults reproduce the reference):
 
 * ``precision``: Newton-Schulz operand type, fp32 accumulation throughout.
-  "tf32" (default): operands rounded to tf32. "fp16": operands in fp16
-  (the same 11-bit significand as tf32, twice the tensor-core rate), each
-  stored matrix scaled by a power of two to stay in fp16's range; accuracy
-  equal to "tf32". "bf16": fastest storage, ~1e-2 relative update error.
+  "fp16" (default): operands in fp16, each stored matrix scaled by a power
+  of two to stay in fp16's range; the same 11-bit significand as tf32 at
+  twice the tensor-core rate. "tf32": operands rounded to tf32, the same
+  accuracy at half the rate. "bf16": ~1e-2 relative update error (opt-in).
 * ``scale_mode``: "reference" (lr * lr_scale * coefficient * sqrt(max(r, c)))
   or "shape" (lr * lr_scale * max(1, r / c) ** 0.5).
 * ``sharding``: "auto" (default: with world size > 1 and replicated
@@ -146,7 +146,7 @@ def _engine_for(device: torch.device, precision: str) -> CudaMuonEngine:
 
 
 def zeropower_via_newtonschulz5(matrix: torch.Tensor, steps: int = 5, eps: float = 1e-7, *,
-                                precision: str = "tf32") -> torch.Tensor:
+                                precision: str = "fp16") -> torch.Tensor:
     """Quintic Newton-Schulz orthogonalisation on the GPU (reference :101-128).
 
     Returns fp32 with the input's shape; a zero or non-finite input gives
@@ -166,7 +166,7 @@ class MuonAdamW(torch.optim.Optimizer):
     def __init__(self, model: torch.nn.Module, *, lr: float, betas: tuple[float, float], eps: float,
                  weight_decay: float, muon_momentum: float = 0.95, muon_nesterov: bool = True,
                  muon_ns_steps: int = 5, muon_lr_scale: float = 1.0, muon_moonlight_coefficient: float = 0.2,
-                 precision: str = "tf32", scale_mode: str = "reference", sharding: str = "auto",
+                 precision: str = "fp16", scale_mode: str = "reference", sharding: str = "auto",
                  state_sharding: bool = False, process_group=None, _engine=None) -> None:
         adamw_params, muon_params, muon_shapes, muon_names = [], [], [], []
         for param in model.parameters():
@@ -207,6 +207,7 @@ class MuonAdamW(torch.optim.Optimizer):
         self._host_steps: dict = {}
         self._owners: dict[int, list[int]] = {}
         self._buckets: dict[int, FlatParamBuckets] = {}
+        self._flag_group = None  # host (gloo) group for the per-step activity flag
 
     # ---------------------------------------------------------------- groups
     def _normalize_param_groups(self) -> None:
@@ -329,14 +330,32 @@ class MuonAdamW(torch.optim.Optimizer):
             return params[0].device
         return torch.device("cuda" if torch.cuda.is_available() else "cpu")
 
+    def _host_flag_group(self):
+        """A gloo group over the ranks of ``process_group``, created on first
+        use (every rank reaches the first Muon step together)."""
+        if self._flag_group is None:
+            pg = self.process_group
+            if dist.get_backend(pg) == "gloo":
+                self._flag_group = (pg,)
+            else:
+                ranks = dist.get_process_group_ranks(pg) if pg is not None else None
+                self._flag_group = (dist.new_group(ranks=ranks, backend="gloo",
+                                                   use_local_synchronization=pg is not None),)
+        return self._flag_group[0]
+
     def _muon_group_is_active(self, params: list[torch.Tensor]) -> bool:
-        """True when any rank has a Muon gradient (reference :350-360)."""
+        """True when any rank has a Muon gradient (reference :350-360).
+
+        The reference reduces a device flag and reads it back, which waits
+        for every kernel queued so far. The flag is a host fact, so here it
+        is reduced over a gloo group on the host: same answer, and the host
+        keeps queueing work while the GPU runs the previous step."""
         local_active = any(p.grad is not None for p in params)
         if not _dist_ready():
             return local_active
-        flag = torch.tensor(int(local_active), dtype=torch.int32, device=self._device_for_params(params))
-        dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=self.process_group)
-        return bool(flag.item())
+        flag = torch.tensor([int(local_active)], dtype=torch.int32)
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=self._host_flag_group())
+        return bool(flag[0])
 
     def _world(self) -> tuple[int, int]:
         if not _dist_ready():
@@ -410,7 +429,10 @@ class MuonAdamW(torch.optim.Optimizer):
             self._partial_update(engine, param, grad, state, shape, plan, eff, momentum, nesterov, wd_factor,
                                  ns_steps)
         if sharded:
+            ev = engine._event_pair("allgather") if getattr(engine, "profile_events", None) is not None else None
             self._buckets[id(group)].sync()
+            if ev is not None:
+                engine._event_end(ev)
 
     def _partial_update(self, engine, param, grad, state, shape, plan, eff, momentum, nesterov, wd_factor,
                         ns_steps) -> None:

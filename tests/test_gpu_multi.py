@@ -1,0 +1,116 @@
+"""Two GPUs over NCCL: the FLOP-balanced Newton-Schulz sharding (each matrix
+orthogonalised by one owner rank, the updated parameters all-gathered into
+flat per-dtype buckets) gives bit-identical parameters to every rank running
+every matrix (sharding="off", the reference's redundant schedule), with every
+momentum buffer current (state_sharding=False) and with owner-only momentum
+consolidated afterwards (state_sharding=True).
+
+Bitwise equality holds because each matrix's kernels see the same inputs in
+both schedules and every reduction (momentum norm partials, tile K order) is
+deterministic per matrix. Needs two CUDA devices; skipped otherwise."""
+
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+# One BASELINE config 2 decoder layer (q/o, k/v, gate/up, down) plus a tall
+# and a ragged matrix, bf16 parameters, and AdamW vectors.
+MUON = [(2048, 2048), (256, 2048), (256, 2048), (2048, 2048), (8192, 2048), (8192, 2048), (2048, 8192),
+        (1000, 300), (72, 130)]
+ADAM = [(2048,), (2048,), (37,)]
+STEPS = 2
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _build(dev, sharding, state_sharding):
+    from opendm_b200.optimizer import MuonAdamW
+
+    g = torch.Generator(device=dev).manual_seed(11)
+    model = torch.nn.Module()
+    for i, shape in enumerate(MUON + ADAM):
+        t = torch.nn.Parameter((torch.randn(shape, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+        if i < len(MUON):
+            t._opendm_muon_shape = tuple(shape)
+            t._opendm_muon_name = f"m{i}"
+        model.register_parameter(f"p{i}", t)
+    opt = MuonAdamW(model, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, sharding=sharding,
+                    state_sharding=state_sharding)
+    return model, opt
+
+
+def _worker(rank, port, outdir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    result = {"rank": rank}
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=timedelta(seconds=60), device_id=dev)
+        runs = {}
+        for name, sharding, state_sharding in (("off", "off", False), ("auto", "auto", False),
+                                               ("auto_owner", "auto", True)):
+            model, opt = _build(dev, sharding, state_sharding)
+            gg = torch.Generator(device=dev).manual_seed(12)
+            for _ in range(STEPS):
+                for p in model.parameters():
+                    p.grad = (torch.randn(p.shape, generator=gg, device=dev) * 1e-3).to(torch.bfloat16)
+                opt.step()
+            opt.consolidate_state_dict()
+            opt.check_device_errors()
+            owners = opt._owners.get(id(opt.param_groups[1]))
+            runs[name] = {"params": [p.detach().cpu() for p in model.parameters()],
+                          "exp_avg": [opt.state[p]["exp_avg"].cpu() for p in opt.param_groups[1]["params"]],
+                          "owners": owners}
+        result["runs"] = runs
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as exc:  # reported to the parent
+        result["error"] = f"{type(exc).__name__}: {exc}"
+        result["trace"] = traceback.format_exc()
+    torch.save(result, os.path.join(outdir, f"rank{rank}.pt"))
+
+
+def test_two_gpu_sharded_equals_unsharded(tmp_path):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
+        pytest.skip("needs two CUDA devices")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, port, str(tmp_path))) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("rank did not finish")
+    res = [torch.load(os.path.join(tmp_path, f"rank{r}.pt"), weights_only=False) for r in range(WORLD)]
+    for r in res:
+        assert "error" not in r, r.get("trace")
+    ref = res[0]["runs"]["off"]
+    owners = res[0]["runs"]["auto"]["owners"]
+    assert owners is not None and set(owners) == {0, 1}  # both ranks own work
+    for r in res:
+        for name in ("off", "auto", "auto_owner"):
+            run = r["runs"][name]
+            for i, (got, want) in enumerate(zip(run["params"], ref["params"])):
+                assert torch.equal(got, want), (r["rank"], name, "param", i)
+            for i, (got, want) in enumerate(zip(run["exp_avg"], ref["exp_avg"])):
+                assert torch.equal(got, want), (r["rank"], name, "exp_avg", i)

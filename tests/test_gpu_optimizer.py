@@ -113,7 +113,7 @@ def test_dropin_matches_reference_golden(golden_dir, name, dtype):
         assert float(st["step"]) == float(z[f"step/{k}"])
 
 
-def _run_config(shapes_muon, shapes_adam, dtype, steps, seed=0):
+def _run_config(shapes_muon, shapes_adam, dtype, steps, seed=0, precision="fp16"):
     """Our optimizer vs the oracle (CUDA rounding semantics) on seeded data."""
     from opendm_b200.optimizer import MuonAdamW, mark_muon_parameters
 
@@ -128,7 +128,7 @@ def _run_config(shapes_muon, shapes_adam, dtype, steps, seed=0):
         model.register_parameter(f"p{i}", torch.nn.Parameter(torch.from_numpy(h).to(dtype).to(dev)))
     n = len(shapes_muon)
     mark_muon_parameters(model, predicate=lambda nm, p: int(nm[1:]) < n)
-    opt = MuonAdamW(model, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01)
+    opt = MuonAdamW(model, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, precision=precision)
     ref = O.OracleMuonAdamW(lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01)
     mp_ = {str(i): host[i].copy() for i in range(n)}
     ap_ = {str(i): host[i].copy() for i in range(n, len(host))}
@@ -167,12 +167,14 @@ def test_baseline_config1_single_gpu():
     _run_config([(512, 512), (512, 2048), (2048, 512), (1024, 1024)] * 2, [(512,)] * 4, torch.float32, 2)
 
 
+@pytest.mark.parametrize("precision", ["fp16", "tf32"])
 @pytest.mark.parametrize("steps", [1, 2])
-def test_baseline_config2_layer_bf16(steps):
+def test_baseline_config2_layer_bf16(steps, precision):
     """One full BASELINE config 2 decoder layer (bf16 params): q/o 2048^2,
-    k/v 256x2048, gate/up 8192x2048, down 2048x8192 + norms; 1 and 2 steps."""
+    k/v 256x2048, gate/up 8192x2048, down 2048x8192 + norms; 1 and 2 steps,
+    both 11-bit operand precisions."""
     shapes = [(2048, 2048), (256, 2048), (256, 2048), (2048, 2048), (8192, 2048), (8192, 2048), (2048, 8192)]
-    _run_config(shapes, [(2048,), (2048,)], torch.bfloat16, steps)
+    _run_config(shapes, [(2048,), (2048,)], torch.bfloat16, steps, precision=precision)
 
 
 def test_update_parity_at_config2_shapes():
