@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define MUON_ABI_VERSION 1
+#define MUON_ABI_VERSION 2
 
 enum muon_status {
   MUON_OK = 0,
@@ -48,6 +48,11 @@ enum muon_dtype {
   MUON_F32 = 1,  /* float32 storage */
   MUON_TF32 = 2, /* float32 storage holding values rounded to tf32 (NS operands) */
   MUON_F16 = 3   /* float16 storage (NS operands, scaled by powers of two) */
+};
+
+enum muon_ns_algo {
+  MUON_NS_STANDARD = 0, /* Newton-Schulz iteration on X */
+  MUON_NS_GRAM = 1      /* iteration on the gram matrix, X updated every 3 iterations */
 };
 
 /* ------------------------------------------------------------------ misc */
@@ -166,12 +171,26 @@ float muon_ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dt
  * transpose is expressed by operand majorness, so X keeps the parameter's
  * layout and no transposed copy is made.
  *
- * Each class owns five caller-provided buffers of op dtype (MUON_BF16 and
+ * Two algorithms (muon_ns_class.algo):
+ *   MUON_NS_STANDARD  every iteration on X: gram, poly and apply launches.
+ *   MUON_NS_GRAM      the iteration on the m x m gram matrix A = X X^T: each
+ *                     P_j = a + b A_j + c A_j^2 is a polynomial of A_j, so
+ *                     A_{j+1} = P_j (P_j A_j) and X_k = (P_{k-1} ... P_s) X_s;
+ *                     the product is applied to X once per 3 iterations, after
+ *                     which A is recomputed from X (a restart that keeps the
+ *                     rounding of the m x m products from growing). For
+ *                     n >= ~1.5 m it executes about 1.7x fewer FLOPs; it needs
+ *                     MUON_F16 or MUON_TF32 operands. muon_ns_choose_algo
+ *                     returns the cheaper one for a shape.
+ * Both give the same result up to operand rounding.
+ *
+ * Each class owns caller-provided buffers of op dtype (MUON_BF16 and
  * MUON_F16: 2 bytes, MUON_TF32: 4 bytes per element):
  *   x0, x1:     [count][rows][ld_x]  (x0 holds the direction written by
  *               muon_momentum, or by muon_convert_f16 for MUON_F16, which
  *               stores it normalised; x1 is the ping-pong partner)
  *   ap, bp, mm: [count][m][ld_m]     m = min(rows, cols)
+ *   aa, pa, qa, qb: [count][m][ld_m] (MUON_NS_GRAM only; NULL otherwise)
  * ld_x and ld_m must make rows 16-byte aligned (multiple of 8 for 2-byte,
  * of 4 for 4-byte types), and every buffer must be 16-byte aligned.
  * `scales` holds the per-matrix input scale produced by muon_momentum.
@@ -198,6 +217,12 @@ typedef struct muon_ns_class {
   const float* scales; /* [count] device */
   void* u_out;         /* [count][rows][ld_u] of u_dtype */
   int64_t ld_u;
+  int32_t algo;        /* MUON_NS_STANDARD or MUON_NS_GRAM */
+  int32_t reserved;
+  void* aa;            /* MUON_NS_GRAM: A, P A and the two Q buffers */
+  void* pa;
+  void* qa;
+  void* qb;
 } muon_ns_class;
 
 typedef struct muon_ns_plan muon_ns_plan;
@@ -209,17 +234,26 @@ typedef struct muon_ns_plan muon_ns_plan;
 int muon_ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, int steps,
                         muon_ns_plan** plan_out);
 
-/* Run the plan: 3 grouped GEMM launches per iteration. `err_dev` is a device
- * int (0 before the call). */
+/* Run the plan: 3 grouped GEMM launches per iteration, plus one per 3
+ * iterations when a class uses MUON_NS_GRAM. `err_dev` is a device int (0
+ * before the call). */
 int muon_ns_plan_run(const muon_ns_plan* plan, int* err_dev, void* stream);
 
 void muon_ns_plan_destroy(muon_ns_plan* plan);
 
-/* Bytes of one class's workspace when x0, x1, ap, bp and mm are carved from a
- * single buffer with muon_ns_class_layout (each part 256-byte aligned). */
-int64_t muon_ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype);
+/* Kernel launches one muon_ns_plan_run issues (-1 for a null plan). */
+int muon_ns_plan_launches(const muon_ns_plan* plan);
 
-/* Fill x0/x1/ap/bp/mm/ld_x/ld_m of `cls` from one workspace buffer `base` of
+/* Bytes of one class's workspace when its buffers are carved from a single
+ * buffer with muon_ns_class_layout (each part 256-byte aligned). */
+int64_t muon_ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype, int algo);
+
+/* The algorithm with fewer executed FLOPs for a rows x cols class iterated
+ * `steps` times (MUON_NS_STANDARD for MUON_BF16 operands or steps < 3). */
+int muon_ns_choose_algo(int32_t rows, int32_t cols, int op_dtype, int steps);
+
+/* Fill the buffer pointers and ld_x/ld_m of `cls` (rows, cols, count and
+ * algo set by the caller) from one workspace buffer `base` of
  * muon_ns_class_workspace_bytes() bytes. */
 int muon_ns_class_layout(muon_ns_class* cls, void* base, int op_dtype);
 

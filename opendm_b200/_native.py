@@ -25,8 +25,10 @@ MUON_BF16 = 0
 MUON_F32 = 1
 MUON_TF32 = 2
 MUON_F16 = 3
+MUON_NS_STANDARD = 0
+MUON_NS_GRAM = 1
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 
 class MomentumSeg(Structure):
@@ -71,6 +73,12 @@ class NsClass(Structure):
         ("scales", c_void_p),
         ("u_out", c_void_p),
         ("ld_u", c_int64),
+        ("algo", c_int32),
+        ("reserved", c_int32),
+        ("aa", c_void_p),
+        ("pa", c_void_p),
+        ("qa", c_void_p),
+        ("qb", c_void_p),
     ]
 
 
@@ -120,7 +128,9 @@ SIGNATURES = {
     "muon_ns_plan_run": (c_int, [c_void_p, c_void_p, c_void_p]),
     "muon_apply_update": (c_int, [c_void_p, c_int, c_int64, c_float, c_void_p]),
     "muon_ns_plan_destroy": (None, [c_void_p]),
-    "muon_ns_class_workspace_bytes": (c_int64, [c_int32, c_int32, c_int32, c_int]),
+    "muon_ns_plan_launches": (c_int, [c_void_p]),
+    "muon_ns_class_workspace_bytes": (c_int64, [c_int32, c_int32, c_int32, c_int, c_int]),
+    "muon_ns_choose_algo": (c_int, [c_int32, c_int32, c_int, c_int]),
     "muon_ns_class_layout": (c_int, [POINTER(NsClass), c_void_p, c_int]),
     "muon_adamw_chunks": (c_int64, [c_int64]),
     "muon_adamw": (c_int, [c_void_p, c_int, c_int64, c_double, c_double, c_float, c_float, c_void_p]),

@@ -131,8 +131,14 @@ int muon_apply_update(const muon_update_seg* segs_dev, int n_segs, int64_t total
 
 void muon_ns_plan_destroy(muon_ns_plan* plan) { muon::ns_plan_destroy(plan); }
 
-int64_t muon_ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype) {
-  return muon::ns_class_workspace_bytes(rows, cols, count, op_dtype);
+int muon_ns_plan_launches(const muon_ns_plan* plan) { return muon::ns_plan_launches(plan); }
+
+int64_t muon_ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype, int algo) {
+  return muon::ns_class_workspace_bytes(rows, cols, count, op_dtype, algo);
+}
+
+int muon_ns_choose_algo(int32_t rows, int32_t cols, int op_dtype, int steps) {
+  return muon::ns_choose_algo(rows, cols, op_dtype, steps);
 }
 
 int muon_ns_class_layout(muon_ns_class* cls, void* base, int op_dtype) {

@@ -32,7 +32,9 @@ int ns_plan_run(const muon_ns_plan* plan, int* err_dev, cudaStream_t stream);
 int launch_apply_update(const muon_update_seg* segs_dev, int n_segs, int64_t total_chunks, float wd_factor,
                         cudaStream_t stream);
 void ns_plan_destroy(muon_ns_plan* plan);
-int64_t ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype);
+int ns_plan_launches(const muon_ns_plan* plan);
+int64_t ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype, int algo);
+int ns_choose_algo(int32_t rows, int32_t cols, int op_dtype, int steps);
 int ns_class_layout(muon_ns_class* cls, void* base, int op_dtype);
 float ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dtype);
 

@@ -55,7 +55,7 @@ constexpr int EPI_BYTES = EPI_WARPS * EPI_WARP_BYTES;
 constexpr int BAR_BYTES = 256;
 constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
 constexpr int TMEM_COLS = 2 * BN;
-constexpr int kMaxProblems = 16;
+constexpr int kMaxProblems = 32;  // up to two problems per class per launch
 
 enum EpiKind : int { EPI_GRAM = 0, EPI_POLY = 1, EPI_APPLY = 2, EPI_U_F32 = 3, EPI_U_BF16 = 4 };
 
@@ -74,9 +74,12 @@ struct GemmProblem {
   int epi;
   int first;       // apply the per-matrix input scale
   float mul;       // constant multiplier of the accumulator (power of two)
+  float omul;      // poly: multiplier of the stored M / P (power of two)
+  float omul3;     // gram: of the stored A; poly: of the stored Q (power of two)
   void* out;
   long long out_ld, out_bs;
   void* out2;      // gram: B' (same geometry as out)
+  void* out3;      // optional (gram: A; poly: Q), same geometry as out
   const float* scale;
 };
 
@@ -84,13 +87,17 @@ struct GemmParams {
   CUtensorMap map_a[kMaxProblems];
   CUtensorMap map_b[kMaxProblems];
   CUtensorMap map_out[kMaxProblems];   // D (A', M, X or U): 32 x 32 store boxes
-  CUtensorMap map_out2[kMaxProblems];  // gram: B' 
+  CUtensorMap map_out2[kMaxProblems];  // gram: B'
+  CUtensorMap map_out3[kMaxProblems];  // gram: A; poly: Q (only where out3 is set)
   GemmProblem prob[kMaxProblems];
   int n_problems;
   int total_tiles;
   float alpha, beta, gamma;
   int* err;
 };
+
+// The whole launch descriptor is one __grid_constant__ kernel parameter.
+static_assert(sizeof(GemmParams) <= 32764, "GemmParams exceeds the kernel parameter limit");
 
 struct TileCoord {
   int p, g, ti, tj;
@@ -468,6 +475,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const int myrow = row0 + lane;
       const CUtensorMap* map1 = &P.map_out[tc.p];
       const CUtensorMap* map2 = &P.map_out2[tc.p];
+      const CUtensorMap* map3 = &P.map_out3[tc.p];
+      const bool has3 = pr.out3 != nullptr;
 
       for (int ch = 0; ch < BN / 32; ++ch) {
         const int col0 = tc.tj * BN + ch * 32;
@@ -480,12 +489,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         const bool mirror = sym && col0 >= row0 + 32;
         float x[32];
         if (pr.epi == EPI_GRAM) {
+          uint32_t w[kOpWords];
+          if (has3) {  // A itself, scaled for storage
+            const float m3 = pr.omul3;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) x[i] = zero ? 0.f : (v[i] * f) * m3;
+            pack_row<kOpWords>(x, kOpKind, w);
+            store_chunk<kOpWords>(ring, map3, lane, w, col0, row0, tc.g, mirror);
+          }
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const float a = zero ? 0.f : v[i] * f;
             x[i] = (myrow == col0 + i) ? a - 1.f : a;  // A'
           }
-          uint32_t w[kOpWords];
           pack_row<kOpWords>(x, kOpKind, w);
           store_chunk<kOpWords>(ring, map1, lane, w, col0, row0, tc.g, mirror);
 #pragma unroll
@@ -493,9 +509,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           pack_row<kOpWords>(x, kOpKind, w);
           store_chunk<kOpWords>(ring, map2, lane, w, col0, row0, tc.g, mirror);
         } else if (pr.epi == EPI_POLY) {
+          const float pm = pr.mul, om = pr.omul;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) x[i] = (myrow == col0 + i) ? v[i] + P.alpha : v[i];
+          for (int i = 0; i < 32; ++i) x[i] = (myrow == col0 + i) ? fmaf(v[i], pm, P.alpha) : v[i] * pm;
           uint32_t w[kOpWords];
+          if (has3) {  // the same polynomial, stored a second time at another scale
+            float y[32];
+            const float m3 = pr.omul3;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) y[i] = x[i] * m3;
+            pack_row<kOpWords>(y, kOpKind, w);
+            store_chunk<kOpWords>(ring, map3, lane, w, col0, row0, tc.g, mirror);
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) x[i] *= om;
           pack_row<kOpWords>(x, kOpKind, w);
           store_chunk<kOpWords>(ring, map1, lane, w, col0, row0, tc.g, mirror);
         } else {
@@ -504,7 +531,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           if (pr.epi == EPI_APPLY) {
             uint32_t w[kOpWords];
             pack_row<kOpWords>(x, kOpKind, w);
-            store_chunk<kOpWords>(ring, map1, lane, w, col0, row0, tc.g, false);
+            store_chunk<kOpWords>(ring, map1, lane, w, col0, row0, tc.g, mirror);
           } else if (pr.epi == EPI_U_BF16) {
             uint32_t w[16];
             pack_row<16>(x, 3, w);
@@ -597,7 +624,7 @@ struct muon_ns_plan {
   int steps;
   int n_classes;
   int num_sms;
-  std::vector<muon::GemmParams> launches;  // 3 * steps
+  std::vector<muon::GemmParams> launches;  // non-empty launch slots, in order
 };
 
 namespace muon {
@@ -654,22 +681,79 @@ static int encode_output(CUtensorMap* map, const void* base, int dtype, long lon
   return MUON_OK;
 }
 
-int64_t ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype) {
+// ------------------------------------------------------------ algorithms
+// MUON_NS_STANDARD runs every iteration on X (gram, poly, apply: 3 launches
+// per iteration). MUON_NS_GRAM runs the iteration on the m x m gram matrix
+// instead, for matrices with n noticeably larger than m:
+//   X_k = P_{k-1} ... P_0 X_0 with P_j = a + b A_j + c A_j^2 (a polynomial of
+//   A_j) and A_{j+1} = P_j A_j P_j = P_j (P_j A_j), since P_j and A_j commute.
+// The product Q = P_j ... P_s is accumulated in m x m and applied to X only
+// at the end of a segment of kGramSegment iterations, after which the gram
+// matrix is recomputed from the new X (a restart: without it, rounding in the
+// m x m products grows in the directions of small singular values). Per
+// segment of L iterations: one gram (m^2 n), 4L - 3 symmetric m x m products
+// and one apply (2 m^2 n), against L (3 m^2 n + m^3) for the standard form.
+// Each launch slot of an iteration still holds three dependent phases, so
+// both algorithms share launches; a segment end adds one apply launch.
+constexpr int kGramSegment = 3;
+constexpr int kGramMaxM = 32768;  // keeps the scaled fp16 values of A, P and Q finite
+
+static double p2_near(double x) { return std::ldexp(1.0, static_cast<int>(std::lround(std::log2(x)))); }
+
+// fp16 storage scales of the gram-form m x m matrices (1 for tf32): A, P, PA
+// have eigenvalues below 3.5 and are stored times m/4; Q (a product of up to
+// three P) below 41, stored times m/64.
+static float gram_scale_a(int m, int op) { return op == MUON_F16 ? float(p2_near(m / 4.0)) : 1.0f; }
+static float gram_scale_q(int m, int op) { return op == MUON_F16 ? float(p2_near(m / 64.0)) : 1.0f; }
+
+static double exec_flops(int rows, int cols, int steps, int algo) {
+  const double m = std::min(rows, cols), n = std::max(rows, cols);
+  auto kp = [](double k) { return std::ceil(k / 64.0) * 64.0; };
+  const double t = std::ceil(m / 256.0);
+  const double tile = 256.0 * 256.0 * 2.0;
+  const double gram = t * (t + 1) / 2 * tile * kp(n);
+  const double sq = t * (t + 1) / 2 * tile * kp(m);
+  const double app = std::ceil(rows / 256.0) * std::ceil(cols / 256.0) * tile * kp(m);
+  if (algo == MUON_NS_STANDARD) return steps * (gram + sq + app);
+  double f = 0;
+  for (int s0 = 0; s0 < steps; s0 += kGramSegment) {
+    const int len = std::min(kGramSegment, steps - s0);
+    f += gram + (4 * len - 3) * sq + app;
+  }
+  return f;
+}
+
+int ns_choose_algo(int32_t rows, int32_t cols, int op_dtype, int steps) {
+  if (op_dtype != MUON_F16 && op_dtype != MUON_TF32) return MUON_NS_STANDARD;
+  if (rows <= 0 || cols <= 0 || steps < kGramSegment) return MUON_NS_STANDARD;
+  if (std::min(rows, cols) > kGramMaxM) return MUON_NS_STANDARD;
+  return exec_flops(rows, cols, steps, MUON_NS_GRAM) < 0.9 * exec_flops(rows, cols, steps, MUON_NS_STANDARD)
+             ? MUON_NS_GRAM
+             : MUON_NS_STANDARD;
+}
+
+int64_t ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype, int algo) {
   if (rows <= 0 || cols <= 0 || count <= 0) return 0;
   if (op_dtype != MUON_TF32 && op_dtype != MUON_BF16 && op_dtype != MUON_F16) return 0;
+  if (algo != MUON_NS_STANDARD && algo != MUON_NS_GRAM) return 0;
   const int es = op_bytes(op_dtype);
   const int align_el = 16 / es;
   const int64_t m = std::min(rows, cols);
   const int64_t ld_x = (cols + align_el - 1) / align_el * align_el;
   const int64_t ld_m = (m + align_el - 1) / align_el * align_el;
   auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
-  return 2 * up(int64_t(count) * rows * ld_x * es) + 3 * up(int64_t(count) * m * ld_m * es);
+  const int n_mm = algo == MUON_NS_GRAM ? 7 : 3;
+  return 2 * up(int64_t(count) * rows * ld_x * es) + n_mm * up(int64_t(count) * m * ld_m * es);
 }
 
 int ns_class_layout(muon_ns_class* cls, void* base, int op_dtype) {
   if (!cls || !base) return set_error(MUON_ERR_ARG, "null class or workspace");
   if ((reinterpret_cast<uintptr_t>(base) & 255u) != 0)
     return set_error(MUON_ERR_ARG, "NS workspace must be 256-byte aligned");
+  if (op_dtype != MUON_TF32 && op_dtype != MUON_BF16 && op_dtype != MUON_F16)
+    return set_error(MUON_ERR_ARG, "op_dtype must be MUON_TF32, MUON_BF16 or MUON_F16");
+  if (cls->algo != MUON_NS_STANDARD && cls->algo != MUON_NS_GRAM)
+    return set_error(MUON_ERR_ARG, "algo must be MUON_NS_STANDARD or MUON_NS_GRAM");
   const int es = op_bytes(op_dtype);
   const int align_el = 16 / es;
   const int64_t rows = cls->rows, cols = cls->cols, count = cls->count;
@@ -685,8 +769,152 @@ int ns_class_layout(muon_ns_class* cls, void* base, int op_dtype) {
   cls->ap = p + 2 * xb;
   cls->bp = p + 2 * xb + mb;
   cls->mm = p + 2 * xb + 2 * mb;
+  if (cls->algo == MUON_NS_GRAM) {
+    cls->aa = p + 2 * xb + 3 * mb;
+    cls->pa = p + 2 * xb + 4 * mb;
+    cls->qa = p + 2 * xb + 5 * mb;
+    cls->qb = p + 2 * xb + 6 * mb;
+  } else {
+    cls->aa = cls->pa = cls->qa = cls->qb = nullptr;
+  }
   return MUON_OK;
 }
+
+namespace {
+
+struct OpDesc {
+  const void* base = nullptr;
+  long long inner = 0, outer = 0, ld = 0, bs = 0;
+  int box = 0;
+  bool mn = false;
+};
+
+struct OutDesc {
+  const void* base = nullptr;
+  int dtype = 0;
+  long long inner = 0, outer = 0, ld = 0, bs = 0;
+};
+
+// One GEMM problem of a launch before its tensor maps are encoded.
+struct Pending {
+  GemmProblem pr;
+  OpDesc a, b;
+  OutDesc o1, o2, o3;
+  double work = 0;
+};
+
+struct ClassGeom {
+  const muon_ns_class* k;
+  int op, es, m, n;
+  bool wide;
+  long long xbs, mbs;
+
+  OpDesc mat(const void* buf, int box) const { return OpDesc{buf, m, m, k->ld_m, mbs, box, false}; }
+  OutDesc mat_out(const void* buf) const { return OutDesc{buf, op, m, m, k->ld_m, mbs}; }
+  OutDesc x_out(const void* buf) const { return OutDesc{buf, op, k->cols, k->rows, k->ld_x, xbs}; }
+  OutDesc u_out() const {
+    return OutDesc{k->u_out, k->u_dtype, k->cols, k->rows, k->ld_u, static_cast<long long>(k->rows) * k->ld_u};
+  }
+
+  Pending base(int M, int N, int K, int sym, int epi) const {
+    Pending p;
+    memset(&p.pr, 0, sizeof(p.pr));
+    p.pr.M = M;
+    p.pr.N = N;
+    p.pr.K = K;
+    p.pr.batch = k->count;
+    p.pr.symmetric = sym;
+    p.pr.epi = epi;
+    p.pr.mul = 1.0f;
+    p.pr.omul = 1.0f;
+    p.pr.omul3 = 1.0f;
+    p.pr.scale = k->scales;
+    p.work = double(M) * N * K * k->count;
+    return p;
+  }
+
+  // A' = f X X^T - I and B' (and A * a_scale when `a_out`), K = n.
+  Pending gram_x(const void* xin, bool first, float mul, void* a_out, float a_scale) const {
+    Pending p = base(m, m, n, 1, EPI_GRAM);
+    p.pr.first = first;
+    p.pr.mul = mul;
+    p.pr.a_mn = p.pr.b_mn = wide ? 0 : 1;
+    if (wide) {
+      p.a = OpDesc{xin, k->cols, k->rows, k->ld_x, xbs, BM, false};
+      p.b = OpDesc{xin, k->cols, k->rows, k->ld_x, xbs, BN_CTA, false};
+    } else {
+      p.a = OpDesc{xin, k->cols, k->rows, k->ld_x, xbs, 128 / es, true};
+      p.b = OpDesc{xin, k->cols, k->rows, k->ld_x, xbs, 128 / es, true};
+    }
+    p.o1 = mat_out(k->ap);
+    p.o2 = mat_out(k->bp);
+    if (a_out) {
+      p.o3 = mat_out(a_out);
+      p.pr.omul3 = a_scale;
+    }
+    return p;
+  }
+
+  // Symmetric product of two symmetric m x m operands (both K-major) into
+  // the m x m buffer `out`.
+  Pending sym(const void* lhs, const void* rhs, int epi, float mul, const void* out) const {
+    Pending p = base(m, m, m, 1, epi);
+    p.pr.mul = mul;
+    p.a = mat(lhs, BM);
+    p.b = mat(rhs, BN_CTA);
+    p.o1 = mat_out(out);
+    return p;
+  }
+
+  // X' = M X (wide) or X M (tall) with M symmetric m x m; writes X' (op
+  // dtype) or, when `xout` is null, U.
+  Pending apply(const void* mbuf, const void* xin, bool first, float mul, const void* xout) const {
+    Pending p = base(k->rows, k->cols, m, 0, xout ? EPI_APPLY : (k->u_dtype == MUON_BF16 ? EPI_U_BF16 : EPI_U_F32));
+    p.pr.first = first;
+    p.pr.mul = mul;
+    if (wide) {
+      p.pr.a_mn = 0;
+      p.pr.b_mn = 1;
+      p.a = mat(mbuf, BM);
+      p.b = OpDesc{xin, k->cols, k->rows, k->ld_x, xbs, 128 / es, true};
+    } else {
+      p.pr.a_mn = 0;
+      p.pr.b_mn = 0;
+      p.a = OpDesc{xin, k->cols, k->rows, k->ld_x, xbs, BM, false};
+      p.b = mat(mbuf, BN_CTA);
+    }
+    p.o1 = xout ? x_out(xout) : u_out();
+    return p;
+  }
+};
+
+int encode_pending(GemmParams& L, int pi, const Pending& q, int op) {
+  int rc = encode_operand(&L.map_a[pi], q.a.base, op, q.a.inner, q.a.outer, q.pr.batch, q.a.ld, q.a.bs, q.a.box,
+                          q.a.mn);
+  if (!rc)
+    rc = encode_operand(&L.map_b[pi], q.b.base, op, q.b.inner, q.b.outer, q.pr.batch, q.b.ld, q.b.bs, q.b.box,
+                        q.b.mn);
+  if (!rc)
+    rc = encode_output(&L.map_out[pi], q.o1.base, q.o1.dtype, q.o1.inner, q.o1.outer, q.pr.batch, q.o1.ld,
+                       q.o1.bs);
+  if (!rc && q.o2.base)
+    rc = encode_output(&L.map_out2[pi], q.o2.base, q.o2.dtype, q.o2.inner, q.o2.outer, q.pr.batch, q.o2.ld,
+                       q.o2.bs);
+  if (!rc && q.o3.base)
+    rc = encode_output(&L.map_out3[pi], q.o3.base, q.o3.dtype, q.o3.inner, q.o3.outer, q.pr.batch, q.o3.ld,
+                       q.o3.bs);
+  if (rc) return rc;
+  GemmProblem& pr = L.prob[pi];
+  pr = q.pr;
+  pr.out = const_cast<void*>(q.o1.base);
+  pr.out_ld = q.o1.ld;
+  pr.out_bs = q.o1.bs;
+  pr.out2 = const_cast<void*>(q.o2.base);
+  pr.out3 = const_cast<void*>(q.o3.base);
+  return MUON_OK;
+}
+
+}  // namespace
 
 int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, int steps,
                    muon_ns_plan** plan_out) {
@@ -695,9 +923,9 @@ int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, in
   if (op_dtype != MUON_TF32 && op_dtype != MUON_BF16 && op_dtype != MUON_F16)
     return set_error(MUON_ERR_ARG, "op_dtype must be MUON_TF32, MUON_BF16 or MUON_F16");
   if (steps < 1) return set_error(MUON_ERR_UNSUPPORTED, "Newton-Schulz plans need steps >= 1");
-  if (n_classes < 1 || n_classes > kMaxProblems)
+  if (n_classes < 1 || n_classes > kMaxProblems / 2)
     return set_error(MUON_ERR_ARG, "n_classes must be in [1, 16]");
-  const int es = op_bytes(op_dtype);
+  bool any_gram = false;
   for (int c = 0; c < n_classes; ++c) {
     const muon_ns_class& k = classes[c];
     if (k.rows <= 0 || k.cols <= 0 || k.count <= 0)
@@ -709,162 +937,137 @@ int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, in
     const int m = std::min(k.rows, k.cols);
     if (k.ld_x < k.cols || k.ld_m < m) return set_error(MUON_ERR_ARG, "leading dimension too small");
     if (k.ld_u < k.cols) return set_error(MUON_ERR_ARG, "ld_u too small");
+    if (k.algo == MUON_NS_GRAM) {
+      if (op_dtype == MUON_BF16) return set_error(MUON_ERR_UNSUPPORTED, "MUON_NS_GRAM needs MUON_F16 or MUON_TF32");
+      if (m > kGramMaxM) return set_error(MUON_ERR_UNSUPPORTED, "MUON_NS_GRAM supports min(rows, cols) <= 32768");
+      if (!k.aa || !k.pa || !k.qa || !k.qb) return set_error(MUON_ERR_ARG, "gram class buffer pointer is null");
+      any_gram = true;
+    } else if (k.algo != MUON_NS_STANDARD) {
+      return set_error(MUON_ERR_ARG, "algo must be MUON_NS_STANDARD or MUON_NS_GRAM");
+    }
   }
   int dev = 0, sms = 0;
   if (check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return MUON_ERR_CUDA;
   if (check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "SM count"))
     return MUON_ERR_CUDA;
 
+  const bool f16 = op_dtype == MUON_F16;
+  const int es = op_bytes(op_dtype);
+
+  // Launch slots: three phases per iteration, plus one apply slot at the end
+  // of each gram segment when a class uses the gram form.
+  std::vector<int> slot_of(3 * steps), ex_slot(steps, -1);
+  int n_slots = 0;
+  for (int it = 0; it < steps; ++it) {
+    for (int ph = 0; ph < 3; ++ph) slot_of[3 * it + ph] = n_slots++;
+    if (any_gram && (it % kGramSegment == kGramSegment - 1 || it == steps - 1)) ex_slot[it] = n_slots++;
+  }
+  std::vector<std::vector<Pending>> slots(n_slots);
+
+  for (int c = 0; c < n_classes; ++c) {
+    const muon_ns_class& k = classes[c];
+    ClassGeom G{&k, op_dtype, es, std::min(k.rows, k.cols), std::max(k.rows, k.cols), k.rows <= k.cols,
+                static_cast<long long>(k.rows) * k.ld_x, static_cast<long long>(std::min(k.rows, k.cols)) * k.ld_m};
+    auto xscale = [&](int it) { return ns_operand_scale(k.rows, k.cols, it, op_dtype); };
+    if (k.algo == MUON_NS_STANDARD) {
+      for (int it = 0; it < steps; ++it) {
+        const void* xin = (it % 2 == 0) ? k.x0 : k.x1;
+        const void* xout = (it % 2 == 0) ? k.x1 : k.x0;
+        const bool last = it == steps - 1;
+        // fp16: X is stored pre-normalised and scaled by S_it, so A = acc / S_it^2.
+        const float S = xscale(it);
+        slots[slot_of[3 * it]].push_back(G.gram_x(xin, !f16 && it == 0, 1.0f / (S * S), nullptr, 1.0f));
+        slots[slot_of[3 * it + 1]].push_back(G.sym(k.ap, k.bp, EPI_POLY, 1.0f, k.mm));
+        // acc = M (S_it X): rescale to S_{it+1} X' for the next iteration, or to X' itself.
+        const float Sn = last ? 1.0f : xscale(it + 1);
+        slots[slot_of[3 * it + 2]].push_back(G.apply(k.mm, xin, !f16 && it == 0, Sn / S, last ? nullptr : xout));
+      }
+      continue;
+    }
+    const float SA = gram_scale_a(G.m, op_dtype), SQ = gram_scale_q(G.m, op_dtype);
+    for (int s0 = 0; s0 < steps; s0 += kGramSegment) {
+      const int s1 = std::min(s0 + kGramSegment, steps);
+      const int seg = s0 / kGramSegment;
+      const void* xseg = (seg % 2 == 0) ? k.x0 : k.x1;
+      const void* xnext = (seg % 2 == 0) ? k.x1 : k.x0;
+      const float S = xscale(s0);
+      auto qbuf = [&](int j) { return ((j - s0) % 2 == 0) ? k.qa : k.qb; };
+      for (int it = s0; it < s1; ++it) {
+        // phase 0: A' and B' of A_it, and A_it * SA
+        if (it == s0)
+          slots[slot_of[3 * it]].push_back(G.gram_x(xseg, !f16 && it == 0, 1.0f / (S * S), k.aa, SA));
+        else  // A_it = P_{it-1} (P_{it-1} A_{it-1}), operands stored times SA
+          slots[slot_of[3 * it]].push_back([&] {
+            Pending p = G.sym(k.mm, k.pa, EPI_GRAM, 1.0f / (SA * SA), k.ap);
+            p.o2 = G.mat_out(k.bp);
+            p.o3 = G.mat_out(k.aa);
+            p.pr.omul3 = SA;
+            return p;
+          }());
+        // phase 1: P_it = alpha I + A' B', stored times SA (and as Q times SQ
+        // at the start of a segment)
+        {
+          Pending p = G.sym(k.ap, k.bp, EPI_POLY, 1.0f, k.mm);
+          p.pr.omul = SA;
+          if (it == s0) {
+            p.o3 = G.mat_out(qbuf(it));
+            p.pr.omul3 = SQ;
+          }
+          slots[slot_of[3 * it + 1]].push_back(p);
+        }
+        // phase 2: P A (for the next A) and Q_it = P_it Q_{it-1}
+        if (it < s1 - 1) {
+          Pending p = G.sym(k.mm, k.aa, EPI_APPLY, 1.0f / SA, k.pa);
+          slots[slot_of[3 * it + 2]].push_back(p);
+        }
+        if (it > s0) {
+          Pending p = G.sym(k.mm, qbuf(it - 1), EPI_APPLY, 1.0f / SA, qbuf(it));
+          slots[slot_of[3 * it + 2]].push_back(p);
+        }
+      }
+      // segment end: X_{s1} = Q X_{s0} (or U)
+      const bool last = s1 == steps;
+      const float Sn = last ? 1.0f : xscale(s1);
+      slots[ex_slot[s1 - 1]].push_back(G.apply(qbuf(s1 - 1), xseg, !f16 && s0 == 0, Sn / (SQ * S),
+                                               last ? nullptr : xnext));
+    }
+  }
+
   muon_ns_plan* plan = new muon_ns_plan();
   plan->op_dtype = op_dtype;
   plan->steps = steps;
   plan->n_classes = n_classes;
   plan->num_sms = sms;
-  plan->launches.resize(3 * steps);
-
-  const bool f16 = op_dtype == MUON_F16;
   const float alpha = float(kNsA + kNsB + kNsC);
   const float beta = float(kNsB + 2.0 * kNsC);
   const float gamma = float(kNsC);
-
-  for (int it = 0; it < steps; ++it) {
-    for (int phase = 0; phase < 3; ++phase) {
-      GemmParams& L = plan->launches[3 * it + phase];
-      memset(&L, 0, sizeof(L));
-      L.alpha = alpha;
-      L.beta = beta;
-      L.gamma = gamma;
-      // Order problems by K (largest first) so long tiles start early.
-      std::vector<int> order(n_classes);
-      for (int c = 0; c < n_classes; ++c) order[c] = c;
-      auto kdim = [&](int c) {
-        const muon_ns_class& k = classes[c];
-        const int m = std::min(k.rows, k.cols), n = std::max(k.rows, k.cols);
-        return phase == 0 ? n : m;
-      };
-      auto work = [&](int c) {
-        const muon_ns_class& k = classes[c];
-        const double m = std::min(k.rows, k.cols), n = std::max(k.rows, k.cols);
-        return double(kdim(c)) * (phase == 2 ? m * n : m * m) * k.count;
-      };
-      std::stable_sort(order.begin(), order.end(), [&](int x, int y) {
-        if (kdim(x) != kdim(y)) return kdim(x) > kdim(y);
-        return work(x) > work(y);
-      });
-      int tile_begin = 0;
-      for (int pi = 0; pi < n_classes; ++pi) {
-        const int c = order[pi];
-        const muon_ns_class& k = classes[c];
-        GemmProblem& pr = L.prob[pi];
-        const bool wide = k.rows <= k.cols;
-        const int m = std::min(k.rows, k.cols), n = std::max(k.rows, k.cols);
-        void* xin = (it % 2 == 0) ? k.x0 : k.x1;
-        void* xout = (it % 2 == 0) ? k.x1 : k.x0;
-        const long long xbs = static_cast<long long>(k.rows) * k.ld_x;
-        const long long mbs = static_cast<long long>(m) * k.ld_m;
-        int rc = MUON_OK;
-        pr.batch = k.count;
-        pr.scale = k.scales;
-        if (phase == 0) {
-          // A' = s^2 X X^T - I over the wide orientation.
-          pr.M = m;
-          pr.N = m;
-          pr.K = n;
-          pr.symmetric = 1;
-          pr.epi = EPI_GRAM;
-          // fp16: X is stored pre-normalised and scaled by S_it, so A = acc / S_it^2.
-          pr.first = f16 ? 0 : it == 0;
-          {
-            const float S = ns_operand_scale(k.rows, k.cols, it, op_dtype);
-            pr.mul = 1.0f / (S * S);
-          }
-          pr.a_mn = pr.b_mn = wide ? 0 : 1;
-          pr.out = k.ap;
-          pr.out2 = k.bp;
-          pr.out_ld = k.ld_m;
-          pr.out_bs = mbs;
-          if (wide) {
-            rc = encode_operand(&L.map_a[pi], xin, op_dtype, k.cols, k.rows, k.count, k.ld_x, xbs, BM);
-            if (!rc) rc = encode_operand(&L.map_b[pi], xin, op_dtype, k.cols, k.rows, k.count, k.ld_x, xbs, BN_CTA);
-          } else {
-            rc = encode_operand(&L.map_a[pi], xin, op_dtype, k.cols, k.rows, k.count, k.ld_x, xbs, 128 / es, true);
-            if (!rc) rc = encode_operand(&L.map_b[pi], xin, op_dtype, k.cols, k.rows, k.count, k.ld_x, xbs, 128 / es, true);
-          }
-        } else if (phase == 1) {
-          // M = alpha I + A' B' (A', B' symmetric: both operands K-major).
-          pr.M = pr.N = pr.K = m;
-          pr.symmetric = 1;
-          pr.epi = EPI_POLY;
-          pr.first = 0;
-          pr.mul = 1.0f;
-          pr.a_mn = pr.b_mn = 0;
-          pr.out = k.mm;
-          pr.out_ld = k.ld_m;
-          pr.out_bs = mbs;
-          rc = encode_operand(&L.map_a[pi], k.ap, op_dtype, m, m, k.count, k.ld_m, mbs, BM);
-          if (!rc) rc = encode_operand(&L.map_b[pi], k.bp, op_dtype, m, m, k.count, k.ld_m, mbs, BN_CTA);
-        } else {
-          // Wide: X' = M X (B operand MN-major). Tall: X' = X M (both K-major).
-          pr.M = k.rows;
-          pr.N = k.cols;
-          pr.K = m;
-          pr.symmetric = 0;
-          pr.first = f16 ? 0 : it == 0;
-          const bool last = it == steps - 1;
-          {
-            // acc = M (S_it X): rescale to S_{it+1} X' for the next iteration,
-            // or to X' itself for the output.
-            const float S = ns_operand_scale(k.rows, k.cols, it, op_dtype);
-            const float Sn = last ? 1.0f : ns_operand_scale(k.rows, k.cols, it + 1, op_dtype);
-            pr.mul = Sn / S;
-          }
-          if (wide) {
-            pr.a_mn = 0;
-            pr.b_mn = 1;
-            rc = encode_operand(&L.map_a[pi], k.mm, op_dtype, m, m, k.count, k.ld_m, mbs, BM);
-            if (!rc) rc = encode_operand(&L.map_b[pi], xin, op_dtype, k.cols, k.rows, k.count, k.ld_x, xbs, 128 / es, true);
-          } else {
-            pr.a_mn = 0;
-            pr.b_mn = 0;
-            rc = encode_operand(&L.map_a[pi], xin, op_dtype, k.cols, k.rows, k.count, k.ld_x, xbs, BM);
-            if (!rc) rc = encode_operand(&L.map_b[pi], k.mm, op_dtype, m, m, k.count, k.ld_m, mbs, BN_CTA);
-          }
-          if (!last) {
-            pr.epi = EPI_APPLY;
-            pr.out = xout;
-            pr.out_ld = k.ld_x;
-            pr.out_bs = xbs;
-          } else {
-            pr.epi = k.u_dtype == MUON_BF16 ? EPI_U_BF16 : EPI_U_F32;
-            pr.out = k.u_out;
-            pr.out_ld = k.ld_u;
-            pr.out_bs = static_cast<long long>(k.rows) * k.ld_u;
-          }
-        }
-        if (rc == MUON_OK) {
-          if (phase == 0) {
-            rc = encode_output(&L.map_out[pi], k.ap, op_dtype, m, m, k.count, k.ld_m, mbs);
-            if (!rc) rc = encode_output(&L.map_out2[pi], k.bp, op_dtype, m, m, k.count, k.ld_m, mbs);
-          } else if (phase == 1) {
-            rc = encode_output(&L.map_out[pi], k.mm, op_dtype, m, m, k.count, k.ld_m, mbs);
-          } else if (pr.epi == EPI_APPLY) {
-            rc = encode_output(&L.map_out[pi], pr.out, op_dtype, k.cols, k.rows, k.count, k.ld_x, xbs);
-          } else {
-            rc = encode_output(&L.map_out[pi], k.u_out, k.u_dtype, k.cols, k.rows, k.count, k.ld_u,
-                               static_cast<long long>(k.rows) * k.ld_u);
-          }
-        }
-        if (rc != MUON_OK) {
-          delete plan;
-          return rc;
-        }
-        pr.tiles_per_mat = tiles_per_matrix(pr.M, pr.N, pr.symmetric != 0, &pr.tiles_m, &pr.tiles_n);
-        pr.tile_begin = tile_begin;
-        tile_begin += pr.tiles_per_mat * pr.batch;
+  for (auto& list : slots) {
+    if (list.empty()) continue;
+    // Order problems by K (largest first) so long tiles start early.
+    std::stable_sort(list.begin(), list.end(), [](const Pending& x, const Pending& y) {
+      if (x.pr.K != y.pr.K) return x.pr.K > y.pr.K;
+      return x.work > y.work;
+    });
+    plan->launches.emplace_back();
+    GemmParams& L = plan->launches.back();
+    memset(&L, 0, sizeof(L));
+    L.alpha = alpha;
+    L.beta = beta;
+    L.gamma = gamma;
+    int tile_begin = 0;
+    for (size_t pi = 0; pi < list.size(); ++pi) {
+      const int rc = encode_pending(L, static_cast<int>(pi), list[pi], op_dtype);
+      if (rc != MUON_OK) {
+        delete plan;
+        return rc;
       }
-      L.n_problems = n_classes;
-      L.total_tiles = tile_begin;
+      GemmProblem& pr = L.prob[pi];
+      pr.tiles_per_mat = tiles_per_matrix(pr.M, pr.N, pr.symmetric != 0, &pr.tiles_m, &pr.tiles_n);
+      pr.tile_begin = tile_begin;
+      tile_begin += pr.tiles_per_mat * pr.batch;
     }
+    L.n_problems = static_cast<int>(list.size());
+    L.total_tiles = tile_begin;
   }
   *plan_out = plan;
   return MUON_OK;
@@ -920,5 +1123,12 @@ int ns_plan_run(const muon_ns_plan* plan, int* err_dev, cudaStream_t stream) {
 }
 
 void ns_plan_destroy(muon_ns_plan* plan) { delete plan; }
+
+int ns_plan_launches(const muon_ns_plan* plan) {
+  if (!plan) return -1;
+  int n = 0;
+  for (const auto& L : plan->launches) n += L.total_tiles > 0 ? 1 : 0;
+  return n;
+}
 
 }  // namespace muon

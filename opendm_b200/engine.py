@@ -29,6 +29,9 @@ from . import _native as N
 
 _DTYPE_CODE = {torch.bfloat16: N.MUON_BF16, torch.float32: N.MUON_F32}
 PRECISIONS = {"tf32": N.MUON_TF32, "fp16": N.MUON_F16, "bf16": N.MUON_BF16}
+# Newton-Schulz algorithm per shape class: "auto" (the library's choice by
+# executed FLOPs), "standard" (iterate on X) or "gram" (iterate on X X^T).
+NS_ALGOS = ("auto", "standard", "gram")
 _OP_TORCH = {N.MUON_TF32: torch.float32, N.MUON_F16: torch.float16, N.MUON_BF16: torch.bfloat16}
 
 
@@ -77,13 +80,18 @@ class _ClassState:
     """Workspace and buffers of one shape class."""
 
     def __init__(self, rows: int, cols: int, param_dtype: torch.dtype, count: int, op_dtype: int,
-                 device: torch.device):
+                 device: torch.device, steps: int, algo: str = "auto"):
         lib = N.lib()
         self.rows, self.cols, self.count, self.param_dtype = rows, cols, count, param_dtype
-        nbytes = lib.muon_ns_class_workspace_bytes(rows, cols, count, op_dtype)
+        if algo == "auto":
+            code = int(lib.muon_ns_choose_algo(rows, cols, op_dtype, steps))
+        else:
+            code = {"standard": N.MUON_NS_STANDARD, "gram": N.MUON_NS_GRAM}[algo]
+        nbytes = lib.muon_ns_class_workspace_bytes(rows, cols, count, op_dtype, code)
         self.workspace = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
         self.cls = N.NsClass()
         self.cls.rows, self.cls.cols, self.cls.count = rows, cols, count
+        self.cls.algo = code
         N.check(lib.muon_ns_class_layout(byref(self.cls), c_void_p(self.workspace.data_ptr()), op_dtype),
                 "muon_ns_class_layout")
         self.op_dtype = op_dtype
@@ -103,9 +111,12 @@ class _ClassState:
 class CudaMuonEngine:
     """Runs the Muon and AdamW kernels on one CUDA device."""
 
-    def __init__(self, device: torch.device | str | int, precision: str = "fp16"):
+    def __init__(self, device: torch.device | str | int, precision: str = "fp16", ns_algo: str = "auto"):
         if precision not in PRECISIONS:
             raise ValueError(f"precision must be one of {sorted(PRECISIONS)}, got {precision!r}")
+        if ns_algo not in NS_ALGOS:
+            raise ValueError(f"ns_algo must be one of {NS_ALGOS}, got {ns_algo!r}")
+        self.ns_algo = ns_algo
         self.device = torch.device(device) if not isinstance(device, int) else torch.device("cuda", device)
         if self.device.type != "cuda":
             raise RuntimeError("opendm_b200 runs on CUDA (sm_100) devices only; got " + str(self.device))
@@ -123,6 +134,7 @@ class CudaMuonEngine:
         self._err_host = torch.zeros(1, dtype=torch.int32).pin_memory()
         self._err_event = None
         self.kernel_launches = 0  # launches issued by this engine (for benchmarks)
+        self.ns_launches_per_run = 0  # Newton-Schulz launches of the cached plan
         # When a list, (name, start, end) CUDA events are appended around the
         # momentum, Newton-Schulz and AdamW launches (benchmark instrumentation).
         self.profile_events: list | None = None
@@ -161,6 +173,11 @@ class CudaMuonEngine:
             self._err.zero_()
             raise RuntimeError(f"opendm_b200 kernel reported device error 0x{code:x} (bounded wait expired)")
 
+    def _class_algo(self) -> str:
+        if self.ns_algo == "gram" and self.op_dtype == N.MUON_BF16:
+            return "standard"  # the gram form needs 11-bit operands
+        return self.ns_algo
+
     # ------------------------------------------------------------- planning
     def _key(self, items: list[MatrixItem], ns_steps: int):
         return (ns_steps, tuple((it.param.data_ptr(), tuple(it.param.shape), it.param.dtype,
@@ -178,7 +195,7 @@ class CudaMuonEngine:
         self._order = [(0, 0)] * len(items)
         self._seg_order: list[int] = []
         for ci, ((r, c, dt), idxs) in enumerate(groups.items()):
-            cs = _ClassState(r, c, dt, len(idxs), self.op_dtype, self.device)
+            cs = _ClassState(r, c, dt, len(idxs), self.op_dtype, self.device, ns_steps, self._class_algo())
             for slot, i in enumerate(idxs):
                 self._order[i] = (ci, slot)
                 self._seg_order.append(i)
@@ -226,6 +243,7 @@ class CudaMuonEngine:
             N.check(self.lib.muon_ns_plan_create(arr, len(self._classes), self.op_dtype, ns_steps, byref(plan)),
                     "muon_ns_plan_create")
             self._plan = plan
+            self.ns_launches_per_run = int(self.lib.muon_ns_plan_launches(plan))
         self._plan_key = self._key(items, ns_steps)
 
     # --------------------------------------------------------------- launches
@@ -307,7 +325,7 @@ class CudaMuonEngine:
             N.check(self.lib.muon_ns_plan_run(self._plan, c_void_p(self._err.data_ptr()), _stream_handle()),
                     "muon_ns_plan_run")
             self._event_end(ev)
-            self.kernel_launches += 3 * ns_steps
+            self.kernel_launches += self.ns_launches_per_run
             self._record_error_check()
             self._apply_updates(items, weight_decay_factor)
         else:
@@ -404,7 +422,7 @@ class CudaMuonEngine:
         out = out_buf[:, :cols]
         src = matrix if matrix.dtype in (torch.float32, torch.bfloat16) else matrix.float()
         src = src.contiguous()
-        cs = _ClassState(rows, cols, torch.float32, 1, self.op_dtype, self.device)
+        cs = _ClassState(rows, cols, torch.float32, 1, self.op_dtype, self.device, int(steps), self._class_algo())
         scales = torch.zeros(1, dtype=torch.float32, device=self.device)
         exp_avg = torch.zeros((rows, cols), dtype=torch.float32, device=self.device)
         seg = N.MomentumSeg()
@@ -442,9 +460,9 @@ class CudaMuonEngine:
         try:
             N.check(self.lib.muon_ns_plan_run(plan, c_void_p(self._err.data_ptr()), _stream_handle()),
                     "muon_ns_plan_run")
+            self.kernel_launches += int(self.lib.muon_ns_plan_launches(plan))
         finally:
             self.lib.muon_ns_plan_destroy(plan)
-        self.kernel_launches += 3 * int(steps)
         self._record_error_check()
         # Keep the workspace alive until the kernels that use it have run.
         cs.workspace.record_stream(torch.cuda.current_stream())

@@ -40,11 +40,21 @@ def test_host_only_entry_points(lib):
     assert lib.muon_momentum_chunks(2048, 8192) == (2048 * 8192 + 16383) // 16384
     assert lib.muon_momentum_chunks(0, 5) == 0
     assert lib.muon_adamw_chunks(8193) == 2
-    # two x buffers (ld padded to 16 bytes) + three m x m buffers, 256-byte aligned parts
-    assert lib.muon_ns_class_workspace_bytes(3, 5, 2, N.MUON_TF32) == 2 * 256 + 3 * 256
-    assert lib.muon_ns_class_workspace_bytes(256, 2048, 1, N.MUON_BF16) == 2 * 256 * 2048 * 2 + 3 * 256 * 256 * 2
-    assert lib.muon_ns_class_workspace_bytes(256, 2048, 1, N.MUON_F16) == 2 * 256 * 2048 * 2 + 3 * 256 * 256 * 2
-    assert lib.muon_ns_class_workspace_bytes(4, 4, 1, N.MUON_F32) == 0  # not an operand type
+    std, gram = N.MUON_NS_STANDARD, N.MUON_NS_GRAM
+    # two x buffers (ld padded to 16 bytes) + three m x m buffers (seven for
+    # the gram form), 256-byte aligned parts
+    assert lib.muon_ns_class_workspace_bytes(3, 5, 2, N.MUON_TF32, std) == 2 * 256 + 3 * 256
+    assert lib.muon_ns_class_workspace_bytes(256, 2048, 1, N.MUON_BF16, std) == 2 * 256 * 2048 * 2 + 3 * 256 * 256 * 2
+    assert lib.muon_ns_class_workspace_bytes(256, 2048, 1, N.MUON_F16, std) == 2 * 256 * 2048 * 2 + 3 * 256 * 256 * 2
+    assert lib.muon_ns_class_workspace_bytes(256, 2048, 1, N.MUON_F16, gram) == 2 * 256 * 2048 * 2 + 7 * 256 * 256 * 2
+    assert lib.muon_ns_class_workspace_bytes(4, 4, 1, N.MUON_F32, std) == 0  # not an operand type
+    assert lib.muon_ns_class_workspace_bytes(4, 4, 1, N.MUON_F16, 7) == 0  # not an algorithm
+    # algorithm choice: the gram form where it executes >= 10% fewer FLOPs, 11-bit operands, >= 3 steps
+    assert lib.muon_ns_choose_algo(2048, 8192, N.MUON_F16, 5) == gram
+    assert lib.muon_ns_choose_algo(8192, 2048, N.MUON_TF32, 5) == gram
+    assert lib.muon_ns_choose_algo(2048, 2048, N.MUON_F16, 5) == std
+    assert lib.muon_ns_choose_algo(2048, 8192, N.MUON_BF16, 5) == std
+    assert lib.muon_ns_choose_algo(2048, 8192, N.MUON_F16, 2) == std
     # fp16 operand scales: powers of two bringing entries to magnitude ~1
     assert lib.muon_ns_operand_scale(2048, 8192, 0, N.MUON_F16) == 4096.0
     assert lib.muon_ns_operand_scale(2048, 8192, 1, N.MUON_F16) == 128.0
@@ -59,6 +69,19 @@ def test_argument_validation_reports_errors(lib):
     assert "empty" in N.last_error()
     assert lib.muon_ns_plan_create(ctypes.byref(cls), 1, N.MUON_F32, 5, ctypes.byref(plan)) == N.MUON_ERR_ARG
     assert lib.muon_ns_plan_create(ctypes.byref(cls), 1, N.MUON_TF32, 0, ctypes.byref(plan)) == N.MUON_ERR_UNSUPPORTED
+    # a well-formed class (pointers are only checked, never read, before the
+    # device query) asking for the gram form with bf16 operands
+    cls.rows, cls.cols, cls.count, cls.u_dtype = 64, 128, 1, N.MUON_BF16
+    for f in ("x0", "x1", "ap", "bp", "mm", "scales", "u_out", "aa", "pa", "qa", "qb"):
+        setattr(cls, f, 4096)
+    cls.ld_x, cls.ld_m, cls.ld_u = 128, 64, 128
+    cls.algo = N.MUON_NS_GRAM
+    assert lib.muon_ns_plan_create(ctypes.byref(cls), 1, N.MUON_BF16, 5, ctypes.byref(plan)) == N.MUON_ERR_UNSUPPORTED
+    assert "MUON_NS_GRAM" in N.last_error()
+    cls.qb = None
+    assert lib.muon_ns_plan_create(ctypes.byref(cls), 1, N.MUON_F16, 5, ctypes.byref(plan)) == N.MUON_ERR_ARG
+    cls.algo = 5
+    assert lib.muon_ns_plan_create(ctypes.byref(cls), 1, N.MUON_F16, 5, ctypes.byref(plan)) == N.MUON_ERR_ARG
     assert lib.muon_momentum(None, 2, 4, N.MUON_BF16, N.MUON_TF32, 0.9, 1, 1e-7, None, None, None) == N.MUON_ERR_ARG
     assert lib.muon_apply_update(None, 2, 4, 1.0, None) == N.MUON_ERR_ARG
     assert lib.muon_convert_f16(None, 2, 4, None, None) == N.MUON_ERR_ARG

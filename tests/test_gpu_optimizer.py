@@ -14,9 +14,10 @@ elements round to the neighbouring bf16 value, each flip being a whole ulp
 (~0.4%). For bf16 parameters the checks are therefore: the parameter change
 p_new - p_old*(1-lr*wd) within the 1e-2 update bar at every step, the
 parameters within 2e-3 relative after one step (growing as sqrt(steps) over
-several steps, as the flips accumulate), and, after one step, fewer than 1%
-of the elements more than one bf16 ulp (at the parameter's scale) from the
-reference.
+several steps, as the flips accumulate), and, after one step, fewer than 2%
+(3% against the CPU-rounded golden values) of the elements more than one
+bf16 ulp (at the parameter's scale) from the reference: those are near-zero
+parameters, whose ulp is far below the rounding of the update itself.
 """
 
 import copy
@@ -153,7 +154,7 @@ def _run_config(shapes_muon, shapes_adam, dtype, steps, seed=0, precision="fp16"
         if i < n:
             # element-level flips compound over steps; checked for one-step runs only
             _check_params(got, want, before_got[i], before_want[i], 1.0 - 0.02 * 0.01, dtype, i,
-                          max_beyond=1e-2 if steps == 1 else None, step=steps - 1)
+                          max_beyond=2e-2 if steps == 1 else None, step=steps - 1)
         else:
             assert O.rel_frobenius(got, want) < (BF16_PARAM_TOL if dtype == torch.bfloat16 else 1e-5), i
     for i in range(n):
