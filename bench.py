@@ -374,11 +374,14 @@ def run_ours(args):
     per = {}
     for name, s, e in events:
         per.setdefault(name, []).append(s.elapsed_time(e))
-    ns_ms = max_over_ranks(statistics.mean(per.get("ns", [0.0]))) if per.get("ns") else 0.0
-    mom_ms = statistics.mean(per.get("momentum", [0.0])) if per.get("momentum") else 0.0
-    adam_ms = statistics.mean(per.get("adamw", [0.0])) if per.get("adamw") else 0.0
-    upd_ms = statistics.mean(per.get("update", [0.0])) if per.get("update") else 0.0
-    ag_ms = max_over_ranks(statistics.mean(per["allgather"])) if per.get("allgather") else 0.0
+    def per_step(name):  # an event name can occur several times per step (one per wave)
+        return sum(per.get(name, [])) / args.steps
+
+    ns_ms = max_over_ranks(per_step("ns"))
+    mom_ms = per_step("momentum")
+    adam_ms = per_step("adamw")
+    upd_ms = per_step("update")
+    ag_wait_ms = max_over_ranks(per_step("allgather_wait"))
 
     muon_shapes = [s for n, s in spec if is_muon(n, s)]
     total_flops = sum(ns_flops(s) for s in muon_shapes)
@@ -390,16 +393,28 @@ def run_ours(args):
         mine = muon_shapes
     my_flops = sum(ns_flops(s) for s in mine)
     # the algorithm each shape class ran (the engine's classes, as planned)
-    algo_of = {(cs.rows, cs.cols): ("gram" if int(cs.cls.algo) == 1 else "standard") for cs in engine._classes}
+    algo_of = {(cs.rows, cs.cols): ("gram" if int(cs.cls.algo) == 1 else "standard") for cs in engine.classes}
     my_exec = sum(ns_executed_flops(s, algo=algo_of.get(tuple(s), "standard")) for s in mine)
     my_elems = sum(math.prod(s) for s in mine)
-    my_ns_ms = statistics.mean(per["ns"]) if per.get("ns") else 0.0
+    my_ns_ms = per_step("ns")
     ns_tflops = my_flops / (my_ns_ms * 1e-3) / 1e12 if my_ns_ms > 0 else 0.0
     ns_exec_tflops = my_exec / (my_ns_ms * 1e-3) / 1e12 if my_ns_ms > 0 else 0.0
     ns_tflops = -max_over_ranks(-ns_tflops)  # slowest rank
     ns_exec_tflops = -max_over_ranks(-ns_exec_tflops)
     bucket = opt._buckets.get(id(opt.param_groups[1]))
     ag_bytes = bucket.nbytes_received() if bucket is not None else 0
+    ag_ms = 0.0
+    if bucket is not None:
+        # the parameter all-gather alone (same group and CTA limit), once, untimed by the step
+        ag_group = opt._allgather_group(device)
+        sync_all()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for h in bucket.sync(async_op=True, group=ag_group):
+            h.wait()
+        a1.record()
+        sync_all()
+        ag_ms = max_over_ranks(a0.elapsed_time(a1))
     # grad (bf16) + exp_avg read/write + direction write (+ the fp16 convert pass)
     mom_bytes = my_elems * {"tf32": 2 + 4 + 4 + 4, "bf16": 2 + 4 + 4 + 2, "fp16": 2 + 8 + 4 + 4 + 2}[args.precision]
     mom_gbs = mom_bytes / (mom_ms * 1e-3) / 1e9 if mom_ms > 0 else 0.0
@@ -470,8 +485,12 @@ def run_ours(args):
                             "update_gbs": round(my_elems * 6 / (upd_ms * 1e-3) / 1e9, 1) if upd_ms > 0 else 0.0,
                             "adamw_ms": round(adam_ms, 3), "adamw_gbs": round(adam_gbs, 1),
                             "hbm_peak_gbs": peaks["hbm_gbs"]},
-            "collective": ({"allgather_ms": round(ag_ms, 3), "allgather_bytes_received": ag_bytes,
-                            "allgather_gbs": round(ag_bytes / (ag_ms * 1e-3) / 1e9, 1) if ag_ms > 0 else 0.0}
+            "collective": ({"allgather_bytes_received": ag_bytes,
+                            "allgather_alone_ms": round(ag_ms, 3),
+                            "allgather_alone_gbs": round(ag_bytes / (ag_ms * 1e-3) / 1e9, 1) if ag_ms > 0 else 0.0,
+                            "waves": bucket.n_waves if bucket is not None else 1,
+                            "comm_sms": opt.comm_sms,
+                            "exposed_wait_ms": round(ag_wait_ms, 3)}
                            if world > 1 else None),
             "clocks": clocks,
             "cpu_baseline": cpu,

@@ -244,6 +244,12 @@ void muon_ns_plan_destroy(muon_ns_plan* plan);
 /* Kernel launches one muon_ns_plan_run issues (-1 for a null plan). */
 int muon_ns_plan_launches(const muon_ns_plan* plan);
 
+/* Let the plan's launches use at most `sms` SMs (0: all, the default), so a
+ * collective launched on another stream finds SMs free while the plan runs
+ * (each Newton-Schulz CTA takes a whole SM). No counterpart in the
+ * reference, which runs its collectives and GEMMs one after the other. */
+int muon_ns_plan_set_sm_limit(muon_ns_plan* plan, int sms);
+
 /* Bytes of one class's workspace when its buffers are carved from a single
  * buffer with muon_ns_class_layout (each part 256-byte aligned). */
 int64_t muon_ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype, int algo);

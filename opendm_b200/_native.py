@@ -129,6 +129,7 @@ SIGNATURES = {
     "muon_apply_update": (c_int, [c_void_p, c_int, c_int64, c_float, c_void_p]),
     "muon_ns_plan_destroy": (None, [c_void_p]),
     "muon_ns_plan_launches": (c_int, [c_void_p]),
+    "muon_ns_plan_set_sm_limit": (c_int, [c_void_p, c_int]),
     "muon_ns_class_workspace_bytes": (c_int64, [c_int32, c_int32, c_int32, c_int, c_int]),
     "muon_ns_choose_algo": (c_int, [c_int32, c_int32, c_int, c_int]),
     "muon_ns_class_layout": (c_int, [POINTER(NsClass), c_void_p, c_int]),

@@ -133,6 +133,8 @@ void muon_ns_plan_destroy(muon_ns_plan* plan) { muon::ns_plan_destroy(plan); }
 
 int muon_ns_plan_launches(const muon_ns_plan* plan) { return muon::ns_plan_launches(plan); }
 
+int muon_ns_plan_set_sm_limit(muon_ns_plan* plan, int sms) { return muon::ns_plan_set_sm_limit(plan, sms); }
+
 int64_t muon_ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype, int algo) {
   return muon::ns_class_workspace_bytes(rows, cols, count, op_dtype, algo);
 }

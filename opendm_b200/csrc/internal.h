@@ -33,6 +33,7 @@ int launch_apply_update(const muon_update_seg* segs_dev, int n_segs, int64_t tot
                         cudaStream_t stream);
 void ns_plan_destroy(muon_ns_plan* plan);
 int ns_plan_launches(const muon_ns_plan* plan);
+int ns_plan_set_sm_limit(muon_ns_plan* plan, int sms);
 int64_t ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype, int algo);
 int ns_choose_algo(int32_t rows, int32_t cols, int op_dtype, int steps);
 int ns_class_layout(muon_ns_class* cls, void* base, int op_dtype);

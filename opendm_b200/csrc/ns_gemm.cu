@@ -33,6 +33,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <vector>
 
 #include "common.cuh"
@@ -624,6 +625,7 @@ struct muon_ns_plan {
   int steps;
   int n_classes;
   int num_sms;
+  int sm_limit = 0;  // 0: every SM; else at most this many SMs per launch
   std::vector<muon::GemmParams> launches;  // non-empty launch slots, in order
 };
 
@@ -1073,16 +1075,31 @@ int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, in
   return MUON_OK;
 }
 
+int ns_plan_set_sm_limit(muon_ns_plan* plan, int sms) {
+  if (!plan) return set_error(MUON_ERR_ARG, "plan is null");
+  if (sms < 0) return set_error(MUON_ERR_ARG, "sm limit must be >= 0");
+  if (sms != 0 && sms < 2) return set_error(MUON_ERR_ARG, "sm limit must leave at least one CTA pair (2 SMs)");
+  plan->sm_limit = sms;
+  return MUON_OK;
+}
+
 int ns_plan_run(const muon_ns_plan* plan, int* err_dev, cudaStream_t stream) {
   if (!plan) return set_error(MUON_ERR_ARG, "plan is null");
   if (!err_dev) return set_error(MUON_ERR_ARG, "err_dev is null");
-  static bool attr_set[4] = {false, false, false, false};
+  constexpr int kMaxDevices = 64;
+  static std::mutex attr_mu;
+  static int max_clusters[kMaxDevices][4] = {};  // 0: not set up on that device yet
   const int op = plan->op_dtype;
   const void* fn = op == MUON_TF32   ? reinterpret_cast<const void*>(&ns_gemm_kernel<kOpTf32>)
                    : op == MUON_BF16 ? reinterpret_cast<const void*>(&ns_gemm_kernel<kOpBf16>)
                                      : reinterpret_cast<const void*>(&ns_gemm_kernel<kOpF16>);
-  static int max_clusters[4] = {0, 0, 0, 0};
-  if (!attr_set[op]) {
+  int dev = 0;
+  if (check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return MUON_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return set_error(MUON_ERR_UNSUPPORTED, "device ordinal above 63");
+  int clusters = 0;
+  {
+  std::lock_guard<std::mutex> lock(attr_mu);
+  if (max_clusters[dev][op] == 0) {
     if (check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
                    "cudaFuncSetAttribute(ns_gemm)"))
       return MUON_ERR_CUDA;
@@ -1099,18 +1116,20 @@ int ns_plan_run(const muon_ns_plan* plan, int* err_dev, cudaStream_t stream) {
     attr.val.clusterDim.z = 1;
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
-    int clusters = 0;
-    if (check_cuda(cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg), "cudaOccupancyMaxActiveClusters"))
+    int resident = 0;
+    if (check_cuda(cudaOccupancyMaxActiveClusters(&resident, fn, &cfg), "cudaOccupancyMaxActiveClusters"))
       return MUON_ERR_CUDA;
-    max_clusters[op] = std::max(1, std::min(clusters, plan->num_sms / 2));
-    attr_set[op] = true;
+    max_clusters[dev][op] = std::max(1, std::min(resident, plan->num_sms / 2));
   }
+  clusters = max_clusters[dev][op];
+  }
+  if (plan->sm_limit > 0) clusters = std::max(1, std::min(clusters, plan->sm_limit / 2));
   const int n = static_cast<int>(plan->launches.size());
   for (int i = 0; i < n; ++i) {
     GemmParams L = plan->launches[i];
     L.err = err_dev;
     if (L.total_tiles == 0) continue;
-    const int grid = 2 * std::min(L.total_tiles, max_clusters[op]);  // CTA pairs
+    const int grid = 2 * std::min(L.total_tiles, clusters);  // CTA pairs
     if (op == MUON_TF32)
       ns_gemm_kernel<kOpTf32><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(L);
     else if (op == MUON_BF16)

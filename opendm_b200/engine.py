@@ -108,8 +108,29 @@ class _ClassState:
             self.workspace.untyped_storage(), off, (self.rows, self.cols), (ld, 1))
 
 
+class _PlanState:
+    """Everything cached for one set of matrices: shape classes with their
+    workspaces, the segment order, the fp16 staging table and the plan."""
+
+    def __init__(self):
+        self.plan = None
+        self.classes: list[_ClassState] = []
+        self.order: list[tuple[int, int]] = []  # item index -> (class index, slot)
+        self.seg_order: list[int] = []
+        self.scales = None
+        self.staging = None
+        self.staging_off: dict[int, int] = {}
+        self.convert_table = None
+        self.convert_n = 0
+        self.convert_chunks = 0
+        self.ns_launches = 0
+        self.sm_limit = 0
+
+
 class CudaMuonEngine:
     """Runs the Muon and AdamW kernels on one CUDA device."""
+
+    MAX_PLANS = 16  # cached matrix sets (e.g. the waves of a sharded step)
 
     def __init__(self, device: torch.device | str | int, precision: str = "fp16", ns_algo: str = "auto"):
         if precision not in PRECISIONS:
@@ -125,16 +146,15 @@ class CudaMuonEngine:
         self.lib = N.lib()
         idx = self.device.index if self.device.index is not None else torch.cuda.current_device()
         N.check(self.lib.muon_device_check(idx), "muon_device_check")
-        self._plan = None
-        self._plan_key = None
-        self._classes: list[_ClassState] = []
-        self._order: list[tuple[int, int]] = []  # item index -> (class index, slot)
-        self._scales = None
+        self._plans: dict = {}  # matrix-set key -> _PlanState, least recently used first
+        # At most this many SMs per Newton-Schulz launch (0: all), leaving the
+        # rest to a collective that overlaps it.
+        self.sm_limit = 0
         self._err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._err_host = torch.zeros(1, dtype=torch.int32).pin_memory()
         self._err_event = None
         self.kernel_launches = 0  # launches issued by this engine (for benchmarks)
-        self.ns_launches_per_run = 0  # Newton-Schulz launches of the cached plan
+        self.ns_launches_per_run = 0  # Newton-Schulz launches of the last plan run
         # When a list, (name, start, end) CUDA events are appended around the
         # momentum, Newton-Schulz and AdamW launches (benchmark instrumentation).
         self.profile_events: list | None = None
@@ -183,22 +203,38 @@ class CudaMuonEngine:
         return (ns_steps, tuple((it.param.data_ptr(), tuple(it.param.shape), it.param.dtype,
                                  it.exp_avg.data_ptr()) for it in items))
 
-    def _build(self, items: list[MatrixItem], ns_steps: int) -> None:
-        if self._plan is not None:
-            self.lib.muon_ns_plan_destroy(self._plan)
-            self._plan = None
+    @property
+    def classes(self) -> list[_ClassState]:
+        """Shape classes of every cached plan."""
+        return [cs for st in self._plans.values() for cs in st.classes]
+
+    def _state_for(self, items: list[MatrixItem], ns_steps: int) -> _PlanState:
+        key = self._key(items, ns_steps)
+        st = self._plans.pop(key, None)
+        if st is None:
+            st = self._build(items, ns_steps)
+            while len(self._plans) >= self.MAX_PLANS:
+                old = self._plans.pop(next(iter(self._plans)))
+                if old.plan is not None:
+                    self.lib.muon_ns_plan_destroy(old.plan)
+        self._plans[key] = st  # most recently used last
+        if st.plan is not None and st.sm_limit != self.sm_limit:
+            N.check(self.lib.muon_ns_plan_set_sm_limit(st.plan, int(self.sm_limit)), "muon_ns_plan_set_sm_limit")
+            st.sm_limit = self.sm_limit
+        return st
+
+    def _build(self, items: list[MatrixItem], ns_steps: int) -> _PlanState:
+        st = _PlanState()
         groups: dict[tuple, list[int]] = {}
         for i, it in enumerate(items):
             r, c = it.param.shape
             groups.setdefault((int(r), int(c), it.param.dtype), []).append(i)
-        self._classes = []
-        self._order = [(0, 0)] * len(items)
-        self._seg_order: list[int] = []
+        st.order = [(0, 0)] * len(items)
         for ci, ((r, c, dt), idxs) in enumerate(groups.items()):
             cs = _ClassState(r, c, dt, len(idxs), self.op_dtype, self.device, ns_steps, self._class_algo())
             for slot, i in enumerate(idxs):
-                self._order[i] = (ci, slot)
-                self._seg_order.append(i)
+                st.order[i] = (ci, slot)
+                st.seg_order.append(i)
             # U, rounded to the parameter dtype, for muon_apply_update; rows padded
             # to 16 bytes for the epilogue's TMA stores.
             ld_u = _pad16(c, dt)
@@ -206,27 +242,24 @@ class CudaMuonEngine:
             cs.cls.u_dtype = _dtype_code(items[idxs[0]].param)
             cs.cls.u_out = c_void_p(cs.u_buf.data_ptr())
             cs.cls.ld_u = ld_u
-            self._classes.append(cs)
-        self._scales = torch.zeros(max(len(items), 1), dtype=torch.float32, device=self.device)
+            st.classes.append(cs)
+        st.scales = torch.zeros(max(len(items), 1), dtype=torch.float32, device=self.device)
         first = 0
-        for cs in self._classes:
+        for cs in st.classes:
             cs.first_seg = first
-            cs.cls.scales = c_void_p(self._scales.data_ptr() + 4 * first)
+            cs.cls.scales = c_void_p(st.scales.data_ptr() + 4 * first)
             first += cs.count
-        self._staging = None
-        self._staging_off: dict[int, int] = {}
-        self._convert_table = None
         if self.op_dtype == N.MUON_F16:
             # fp32 directions, normalised into fp16 x0 by muon_convert_f16.
-            total = sum(cs.rows * cs.cols * cs.count for cs in self._classes)
-            self._staging = torch.empty(max(total, 1), dtype=torch.float32, device=self.device)
+            total = sum(cs.rows * cs.cols * cs.count for cs in st.classes)
+            st.staging = torch.empty(max(total, 1), dtype=torch.float32, device=self.device)
             segs, off, chunks = [], 0, 0
-            for i in self._seg_order:
-                ci, slot = self._order[i]
-                cs = self._classes[ci]
-                self._staging_off[i] = off
+            for i in st.seg_order:
+                ci, slot = st.order[i]
+                cs = st.classes[ci]
+                st.staging_off[i] = off
                 cv = N.ConvertSeg()
-                cv.src = self._staging.data_ptr() + 4 * off
+                cv.src = st.staging.data_ptr() + 4 * off
                 cv.dst = cs.cls.x0 + slot * cs.x_stride
                 cv.rows, cv.cols, cv.ld_src, cv.ld_dst = cs.rows, cs.cols, cs.cols, int(cs.cls.ld_x)
                 cv.chunk_begin = chunks
@@ -235,16 +268,16 @@ class CudaMuonEngine:
                 segs.append(cv)
                 off += cs.rows * cs.cols
                 chunks += int(self.lib.muon_momentum_chunks(cs.rows, cs.cols))
-            self._convert_table = _upload(N.struct_bytes(segs), self.device)
-            self._convert_n, self._convert_chunks = len(segs), chunks
+            st.convert_table = _upload(N.struct_bytes(segs), self.device)
+            st.convert_n, st.convert_chunks = len(segs), chunks
         if ns_steps >= 1:
-            arr = (N.NsClass * len(self._classes))(*[cs.cls for cs in self._classes])
+            arr = (N.NsClass * len(st.classes))(*[cs.cls for cs in st.classes])
             plan = c_void_p()
-            N.check(self.lib.muon_ns_plan_create(arr, len(self._classes), self.op_dtype, ns_steps, byref(plan)),
+            N.check(self.lib.muon_ns_plan_create(arr, len(st.classes), self.op_dtype, ns_steps, byref(plan)),
                     "muon_ns_plan_create")
-            self._plan = plan
-            self.ns_launches_per_run = int(self.lib.muon_ns_plan_launches(plan))
-        self._plan_key = self._key(items, ns_steps)
+            st.plan = plan
+            st.ns_launches = int(self.lib.muon_ns_plan_launches(plan))
+        return st
 
     # --------------------------------------------------------------- launches
     def _momentum(self, segs: list, grad_dtype: int, momentum: float, nesterov: bool, scales_ptr: int,
@@ -275,24 +308,23 @@ class CudaMuonEngine:
         for it in items:
             if it.param.device != self.device or not it.param.is_contiguous() or not it.exp_avg.is_contiguous():
                 raise RuntimeError("Muon matrices must be contiguous tensors on the engine's device")
-        if self._plan_key != self._key(items, ns_steps):
-            self._build(items, ns_steps)
+        st = self._state_for(items, ns_steps)
         grads = [it.grad for it in items]
         gdt = {_dtype_code(g) for g in grads if g is not None} or {N.MUON_F32}
         # Segments in class order: segment index == scale index.
         by_dtype: dict[int, list] = {}
-        for i in self._seg_order:
+        for i in st.seg_order:
             it = items[i]
-            ci, slot = self._order[i]
-            cs = self._classes[ci]
+            ci, slot = st.order[i]
+            cs = st.classes[ci]
             seg = N.MomentumSeg()
             g = it.grad
             if g is not None and not g.is_contiguous():
                 g = g.contiguous()
             seg.grad = g.data_ptr() if g is not None else None
             seg.exp_avg = it.exp_avg.data_ptr()
-            if self._staging is not None:
-                seg.direction = self._staging.data_ptr() + 4 * self._staging_off[i]
+            if st.staging is not None:
+                seg.direction = st.staging.data_ptr() + 4 * st.staging_off[i]
                 seg.rows, seg.cols, seg.ld = cs.rows, cs.cols, cs.cols
             else:
                 seg.direction = cs.cls.x0 + slot * cs.x_stride
@@ -307,37 +339,38 @@ class CudaMuonEngine:
             start = None
             for idx, seg in lst:
                 if run and idx != start + len(run):
-                    self._momentum(run, code, momentum, nesterov, self._scales.data_ptr() + 4 * start)
+                    self._momentum(run, code, momentum, nesterov, st.scales.data_ptr() + 4 * start)
                     run = []
                 if not run:
                     start = idx
                 run.append(seg)
             if run:
-                self._momentum(run, code, momentum, nesterov, self._scales.data_ptr() + 4 * start)
-        if self._convert_table is not None:
-            N.check(self.lib.muon_convert_f16(c_void_p(self._convert_table.data_ptr()), self._convert_n,
-                                              self._convert_chunks, c_void_p(self._scales.data_ptr()),
+                self._momentum(run, code, momentum, nesterov, st.scales.data_ptr() + 4 * start)
+        if st.convert_table is not None:
+            N.check(self.lib.muon_convert_f16(c_void_p(st.convert_table.data_ptr()), st.convert_n,
+                                              st.convert_chunks, c_void_p(st.scales.data_ptr()),
                                               _stream_handle()), "muon_convert_f16")
             self.kernel_launches += 1
         self._event_end(ev)
         if ns_steps >= 1:
             ev = self._event_pair("ns")
-            N.check(self.lib.muon_ns_plan_run(self._plan, c_void_p(self._err.data_ptr()), _stream_handle()),
+            N.check(self.lib.muon_ns_plan_run(st.plan, c_void_p(self._err.data_ptr()), _stream_handle()),
                     "muon_ns_plan_run")
             self._event_end(ev)
-            self.kernel_launches += self.ns_launches_per_run
+            self.ns_launches_per_run = st.ns_launches
+            self.kernel_launches += st.ns_launches
             self._record_error_check()
-            self._apply_updates(items, weight_decay_factor)
+            self._apply_updates(st, items, weight_decay_factor)
         else:
-            self._zero_step_update(items, weight_decay_factor)
+            self._zero_step_update(st, items, weight_decay_factor)
 
-    def _apply_updates(self, items: list[MatrixItem], wd_factor: float) -> None:
+    def _apply_updates(self, st: _PlanState, items: list[MatrixItem], wd_factor: float) -> None:
         """Weight decay + p -= eff * U for every matrix (muon_apply_update)."""
         segs, total = [], 0
-        for i in self._seg_order:
+        for i in st.seg_order:
             it = items[i]
-            ci, slot = self._order[i]
-            cs = self._classes[ci]
+            ci, slot = st.order[i]
+            cs = st.classes[ci]
             sg = N.UpdateSeg()
             sg.param = it.param.data_ptr()
             sg.update = cs.u_buf[slot].data_ptr()
@@ -354,19 +387,19 @@ class CudaMuonEngine:
         self._event_end(ev)
         self.kernel_launches += 1
 
-    def _normalized_input(self, cs: _ClassState, slot: int) -> torch.Tensor:
+    def _normalized_input(self, st: _PlanState, cs: _ClassState, slot: int) -> torch.Tensor:
         """The unit-norm Newton-Schulz input of one matrix, fp32 (ns_steps == 0 result)."""
         x = cs.x0_view(slot).float()
         if self.op_dtype == N.MUON_F16:
             return x / cs.x0_scale
-        return x * self._scales[cs.first_seg + slot]
+        return x * st.scales[cs.first_seg + slot]
 
-    def _zero_step_update(self, items: list[MatrixItem], wd_factor: float) -> None:
+    def _zero_step_update(self, st: _PlanState, items: list[MatrixItem], wd_factor: float) -> None:
         # ns_steps == 0: the reference's update is the normalised direction itself.
-        for i in self._seg_order:
+        for i in st.seg_order:
             it = items[i]
-            ci, slot = self._order[i]
-            u = self._normalized_input(self._classes[ci], slot)
+            ci, slot = st.order[i]
+            u = self._normalized_input(st, st.classes[ci], slot)
             if wd_factor != 1.0:
                 it.param.mul_(wd_factor)
             it.param.add_(u.to(it.param.dtype), alpha=-it.eff)
@@ -504,9 +537,11 @@ class CudaMuonEngine:
         self.kernel_launches += 1
 
     def close(self) -> None:
-        if self._plan is not None:
-            self.lib.muon_ns_plan_destroy(self._plan)
-            self._plan = None
+        for st in self._plans.values():
+            if st.plan is not None:
+                self.lib.muon_ns_plan_destroy(st.plan)
+                st.plan = None
+        self._plans.clear()
 
     def __del__(self):  # pragma: no cover - interpreter teardown order varies
         try:

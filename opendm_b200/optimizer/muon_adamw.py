@@ -34,6 +34,13 @@ The arithmetic runs in the sm_100a kernels of ``libopendm_muon.so`` through
   (momentum is advanced only by the owner; call ``consolidate_state_dict()``
   on all ranks before saving from one rank).
 * ``process_group``: group for the sharded path (default: the world).
+* ``allgather_waves``: with sharding, each rank's matrices are processed in
+  this many waves of decreasing size; the all-gather of a wave overlaps the
+  Newton-Schulz of the next (default: 3 on CUDA when there are at least 6
+  matrices per rank, else 1).
+* ``comm_sms``: SMs the Newton-Schulz launches leave free while an
+  all-gather overlaps them, and the CTA limit of the optimizer's own NCCL
+  group for that all-gather (default 16).
 """
 
 from __future__ import annotations
@@ -46,7 +53,7 @@ import torch
 import torch.distributed as dist
 
 from ..engine import AdamItem, CudaMuonEngine, MatrixItem, effective_lr
-from ..sharding import FlatParamBuckets, assign_owners
+from ..sharding import FlatParamBuckets, assign_owners, assign_waves
 
 _MUON_SHAPE = "_opendm_muon_shape"
 _MUON_NAME = "_opendm_muon_name"
@@ -172,7 +179,7 @@ class MuonAdamW(torch.optim.Optimizer):
                  muon_ns_steps: int = 5, muon_lr_scale: float = 1.0, muon_moonlight_coefficient: float = 0.2,
                  precision: str = "fp16", scale_mode: str = "reference", sharding: str = "auto",
                  state_sharding: bool = False, process_group=None, ns_algo: str = "auto",
-                 _engine=None) -> None:
+                 allgather_waves: int | None = None, comm_sms: int = 16, _engine=None) -> None:
         adamw_params, muon_params, muon_shapes, muon_names = [], [], [], []
         for param in model.parameters():
             if not param.requires_grad:
@@ -215,7 +222,13 @@ class MuonAdamW(torch.optim.Optimizer):
         self._host_steps: dict = {}
         self._owners: dict[int, list[int]] = {}
         self._buckets: dict[int, FlatParamBuckets] = {}
+        self._waves: dict[int, list[int]] = {}
         self._flag_group = None  # host (gloo) group for the per-step activity flag
+        self._ag_group = None  # NCCL group of the parameter all-gather (CTA-limited)
+        if allgather_waves is not None and int(allgather_waves) < 1:
+            raise ValueError("allgather_waves must be >= 1")
+        self.allgather_waves = allgather_waves
+        self.comm_sms = max(int(comm_sms), 0)
 
     # ---------------------------------------------------------------- groups
     def _normalize_param_groups(self) -> None:
@@ -377,16 +390,42 @@ class MuonAdamW(torch.optim.Optimizer):
         return all(p.kind == "replicated" for p in plans) and \
             all(p.is_contiguous() for p in group["params"])
 
+    def _n_waves(self, n_matrices: int, world: int, device: torch.device) -> int:
+        if self.allgather_waves is not None:
+            return int(self.allgather_waves)
+        return 3 if device.type == "cuda" and n_matrices >= 6 * world else 1
+
     def _owners_for(self, group: dict) -> list[int]:
         key = id(group)
         owners = self._owners.get(key)
         if owners is None or len(owners) != len(group["params"]):
             world, rank = self._world()
-            owners = assign_owners(group["muon_shapes"], world, int(group["muon_ns_steps"]))
+            shapes, steps = group["muon_shapes"], int(group["muon_ns_steps"])
+            owners = assign_owners(shapes, world, steps)
+            n_waves = self._n_waves(len(shapes), world, self._device_for_params(group["params"]))
+            waves = assign_waves(shapes, owners, world, n_waves, steps)
             self._owners[key] = owners
+            self._waves[key] = waves
             self._buckets[key] = FlatParamBuckets(list(group["params"]), owners, world, rank,
-                                                  self.process_group)
+                                                  self.process_group, waves)
         return owners
+
+    def _allgather_group(self, device: torch.device):
+        """The group for the parameter all-gather: on CUDA with NCCL, a
+        group of the same ranks whose kernels use at most ``comm_sms`` CTAs
+        on a high-priority stream (created on first use, on every rank)."""
+        pg = self.process_group
+        if device.type != "cuda" or dist.get_backend(pg) != "nccl":
+            return pg
+        if self._ag_group is None:
+            opts = dist.ProcessGroupNCCL.Options()
+            opts.is_high_priority_stream = True
+            if self.comm_sms > 0:
+                opts.config.max_ctas = self.comm_sms
+            ranks = dist.get_process_group_ranks(pg) if pg is not None else None
+            self._ag_group = (dist.new_group(ranks=ranks, backend="nccl", pg_options=opts,
+                                             use_local_synchronization=pg is not None),)
+        return self._ag_group[0]
 
     def _muon_step(self, group: dict) -> None:
         if not self._muon_group_is_active(group["params"]):
@@ -402,7 +441,10 @@ class MuonAdamW(torch.optim.Optimizer):
         owners = self._owners_for(group) if sharded else None
         _, rank = self._world()
 
-        owned, others, partial, step_tensors = [], [], [], []
+        waves = self._waves.get(id(group)) if sharded else None
+        n_waves = (max(waves) + 1) if waves else 1
+        owned = [[] for _ in range(n_waves)]
+        others, partial, step_tensors = [], [], []
         for index, (param, shape, plan) in enumerate(zip(group["params"], group["muon_shapes"], plans, strict=True)):
             if plan.local_numel == 0:
                 continue
@@ -425,20 +467,39 @@ class MuonAdamW(torch.optim.Optimizer):
                 if not self.state_sharding:
                     others.append(item)
             else:
-                owned.append(item)
+                owned[waves[index] if waves else 0].append(item)
         if step_tensors:
             torch._foreach_add_(step_tensors, 1.0)
         device = self._device_for_params(group["params"])
         engine = self._get_engine(device)
-        engine.muon_matrices(owned, momentum=momentum, nesterov=nesterov, weight_decay_factor=wd_factor,
-                             ns_steps=ns_steps)
+        if not sharded:
+            engine.muon_matrices(owned[0], momentum=momentum, nesterov=nesterov, weight_decay_factor=wd_factor,
+                                 ns_steps=ns_steps)
+        else:
+            # Wave w's all-gather runs on the collective's stream while wave
+            # w + 1 is orthogonalised with `comm_sms` SMs left free for it.
+            buckets = self._buckets[id(group)]
+            ag_group = self._allgather_group(device)
+            overlap = device.type == "cuda" and n_waves > 1 and hasattr(engine, "sm_limit")
+            total_sms = torch.cuda.get_device_properties(device).multi_processor_count if overlap else 0
+            handles = []
+            for w in range(n_waves):
+                if overlap:
+                    engine.sm_limit = max(total_sms - self.comm_sms, 2) if w > 0 else 0
+                engine.muon_matrices(owned[w], momentum=momentum, nesterov=nesterov,
+                                     weight_decay_factor=wd_factor, ns_steps=ns_steps)
+                handles += buckets.sync(wave=w, async_op=device.type == "cuda", group=ag_group)
+            if overlap:
+                engine.sm_limit = 0
         engine.momentum_only(others, momentum=momentum, nesterov=nesterov)
         for param, grad, state, shape, plan, eff in partial:
             self._partial_update(engine, param, grad, state, shape, plan, eff, momentum, nesterov, wd_factor,
                                  ns_steps)
         if sharded:
-            ev = engine._event_pair("allgather") if getattr(engine, "profile_events", None) is not None else None
-            self._buckets[id(group)].sync()
+            ev = engine._event_pair("allgather_wait") if getattr(engine, "profile_events", None) is not None \
+                else None
+            for h in handles:
+                h.wait()
             if ev is not None:
                 engine._event_end(ev)
 

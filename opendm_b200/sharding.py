@@ -8,9 +8,13 @@ each matrix gets one owner rank:
   Newton-Schulz FLOPs: matrices in decreasing cost order, each to the least
   loaded rank (ties to the lower rank). Deterministic, so every rank computes
   the same plan without communication.
+* ``assign_waves`` -- each rank's owned matrices, largest first, cut into
+  waves whose Newton-Schulz FLOPs shrink geometrically. The all-gather of
+  wave w runs on the collective's stream while wave w + 1 is orthogonalised,
+  so only the last (smallest) wave's all-gather is exposed.
 * ``FlatParamBuckets`` -- after the owners update their matrices in place, one
-  ``all_gather_into_tensor`` per dtype delivers them to every rank. The
-  parameters are re-pointed once to views of a flat buffer laid out as
+  ``all_gather_into_tensor`` per (dtype, wave) delivers them to every rank.
+  The parameters are re-pointed once to views of flat buffers laid out as
   [rank 0 bucket | rank 1 bucket | ...] (each bucket padded to the same
   size), so the collective writes straight into the parameters: no pack or
   unpack copies.
@@ -42,6 +46,42 @@ def assign_owners(shapes: list[tuple[int, int]], world_size: int, steps: int = 5
     return owners
 
 
+def wave_fractions(n_waves: int, ratio: float = 0.7) -> list[float]:
+    """FLOP share of each wave: geometric, each wave `ratio` times the one
+    before (the all-gather of a wave must hide behind the next wave's
+    Newton-Schulz, which takes ~1.4x longer per byte at 8 ranks)."""
+    w = [ratio ** i for i in range(max(n_waves, 1))]
+    total = sum(w)
+    return [x / total for x in w]
+
+
+def assign_waves(shapes: list[tuple[int, int]], owners: list[int], world_size: int, n_waves: int,
+                 steps: int = 5) -> list[int]:
+    """Wave index of each matrix: every rank cuts its own matrices, in
+    decreasing cost order, at the cumulative shares of ``wave_fractions``.
+    Deterministic, so every rank computes every rank's waves."""
+    waves = [0] * len(shapes)
+    if n_waves <= 1:
+        return waves
+    bounds = []
+    acc = 0.0
+    for f in wave_fractions(n_waves)[:-1]:
+        acc += f
+        bounds.append(acc)
+    for r in range(world_size):
+        mine = sorted((i for i, o in enumerate(owners) if o == r), key=lambda i: (-ns_cost(shapes[i], steps), i))
+        total = sum(ns_cost(shapes[i], steps) for i in mine)
+        done, w = 0.0, 0
+        for i in mine:
+            # a matrix joins the wave its cost midpoint falls into
+            mid = (done + ns_cost(shapes[i], steps) / 2) / total if total > 0 else 0.0
+            while w < len(bounds) and mid > bounds[w]:
+                w += 1
+            waves[i] = w
+            done += ns_cost(shapes[i], steps)
+    return waves
+
+
 def load_balance(shapes: list[tuple[int, int]], owners: list[int], world_size: int, steps: int = 5) -> dict:
     """Per-rank Newton-Schulz FLOPs and the max/mean imbalance of a plan."""
     loads = [0.0] * world_size
@@ -52,25 +92,28 @@ def load_balance(shapes: list[tuple[int, int]], owners: list[int], world_size: i
 
 
 class FlatParamBuckets:
-    """Re-points owned-by-rank parameters into per-dtype flat buffers and
-    all-gathers the owners' buckets into every rank."""
+    """Re-points owned-by-rank parameters into flat buffers, one per (dtype,
+    wave), and all-gathers the owners' buckets into every rank."""
 
     def __init__(self, params: list[torch.Tensor], owners: list[int], world_size: int, rank: int,
-                 process_group=None):
+                 process_group=None, waves: list[int] | None = None):
         self.world_size = world_size
         self.rank = rank
         self.group = process_group
-        self.buffers: list[tuple[torch.Tensor, int]] = []  # (flat buffer, bucket elements)
-        by_dtype: dict[torch.dtype, list[int]] = {}
+        waves = waves if waves is not None else [0] * len(params)
+        self.n_waves = max(waves, default=0) + 1
+        # (flat buffer, bucket elements, wave)
+        self.buffers: list[tuple[torch.Tensor, int, int]] = []
+        by_key: dict[tuple, list[int]] = {}
         for i, p in enumerate(params):
-            by_dtype.setdefault(p.dtype, []).append(i)
-        for dtype, idxs in by_dtype.items():
+            by_key.setdefault((waves[i], str(p.dtype)), []).append(i)
+        for (wave, _), idxs in sorted(by_key.items()):
             sizes = [0] * world_size
             for i in idxs:
                 sizes[owners[i]] += params[i].numel()
             bucket = max(sizes)
             bucket = (bucket + 127) // 128 * 128  # keep every bucket 256-byte aligned
-            device = params[idxs[0]].device
+            dtype, device = params[idxs[0]].dtype, params[idxs[0]].device
             flat = torch.zeros(bucket * world_size, dtype=dtype, device=device)
             offsets = [r * bucket for r in range(world_size)]
             for i in idxs:
@@ -81,16 +124,24 @@ class FlatParamBuckets:
                 view.copy_(p.data)
                 p.data = view
                 offsets[r] += n
-            self.buffers.append((flat, bucket))
+            self.buffers.append((flat, bucket, wave))
 
-    def sync(self) -> None:
-        """All-gather every owner's bucket into all ranks (in place)."""
-        for flat, bucket in self.buffers:
-            if bucket == 0:
+    def sync(self, wave: int | None = None, async_op: bool = False, group=None) -> list:
+        """All-gather every owner's bucket into all ranks (in place), for one
+        wave or all of them. With ``async_op`` (CUDA only) the collectives
+        are queued behind the work already on the current stream and their
+        handles returned; ``wait()`` on each makes the current stream wait
+        for it."""
+        handles = []
+        group = group if group is not None else self.group
+        for flat, bucket, w in self.buffers:
+            if bucket == 0 or (wave is not None and w != wave):
                 continue
             mine = flat[self.rank * bucket:(self.rank + 1) * bucket]
             if flat.device.type == "cuda":
-                dist.all_gather_into_tensor(flat, mine, group=self.group)
+                h = dist.all_gather_into_tensor(flat, mine, group=group, async_op=async_op)
+                if async_op:
+                    handles.append(h)
             else:
                 # gloo has no in-place all_gather_into_tensor: gather a list and copy back.
                 parts = [torch.empty_like(mine) for _ in range(self.world_size)]
@@ -98,7 +149,8 @@ class FlatParamBuckets:
                 for r, part in enumerate(parts):
                     if r != self.rank:
                         flat[r * bucket:(r + 1) * bucket].copy_(part)
+        return handles
 
     def nbytes_received(self) -> int:
         """Bytes each rank receives per sync."""
-        return sum(b * flat.element_size() * (self.world_size - 1) for flat, b in self.buffers)
+        return sum(b * flat.element_size() * (self.world_size - 1) for flat, b, _ in self.buffers)

@@ -69,7 +69,7 @@ def _worker(rank, port, scenario, muon, adam, steps, outdir):
         params, grads = _data(muon, adam, steps)
         model = torch.nn.Module()
         n_muon = len(muon)
-        if scenario in ("replicated", "state_sharding", "fail"):
+        if scenario in ("replicated", "state_sharding", "fail", "waves"):
             for i, p in enumerate(params):
                 t = torch.nn.Parameter(torch.from_numpy(p.copy()))
                 if i < n_muon:
@@ -98,7 +98,8 @@ def _worker(rank, port, scenario, muon, adam, steps, outdir):
                 model.register_parameter(f"p{i}", torch.nn.Parameter(torch.from_numpy(params[i].copy())))
         engine = OracleEngine()
         opt = MuonAdamW(model, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, _engine=engine,
-                        state_sharding=(scenario == "state_sharding"))
+                        state_sharding=(scenario in ("state_sharding", "waves")),
+                        allgather_waves=3 if scenario == "waves" else None)
         plist = list(model.parameters())
         for s in range(steps):
             if scenario == "fail" and rank == 1 and s == 1:
@@ -110,7 +111,7 @@ def _worker(rank, port, scenario, muon, adam, steps, outdir):
                     g = g.reshape(-1)[a:b]
                 p.grad = torch.from_numpy(g.copy())
             opt.step()
-        if scenario == "state_sharding":
+        if scenario in ("state_sharding", "waves"):
             opt.consolidate_state_dict()
         result["params"] = [p.detach().numpy().copy() for p in plist]
         result["exp_avg"] = [opt.state[p]["exp_avg"].numpy().copy() if "exp_avg" in opt.state[p]
@@ -118,6 +119,7 @@ def _worker(rank, port, scenario, muon, adam, steps, outdir):
         result["slices"] = slices
         result["muon_calls"] = engine.matrices_seen
         result["kinds"] = [pl.kind for pl in opt._get_muon_shard_plans(opt.param_groups[1])]
+        result["waves"] = opt._waves.get(id(opt.param_groups[1]))
         dist.barrier()
         dist.destroy_process_group()
     except SystemExit:
@@ -170,6 +172,14 @@ def test_c1_sharded_two_ranks(tmp_path):
     assert all(k == "replicated" for k in res[0]["kinds"])
     assert res[0]["muon_calls"] + res[1]["muon_calls"] == 2 * len(C1_MUON)  # no redundant NS
     assert 0 < res[0]["muon_calls"] < 2 * len(C1_MUON)
+
+
+def test_allgather_waves_two_ranks(tmp_path):
+    """Three all-gather waves per step (each rank's matrices cut by FLOPs,
+    one flat bucket per wave): same result as the single-process oracle."""
+    res = _run("waves", C1_MUON + SMALL_MUON, C1_ADAM, 2, tmp_path)
+    _check(res, C1_MUON + SMALL_MUON, C1_ADAM, 2)
+    assert res[0]["waves"] == res[1]["waves"] and set(res[0]["waves"]) == {0, 1, 2}
 
 
 def test_owner_only_momentum_consolidates(tmp_path):

@@ -310,3 +310,29 @@ def test_lpt_assignment_balances_and_is_deterministic():
         assert lb["max_over_mean"] < 1.02, lb
     assert assign_owners(shapes, 1) == [0] * len(shapes)
     assert ns_cost((8, 4)) == ns_cost((4, 8)) == 5 * (4 * 16 * 8 + 2 * 64)
+
+
+def test_waves_follow_geometric_flop_shares():
+    """Each rank's matrices, largest first, are cut into waves whose FLOP
+    shares shrink geometrically; deterministic and identical on every rank."""
+    from opendm_b200.sharding import assign_waves, wave_fractions
+
+    fr = wave_fractions(3)
+    assert abs(sum(fr) - 1) < 1e-12 and fr[0] > fr[1] > fr[2]
+    shapes = [(2048, 2048)] * 56 + [(256, 2048)] * 56 + [(8192, 2048)] * 56 + [(2048, 8192)] * 28
+    for world in (1, 2, 8):
+        owners = assign_owners(shapes, world)
+        waves = assign_waves(shapes, owners, world, 3)
+        assert waves == assign_waves(shapes, owners, world, 3)
+        for r in range(world):
+            mine = [i for i, o in enumerate(owners) if o == r]
+            total = sum(ns_cost(shapes[i]) for i in mine)
+            share = [sum(ns_cost(shapes[i]) for i in mine if waves[i] == w) / total for w in range(3)]
+            # within one matrix of the target share; waves never grow
+            biggest = max(ns_cost(shapes[i]) for i in mine) / total
+            for w in range(3):
+                assert abs(share[w] - fr[w]) <= biggest + 1e-9, (world, r, share)
+            # larger matrices in earlier waves: waves never decrease along the cost order
+            by_cost = sorted(mine, key=lambda i: (-ns_cost(shapes[i]), i))
+            assert [waves[i] for i in by_cost] == sorted(waves[i] for i in by_cost)
+    assert assign_waves(shapes, assign_owners(shapes, 2), 2, 1) == [0] * len(shapes)
