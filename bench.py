@@ -283,6 +283,10 @@ def run_reference(args):
 
 # -------------------------------------------------------------- GPU leg
 def run_ours(args):
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        # one copy stream per peer (p2p all-gather) next to the compute and NCCL
+        # streams: enough hardware queues that they do not serialise
+        os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
     import torch
     import torch.distributed as dist
 
@@ -316,7 +320,8 @@ def run_ours(args):
     keymap = {name.replace(".", "_"): (name, shape) for name, shape in spec}
     mark_muon_parameters(model, predicate=lambda n, p: is_muon(*keymap[n]))
     opt = MuonAdamW(model, lr=LR, betas=BETAS, eps=EPS, weight_decay=WD, muon_momentum=MOMENTUM,
-                    muon_ns_steps=NS_STEPS, precision=args.precision, state_sharding=world > 1)
+                    muon_ns_steps=NS_STEPS, precision=args.precision, state_sharding=world > 1,
+                    allgather=args.allgather, comm_sms=args.comm_sms)
     params = list(model.parameters())
     ggen = torch.Generator(device=device).manual_seed(1)
     grads = []
@@ -406,12 +411,14 @@ def run_ours(args):
     ag_ms = 0.0
     if bucket is not None:
         # the parameter all-gather alone (same group and CTA limit), once, untimed by the step
-        ag_group = opt._allgather_group(device)
         sync_all()
         a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a0.record()
-        for h in bucket.sync(async_op=True, group=ag_group):
-            h.wait()
+        if hasattr(bucket, "wave_done"):
+            bucket.sync()
+        else:
+            for h in bucket.sync(async_op=True, group=opt._allgather_group(device)):
+                h.wait()
         a1.record()
         sync_all()
         ag_ms = max_over_ranks(a0.elapsed_time(a1))
@@ -489,7 +496,8 @@ def run_ours(args):
                             "allgather_alone_ms": round(ag_ms, 3),
                             "allgather_alone_gbs": round(ag_bytes / (ag_ms * 1e-3) / 1e9, 1) if ag_ms > 0 else 0.0,
                             "waves": bucket.n_waves if bucket is not None else 1,
-                            "comm_sms": opt.comm_sms,
+                            "transport": opt.allgather,
+                            "comm_sms": opt.comm_sms if opt.allgather == "nccl" else 0,
                             "exposed_wait_ms": round(ag_wait_ms, 3)}
                            if world > 1 else None),
             "clocks": clocks,
@@ -510,6 +518,9 @@ def main(argv=None):
     ap.add_argument("--precision", default="fp16", choices=["fp16", "tf32", "bf16"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--allgather", default="nccl", choices=["nccl", "p2p"],
+                    help="parameter all-gather of the sharded step (N > 1)")
+    ap.add_argument("--comm-sms", type=int, default=32, help="SMs left to an overlapping NCCL all-gather")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3

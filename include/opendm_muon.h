@@ -263,6 +263,30 @@ int muon_ns_choose_algo(int32_t rows, int32_t cols, int op_dtype, int steps);
  * muon_ns_class_workspace_bytes() bytes. */
 int muon_ns_class_layout(muon_ns_class* cls, void* base, int op_dtype);
 
+/* ------------------------------- (d') cross-GPU flags for the all-gather
+ * The sharded step moves the owners' updated parameters between GPUs with
+ * cudaMemcpyAsync over NVLink (copy engines, no SMs) out of peer-mapped
+ * buffers. These calls order the copies: no counterpart in the reference,
+ * which gathers with torch.distributed collectives (muon_adamw.py:503-535).
+ * A flag is a 4-byte-aligned uint32 in device memory of this GPU or of a peer
+ * mapped into its address space.
+ *
+ * muon_flags_set: after all work queued before it on `stream`, stores `value`
+ * to each flag with release semantics at system scope.
+ * muon_flags_wait: work queued after it on `stream` starts once every flag
+ * reaches `value` (compared in wrap-around order), read with acquire
+ * semantics. The wait is bounded by `timeout_us`; on expiry it records 0x106
+ * in the device int `err_dev` and lets the stream go on (the host reads the
+ * word with muon_read_error). */
+#define MUON_MAX_FLAGS 32
+typedef struct muon_flag_list {
+  uint32_t* ptr[MUON_MAX_FLAGS];
+  int32_t n;
+} muon_flag_list;
+
+int muon_flags_set(const muon_flag_list* list, uint32_t value, void* stream);
+int muon_flags_wait(const muon_flag_list* list, uint32_t value, int64_t timeout_us, int* err_dev, void* stream);
+
 /* ------------------------------------------- (c) weight decay + update
  * Replaces muon_adamw.py:395-398 and :407-414 for whole matrices, with the
  * reference's rounding order:

@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import POINTER, Structure, c_char_p, c_double, c_float, c_int, c_int32, c_int64, c_void_p
+from ctypes import POINTER, Structure, c_char_p, c_double, c_float, c_int, c_int32, c_int64, c_uint32, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libopendm_muon.so"
@@ -82,6 +82,13 @@ class NsClass(Structure):
     ]
 
 
+MUON_MAX_FLAGS = 32
+
+
+class FlagList(Structure):
+    _fields_ = [("ptr", c_void_p * MUON_MAX_FLAGS), ("n", c_int32)]
+
+
 class UpdateSeg(Structure):
     _fields_ = [
         ("param", c_void_p),
@@ -130,6 +137,8 @@ SIGNATURES = {
     "muon_ns_plan_destroy": (None, [c_void_p]),
     "muon_ns_plan_launches": (c_int, [c_void_p]),
     "muon_ns_plan_set_sm_limit": (c_int, [c_void_p, c_int]),
+    "muon_flags_set": (c_int, [POINTER(FlagList), c_uint32, c_void_p]),
+    "muon_flags_wait": (c_int, [POINTER(FlagList), c_uint32, c_int64, c_void_p, c_void_p]),
     "muon_ns_class_workspace_bytes": (c_int64, [c_int32, c_int32, c_int32, c_int, c_int]),
     "muon_ns_choose_algo": (c_int, [c_int32, c_int32, c_int, c_int]),
     "muon_ns_class_layout": (c_int, [POINTER(NsClass), c_void_p, c_int]),

@@ -133,6 +133,14 @@ void muon_ns_plan_destroy(muon_ns_plan* plan) { muon::ns_plan_destroy(plan); }
 
 int muon_ns_plan_launches(const muon_ns_plan* plan) { return muon::ns_plan_launches(plan); }
 
+int muon_flags_set(const muon_flag_list* list, uint32_t value, void* stream) {
+  return muon::launch_flags_set(list, value, static_cast<cudaStream_t>(stream));
+}
+
+int muon_flags_wait(const muon_flag_list* list, uint32_t value, int64_t timeout_us, int* err_dev, void* stream) {
+  return muon::launch_flags_wait(list, value, timeout_us, err_dev, static_cast<cudaStream_t>(stream));
+}
+
 int muon_ns_plan_set_sm_limit(muon_ns_plan* plan, int sms) { return muon::ns_plan_set_sm_limit(plan, sms); }
 
 int64_t muon_ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype, int algo) {

@@ -30,6 +30,7 @@ enum DeviceError : int {
   kDevTimeoutTmemFull = 0x103, // epilogue waited for an accumulator
   kDevTimeoutTmemEmpty = 0x104,// MMA waited for a drained accumulator
   kDevTimeoutDrain = 0x105,    // final drain of in-flight work
+  kDevTimeoutFlag = 0x106,     // a cross-GPU flag was not raised in time
   kDevSelftest = 0x1ff,        // muon_selftest_bounded_wait
 };
 

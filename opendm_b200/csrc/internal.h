@@ -39,6 +39,10 @@ int ns_choose_algo(int32_t rows, int32_t cols, int op_dtype, int steps);
 int ns_class_layout(muon_ns_class* cls, void* base, int op_dtype);
 float ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dtype);
 
+int launch_flags_set(const muon_flag_list* list, uint32_t value, cudaStream_t stream);
+int launch_flags_wait(const muon_flag_list* list, uint32_t value, int64_t timeout_us, int* err_dev,
+                      cudaStream_t stream);
+
 int launch_convert(const muon_convert_seg* segs_dev, int n_segs, int64_t total_chunks,
                    const float* scales_dev, cudaStream_t stream);
 

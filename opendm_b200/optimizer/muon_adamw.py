@@ -38,9 +38,13 @@ The arithmetic runs in the sm_100a kernels of ``libopendm_muon.so`` through
   this many waves of decreasing size; the all-gather of a wave overlaps the
   Newton-Schulz of the next (default: 3 on CUDA when there are at least 6
   matrices per rank, else 1).
-* ``comm_sms``: SMs the Newton-Schulz launches leave free while an
+* ``comm_sms``: SMs the Newton-Schulz launches leave free while an NCCL
   all-gather overlaps them, and the CTA limit of the optimizer's own NCCL
-  group for that all-gather (default 16).
+  group for that all-gather (default 32).
+* ``allgather``: "nccl" (default) or "p2p": the flat parameter buckets live
+  in peer-mapped memory and each rank pulls its peers' buckets with
+  copy-engine memcpys ordered by cross-GPU flags (``opendm_b200.p2p``), so
+  the Newton-Schulz keeps every SM.
 """
 
 from __future__ import annotations
@@ -179,7 +183,8 @@ class MuonAdamW(torch.optim.Optimizer):
                  muon_ns_steps: int = 5, muon_lr_scale: float = 1.0, muon_moonlight_coefficient: float = 0.2,
                  precision: str = "fp16", scale_mode: str = "reference", sharding: str = "auto",
                  state_sharding: bool = False, process_group=None, ns_algo: str = "auto",
-                 allgather_waves: int | None = None, comm_sms: int = 16, _engine=None) -> None:
+                 allgather_waves: int | None = None, comm_sms: int = 32, allgather: str = "nccl",
+                 _engine=None) -> None:
         adamw_params, muon_params, muon_shapes, muon_names = [], [], [], []
         for param in model.parameters():
             if not param.requires_grad:
@@ -227,6 +232,9 @@ class MuonAdamW(torch.optim.Optimizer):
         self._ag_group = None  # NCCL group of the parameter all-gather (CTA-limited)
         if allgather_waves is not None and int(allgather_waves) < 1:
             raise ValueError("allgather_waves must be >= 1")
+        if allgather not in ("nccl", "p2p"):
+            raise ValueError(f"allgather must be 'nccl' or 'p2p', got {allgather!r}")
+        self.allgather = allgather
         self.allgather_waves = allgather_waves
         self.comm_sms = max(int(comm_sms), 0)
 
@@ -406,9 +414,26 @@ class MuonAdamW(torch.optim.Optimizer):
             waves = assign_waves(shapes, owners, world, n_waves, steps)
             self._owners[key] = owners
             self._waves[key] = waves
-            self._buckets[key] = FlatParamBuckets(list(group["params"]), owners, world, rank,
-                                                  self.process_group, waves)
+            device = self._device_for_params(group["params"])
+            if self._use_p2p(device):
+                from ..p2p import P2PFlatBuckets
+
+                engine = self._get_engine(device)
+                self._buckets[key] = P2PFlatBuckets(list(group["params"]), owners, world, rank, self.process_group,
+                                                    waves, engine._err)
+            else:
+                self._buckets[key] = FlatParamBuckets(list(group["params"]), owners, world, rank,
+                                                      self.process_group, waves)
         return owners
+
+    def _use_p2p(self, device: torch.device) -> bool:
+        if self.allgather != "p2p":
+            return False
+        from .. import p2p
+
+        if device.type != "cuda" or not p2p.available():
+            raise RuntimeError("allgather='p2p' needs CUDA devices and torch symmetric memory")
+        return True
 
     def _allgather_group(self, device: torch.device):
         """The group for the parameter all-gather: on CUDA with NCCL, a
@@ -479,18 +504,27 @@ class MuonAdamW(torch.optim.Optimizer):
             # Wave w's all-gather runs on the collective's stream while wave
             # w + 1 is orthogonalised with `comm_sms` SMs left free for it.
             buckets = self._buckets[id(group)]
-            ag_group = self._allgather_group(device)
-            overlap = device.type == "cuda" and n_waves > 1 and hasattr(engine, "sm_limit")
-            total_sms = torch.cuda.get_device_properties(device).multi_processor_count if overlap else 0
+            p2p = hasattr(buckets, "wave_done")
             handles = []
-            for w in range(n_waves):
+            if p2p:
+                # copy engines: every SM stays with the Newton-Schulz
+                buckets.begin()
+                for w in range(n_waves):
+                    engine.muon_matrices(owned[w], momentum=momentum, nesterov=nesterov,
+                                         weight_decay_factor=wd_factor, ns_steps=ns_steps)
+                    buckets.wave_done(w)
+            else:
+                ag_group = self._allgather_group(device)
+                overlap = device.type == "cuda" and n_waves > 1 and hasattr(engine, "sm_limit")
+                total_sms = torch.cuda.get_device_properties(device).multi_processor_count if overlap else 0
+                for w in range(n_waves):
+                    if overlap:
+                        engine.sm_limit = max(total_sms - self.comm_sms, 2) if w > 0 else 0
+                    engine.muon_matrices(owned[w], momentum=momentum, nesterov=nesterov,
+                                         weight_decay_factor=wd_factor, ns_steps=ns_steps)
+                    handles += buckets.sync(wave=w, async_op=device.type == "cuda", group=ag_group)
                 if overlap:
-                    engine.sm_limit = max(total_sms - self.comm_sms, 2) if w > 0 else 0
-                engine.muon_matrices(owned[w], momentum=momentum, nesterov=nesterov,
-                                     weight_decay_factor=wd_factor, ns_steps=ns_steps)
-                handles += buckets.sync(wave=w, async_op=device.type == "cuda", group=ag_group)
-            if overlap:
-                engine.sm_limit = 0
+                    engine.sm_limit = 0
         engine.momentum_only(others, momentum=momentum, nesterov=nesterov)
         for param, grad, state, shape, plan, eff in partial:
             self._partial_update(engine, param, grad, state, shape, plan, eff, momentum, nesterov, wd_factor,
@@ -500,6 +534,8 @@ class MuonAdamW(torch.optim.Optimizer):
                 else None
             for h in handles:
                 h.wait()
+            if p2p:
+                buckets.finish()
             if ev is not None:
                 engine._event_end(ev)
 

@@ -85,6 +85,17 @@ def test_argument_validation_reports_errors(lib):
     assert lib.muon_momentum(None, 2, 4, N.MUON_BF16, N.MUON_TF32, 0.9, 1, 1e-7, None, None, None) == N.MUON_ERR_ARG
     assert lib.muon_apply_update(None, 2, 4, 1.0, None) == N.MUON_ERR_ARG
     assert lib.muon_convert_f16(None, 2, 4, None, None) == N.MUON_ERR_ARG
+    # cross-GPU flags: list size, null and misaligned pointers are rejected before any launch
+    fl = N.FlagList()
+    fl.n = N.MUON_MAX_FLAGS + 1
+    assert lib.muon_flags_set(ctypes.byref(fl), 1, None) == N.MUON_ERR_ARG
+    fl.n = 1
+    assert lib.muon_flags_set(ctypes.byref(fl), 1, None) == N.MUON_ERR_ARG  # null flag
+    fl.ptr[0] = 4098
+    assert lib.muon_flags_wait(ctypes.byref(fl), 1, 1000, ctypes.c_void_p(4096), None) == N.MUON_ERR_ARG
+    fl.ptr[0] = 4096
+    assert lib.muon_flags_wait(ctypes.byref(fl), 1, 0, ctypes.c_void_p(4096), None) == N.MUON_ERR_ARG
+    assert lib.muon_flags_wait(None, 1, 1000, ctypes.c_void_p(4096), None) == N.MUON_ERR_ARG
     with pytest.raises(RuntimeError, match="failed"):
         N.check(N.MUON_ERR_ARG, "probe")
 

@@ -3,8 +3,9 @@ orthogonalised by one owner rank, the updated parameters all-gathered into
 flat per-dtype buckets) gives bit-identical parameters to every rank running
 every matrix (sharding="off", the reference's redundant schedule), with every
 momentum buffer current (state_sharding=False), with owner-only momentum
-consolidated afterwards (state_sharding=True), and with the all-gather split
-into three waves that overlap the Newton-Schulz of the next wave.
+consolidated afterwards (state_sharding=True), with the all-gather split
+into waves that overlap the Newton-Schulz of the next wave, over NCCL or over
+copy engines out of peer-mapped buffers (allgather="p2p").
 
 Bitwise equality holds because each matrix's kernels see the same inputs in
 both schedules and every reduction (momentum norm partials, tile K order) is
@@ -36,7 +37,7 @@ def _port():
     return port
 
 
-def _build(dev, sharding, state_sharding, waves=None):
+def _build(dev, sharding, state_sharding, waves=None, allgather="nccl"):
     from opendm_b200.optimizer import MuonAdamW
 
     g = torch.Generator(device=dev).manual_seed(11)
@@ -48,7 +49,7 @@ def _build(dev, sharding, state_sharding, waves=None):
             t._opendm_muon_name = f"m{i}"
         model.register_parameter(f"p{i}", t)
     opt = MuonAdamW(model, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, sharding=sharding,
-                    state_sharding=state_sharding, allgather_waves=waves)
+                    state_sharding=state_sharding, allgather_waves=waves, allgather=allgather)
     return model, opt
 
 
@@ -64,10 +65,13 @@ def _worker(rank, port, outdir):
         dev = torch.device("cuda", rank)
         dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=timedelta(seconds=60), device_id=dev)
         runs = {}
-        for name, sharding, state_sharding, waves in (("off", "off", False, None), ("auto", "auto", False, None),
-                                                      ("auto_owner", "auto", True, None),
-                                                      ("waves", "auto", True, 3)):
-            model, opt = _build(dev, sharding, state_sharding, waves)
+        for name, sharding, state_sharding, waves, ag in (("off", "off", False, None, "nccl"),
+                                                          ("auto", "auto", False, None, "nccl"),
+                                                          ("auto_owner", "auto", True, None, "nccl"),
+                                                          ("waves", "auto", True, 3, "nccl"),
+                                                          ("p2p", "auto", True, 3, "p2p"),
+                                                          ("p2p_replicated_state", "auto", False, 2, "p2p")):
+            model, opt = _build(dev, sharding, state_sharding, waves, ag)
             gg = torch.Generator(device=dev).manual_seed(12)
             for _ in range(STEPS):
                 for p in model.parameters():
@@ -110,7 +114,7 @@ def test_two_gpu_sharded_equals_unsharded(tmp_path):
     owners = res[0]["runs"]["auto"]["owners"]
     assert owners is not None and set(owners) == {0, 1}  # both ranks own work
     for r in res:
-        for name in ("off", "auto", "auto_owner", "waves"):
+        for name in ("off", "auto", "auto_owner", "waves", "p2p", "p2p_replicated_state"):
             run = r["runs"][name]
             for i, (got, want) in enumerate(zip(run["params"], ref["params"])):
                 assert torch.equal(got, want), (r["rank"], name, "param", i)
