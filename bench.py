@@ -123,6 +123,11 @@ def ns_flops(shape, steps=NS_STEPS):
 
 GRAM_SEGMENT = 3  # iterations between restarts of the gram-form Newton-Schulz
 
+# DRAM bytes (read + write) per ns_gemm launch, from one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum) of the c2s case, 0.668 GB per
+# launch, scaled by the Muon element count (c2 has 7x c2s's matrices, same classes).
+NS_TRAFFIC_PER_LAUNCH = {"c2": 7 * 0.668e9, "c2s": 0.668e9}
+
 
 def ns_executed_flops(shape, steps=NS_STEPS, algo="standard"):
     """FLOPs the Newton-Schulz launches execute for one matrix: 256 x 256
@@ -486,7 +491,10 @@ def run_ours(args):
                                                   "the symmetric products avoid work, not a tensor-core rate"),
                          "frac_of_tf32_peak": round(ns_tflops / (peak / 2), 4) if args.precision == "tf32" else None,
                          "mma_kind": "kind::tf32" if args.precision == "tf32" else "kind::f16",
-                         "traffic": None, "ns_ms": round(ns_ms, 3)},
+                         "traffic": (NS_TRAFFIC_PER_LAUNCH[cfg] if cfg in NS_TRAFFIC_PER_LAUNCH and world == 1
+                                     else None),
+                         "traffic_unit": "bytes per ns_gemm launch (ncu, c2s capture scaled by element count)",
+                         "ns_ms": round(ns_ms, 3)},
             "elementwise": {"momentum_ms": round(mom_ms, 3), "momentum_gbs": round(mom_gbs, 1),
                             "update_ms": round(upd_ms, 3),
                             "update_gbs": round(my_elems * 6 / (upd_ms * 1e-3) / 1e9, 1) if upd_ms > 0 else 0.0,
