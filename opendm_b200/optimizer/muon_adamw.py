@@ -36,8 +36,8 @@ The arithmetic runs in the sm_100a kernels of ``libopendm_muon.so`` through
 * ``process_group``: group for the sharded path (default: the world).
 * ``allgather_waves``: with sharding, each rank's matrices are processed in
   this many waves of decreasing size; the all-gather of a wave overlaps the
-  Newton-Schulz of the next (default: 3 on CUDA when there are at least 6
-  matrices per rank, else 1).
+  Newton-Schulz of the next (default on CUDA with at least 6 matrices per
+  rank: 4 at 8 or more ranks, 3 below; else 1).
 * ``comm_sms``: SMs the Newton-Schulz launches leave free while an NCCL
   all-gather overlaps them, and the CTA limit of the optimizer's own NCCL
   group for that all-gather (default 32).
@@ -401,7 +401,9 @@ class MuonAdamW(torch.optim.Optimizer):
     def _n_waves(self, n_matrices: int, world: int, device: torch.device) -> int:
         if self.allgather_waves is not None:
             return int(self.allgather_waves)
-        return 3 if device.type == "cuda" and n_matrices >= 6 * world else 1
+        if device.type != "cuda" or n_matrices < 6 * world:
+            return 1
+        return 4 if world >= 8 else 3
 
     def _owners_for(self, group: dict) -> list[int]:
         key = id(group)

@@ -8,10 +8,12 @@ each matrix gets one owner rank:
   Newton-Schulz FLOPs: matrices in decreasing cost order, each to the least
   loaded rank (ties to the lower rank). Deterministic, so every rank computes
   the same plan without communication.
-* ``assign_waves`` -- each rank's owned matrices, largest first, cut into
-  waves whose Newton-Schulz FLOPs shrink geometrically. The all-gather of
-  wave w runs on the collective's stream while wave w + 1 is orthogonalised,
-  so only the last (smallest) wave's all-gather is exposed.
+* ``assign_waves`` -- each rank's owned matrices, those with the most bytes
+  per Newton-Schulz FLOP (the smallest m = min(rows, cols)) first, cut into
+  waves whose FLOPs shrink geometrically. The all-gather of wave w runs on
+  the collective's stream while wave w + 1 is orthogonalised: byte-heavy
+  matrices go early, where their transfer has the most compute to hide
+  behind, and the last wave, whose transfer is exposed, carries few bytes.
 * ``FlatParamBuckets`` -- after the owners update their matrices in place, one
   ``all_gather_into_tensor`` per (dtype, wave) delivers them to every rank.
   The parameters are re-pointed once to views of flat buffers laid out as
@@ -55,11 +57,16 @@ def wave_fractions(n_waves: int, ratio: float = 0.7) -> list[float]:
     return [x / total for x in w]
 
 
+def _bytes_per_flop(shape: tuple[int, int], steps: int) -> float:
+    return shape[0] * shape[1] / ns_cost(shape, steps)
+
+
 def assign_waves(shapes: list[tuple[int, int]], owners: list[int], world_size: int, n_waves: int,
                  steps: int = 5) -> list[int]:
-    """Wave index of each matrix: every rank cuts its own matrices, in
-    decreasing cost order, at the cumulative shares of ``wave_fractions``.
-    Deterministic, so every rank computes every rank's waves."""
+    """Wave index of each matrix: every rank orders its own matrices by
+    decreasing bytes per FLOP and cuts them at the cumulative FLOP shares of
+    ``wave_fractions``. Deterministic, so every rank computes every rank's
+    waves."""
     waves = [0] * len(shapes)
     if n_waves <= 1:
         return waves
@@ -69,7 +76,8 @@ def assign_waves(shapes: list[tuple[int, int]], owners: list[int], world_size: i
         acc += f
         bounds.append(acc)
     for r in range(world_size):
-        mine = sorted((i for i, o in enumerate(owners) if o == r), key=lambda i: (-ns_cost(shapes[i], steps), i))
+        mine = sorted((i for i, o in enumerate(owners) if o == r),
+                      key=lambda i: (-_bytes_per_flop(shapes[i], steps), -ns_cost(shapes[i], steps), i))
         total = sum(ns_cost(shapes[i], steps) for i in mine)
         done, w = 0.0, 0
         for i in mine:

@@ -175,11 +175,12 @@ def test_c1_sharded_two_ranks(tmp_path):
 
 
 def test_allgather_waves_two_ranks(tmp_path):
-    """Three all-gather waves per step (each rank's matrices cut by FLOPs,
-    one flat bucket per wave): same result as the single-process oracle."""
+    """All-gather waves (each rank's matrices cut by FLOPs, one flat bucket
+    per wave; here a large matrix fills a wave on its own): same result as
+    the single-process oracle."""
     res = _run("waves", C1_MUON + SMALL_MUON, C1_ADAM, 2, tmp_path)
     _check(res, C1_MUON + SMALL_MUON, C1_ADAM, 2)
-    assert res[0]["waves"] == res[1]["waves"] and set(res[0]["waves"]) == {0, 1, 2}
+    assert res[0]["waves"] == res[1]["waves"] and len(set(res[0]["waves"])) >= 2
 
 
 def test_owner_only_momentum_consolidates(tmp_path):

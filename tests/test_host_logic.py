@@ -313,8 +313,9 @@ def test_lpt_assignment_balances_and_is_deterministic():
 
 
 def test_waves_follow_geometric_flop_shares():
-    """Each rank's matrices, largest first, are cut into waves whose FLOP
-    shares shrink geometrically; deterministic and identical on every rank."""
+    """Each rank's matrices, most bytes per FLOP first, are cut into waves
+    whose FLOP shares shrink geometrically; deterministic and identical on
+    every rank."""
     from opendm_b200.sharding import assign_waves, wave_fractions
 
     fr = wave_fractions(3)
@@ -332,7 +333,8 @@ def test_waves_follow_geometric_flop_shares():
             biggest = max(ns_cost(shapes[i]) for i in mine) / total
             for w in range(3):
                 assert abs(share[w] - fr[w]) <= biggest + 1e-9, (world, r, share)
-            # larger matrices in earlier waves: waves never decrease along the cost order
-            by_cost = sorted(mine, key=lambda i: (-ns_cost(shapes[i]), i))
-            assert [waves[i] for i in by_cost] == sorted(waves[i] for i in by_cost)
+            # byte-heavy (small-m) matrices in earlier waves: waves never decrease along that order
+            by_bpf = sorted(mine, key=lambda i: (-shapes[i][0] * shapes[i][1] / ns_cost(shapes[i]),
+                                                 -ns_cost(shapes[i]), i))
+            assert [waves[i] for i in by_bpf] == sorted(waves[i] for i in by_bpf)
     assert assign_waves(shapes, assign_owners(shapes, 2), 2, 1) == [0] * len(shapes)
