@@ -21,8 +21,9 @@ Parameters bf16 ~ N(0, 0.02), gradients bf16 ~ N(0, 1e-3), fp32 optimizer state.
 Rank 0 prints one JSON line. `value` is the device time of one optimizer step
 (max over ranks, CUDA events, K steps after W warm-up steps). `e2e` is the
 same step measured through the public API with the gradients copied in from
-pinned host memory every step and a slice of the updated parameters read
-back. `roofline` is the Newton-Schulz GEMMs' dense FLOP rate against the
+pinned host memory every step (double-buffered: the next step's upload runs
+on a copy stream during the current step) and a slice of the updated
+parameters read back. `roofline` is the Newton-Schulz GEMMs' dense FLOP rate against the
 measured bf16 tensor peak (plus the FLOPs the tiles actually execute:
 256 x 256 tiles, upper triangle of symmetric products). The timed steps sit
 inside a CUDA profiler range (ncu --profile-from-start off captures only
@@ -447,13 +448,36 @@ def run_ours(args):
     h2d = sum(g.numel() * g.element_size() for g in host_grads.values())
     d2h = readback.numel() * readback.element_size()
     e2e_steps = max(2, min(args.steps, 5))
+    # Double-buffered input pipeline: step k+1's gradients upload on a copy
+    # stream into the other buffer set while step k runs; p.grad is pointed at
+    # the step's buffer set (as a data loader would hand over a new batch).
+    gbufs = [{i: torch.empty_like(grads[i]) for i in needed} for _ in range(2)]
+    copy_stream = torch.cuda.Stream(device)
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
+    cur = torch.cuda.current_stream(device)
     sync_all()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record()
-    for _ in range(e2e_steps):
-        for i, hg in host_grads.items():
-            params[i].grad.copy_(hg, non_blocking=True)
+    copy_stream.wait_stream(cur)
+
+    def upload(k):
+        with torch.cuda.stream(copy_stream):
+            if k >= 2:
+                copy_stream.wait_event(free[k % 2])  # step k-2 no longer reads this set
+            for i, hg in host_grads.items():
+                gbufs[k % 2][i].copy_(hg, non_blocking=True)
+            ready[k % 2].record(copy_stream)
+
+    upload(0)
+    for k in range(e2e_steps):
+        if k + 1 < e2e_steps:
+            upload(k + 1)
+        cur.wait_event(ready[k % 2])
+        for i in needed:
+            params[i].grad = gbufs[k % 2][i]
         opt.step()
+        free[k % 2].record(cur)
         readback.copy_(probe.detach().reshape(-1)[: readback.numel()], non_blocking=True)
     e_end.record()
     sync_all()
