@@ -471,14 +471,16 @@ def run_ours(args):
 
     upload(0)
     for k in range(e2e_steps):
-        if k + 1 < e2e_steps:
-            upload(k + 1)
         cur.wait_event(ready[k % 2])
         for i in needed:
             params[i].grad = gbufs[k % 2][i]
         opt.step()
         free[k % 2].record(cur)
         readback.copy_(probe.detach().reshape(-1)[: readback.numel()], non_blocking=True)
+        # queued after this step's own small host-to-device copies, so the copy
+        # engine serves those first and the next upload overlaps the step
+        if k + 1 < e2e_steps:
+            upload(k + 1)
     e_end.record()
     sync_all()
     e2e_ms = max_over_ranks(e_start.elapsed_time(e_end) / e2e_steps)

@@ -76,6 +76,27 @@ def _upload(raw: bytes, device: torch.device) -> torch.Tensor:
     return host.to(device, non_blocking=True)
 
 
+class _TableCache:
+    """Device copies of segment tables, reused while a table's bytes repeat
+    (the parameters and workspaces stay put, and gradient buffers are
+    usually reused), so a steady-state step issues no host-to-device copy
+    that could queue behind unrelated transfers."""
+
+    def __init__(self, device: torch.device, capacity: int = 64):
+        self.device, self.capacity = device, capacity
+        self._tables: dict[bytes, torch.Tensor] = {}
+
+    def get(self, raw: bytes) -> torch.Tensor:
+        t = self._tables.pop(raw, None)
+        if t is None:
+            t = _upload(raw, self.device)
+            while len(self._tables) >= self.capacity:
+                self._tables.pop(next(iter(self._tables)))
+        self._tables[raw] = t  # most recently used last
+        t.record_stream(torch.cuda.current_stream(self.device))  # reused later by kernels on this stream
+        return t
+
+
 class _ClassState:
     """Workspace and buffers of one shape class."""
 
@@ -147,6 +168,7 @@ class CudaMuonEngine:
         idx = self.device.index if self.device.index is not None else torch.cuda.current_device()
         N.check(self.lib.muon_device_check(idx), "muon_device_check")
         self._plans: dict = {}  # matrix-set key -> _PlanState, least recently used first
+        self._tables = _TableCache(self.device)
         # At most this many SMs per Newton-Schulz launch (0: all), leaving the
         # rest to a collective that overlaps it.
         self.sm_limit = 0
@@ -288,7 +310,7 @@ class CudaMuonEngine:
         for s in segs:
             s.chunk_begin = total
             total += int(self.lib.muon_momentum_chunks(s.rows, s.cols))
-        table = _upload(N.struct_bytes(segs), self.device)
+        table = self._tables.get(N.struct_bytes(segs))
         partials = torch.empty(max(total, 1), dtype=torch.float32, device=self.device)
         if dir_dtype is None:
             dir_dtype = N.MUON_F32 if self.op_dtype == N.MUON_F16 else self.op_dtype
@@ -380,7 +402,7 @@ class CudaMuonEngine:
             sg.param_dtype = cs.cls.u_dtype
             segs.append(sg)
             total += int(self.lib.muon_momentum_chunks(cs.rows, cs.cols))
-        table = _upload(N.struct_bytes(segs), self.device)
+        table = self._tables.get(N.struct_bytes(segs))
         ev = self._event_pair("update")
         N.check(self.lib.muon_apply_update(c_void_p(table.data_ptr()), len(segs), total, c_float(wd_factor),
                                            _stream_handle()), "muon_apply_update")
