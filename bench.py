@@ -451,7 +451,7 @@ def run_ours(args):
     # Double-buffered input pipeline: step k+1's gradients upload on a copy
     # stream into the other buffer set while step k runs; p.grad is pointed at
     # the step's buffer set (as a data loader would hand over a new batch).
-    gbufs = [{i: torch.empty_like(grads[i]) for i in needed} for _ in range(2)]
+    gbufs = [{i: grads[i] for i in needed}, {i: torch.empty_like(grads[i]) for i in needed}]
     copy_stream = torch.cuda.Stream(device)
     ready = [torch.cuda.Event() for _ in range(2)]
     free = [torch.cuda.Event() for _ in range(2)]

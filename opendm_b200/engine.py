@@ -121,6 +121,13 @@ class _ClassState:
         # fp16 stores X0 normalised and scaled by this power of two.
         self.x0_scale = float(lib.muon_ns_operand_scale(rows, cols, 0, op_dtype))
 
+    def last_x_read(self, steps: int) -> int:
+        """0 or 1: the X buffer (x0, x1) the last Newton-Schulz apply reads;
+        the other one is free when U is written."""
+        if int(self.cls.algo) == N.MUON_NS_GRAM:
+            return ((steps - 1) // 3) % 2  # segments of 3 iterations alternate x0, x1
+        return (steps - 1) % 2
+
     def x0_view(self, slot: int) -> torch.Tensor:
         """The stored Newton-Schulz input of matrix `slot` as a [rows, cols] tensor."""
         ld = int(self.cls.ld_x)
@@ -258,11 +265,21 @@ class CudaMuonEngine:
                 st.order[i] = (ci, slot)
                 st.seg_order.append(i)
             # U, rounded to the parameter dtype, for muon_apply_update; rows padded
-            # to 16 bytes for the epilogue's TMA stores.
+            # to 16 bytes for the epilogue's TMA stores. It goes into the X
+            # buffer that the last Newton-Schulz apply does not read when its
+            # rows fit there (bf16 U in either X type; fp32 U in tf32 X), else
+            # into a buffer of its own.
             ld_u = _pad16(c, dt)
-            cs.u_buf = torch.empty((len(idxs), r, ld_u), dtype=dt, device=self.device)
+            u_es = torch.empty((), dtype=dt).element_size()
+            cs.u_buf = None
+            if ns_steps >= 1 and ld_u * u_es <= int(cs.cls.ld_x) * cs.es:
+                cs.u_base = cs.cls.x1 if cs.last_x_read(ns_steps) == 0 else cs.cls.x0
+            else:
+                cs.u_buf = torch.empty((len(idxs), r, ld_u), dtype=dt, device=self.device)
+                cs.u_base = cs.u_buf.data_ptr()
+            cs.u_stride = r * ld_u * u_es  # bytes per matrix
             cs.cls.u_dtype = _dtype_code(items[idxs[0]].param)
-            cs.cls.u_out = c_void_p(cs.u_buf.data_ptr())
+            cs.cls.u_out = c_void_p(cs.u_base)
             cs.cls.ld_u = ld_u
             st.classes.append(cs)
         st.scales = torch.zeros(max(len(items), 1), dtype=torch.float32, device=self.device)
@@ -395,7 +412,7 @@ class CudaMuonEngine:
             cs = st.classes[ci]
             sg = N.UpdateSeg()
             sg.param = it.param.data_ptr()
-            sg.update = cs.u_buf[slot].data_ptr()
+            sg.update = cs.u_base + slot * cs.u_stride
             sg.rows, sg.cols, sg.ld = cs.rows, cs.cols, int(cs.cls.ld_u)
             sg.chunk_begin = total
             sg.eff = it.eff
