@@ -447,7 +447,7 @@ def run_ours(args):
     readback = torch.empty(min(probe.numel(), 4096), dtype=probe.dtype).pin_memory()
     h2d = sum(g.numel() * g.element_size() for g in host_grads.values())
     d2h = readback.numel() * readback.element_size()
-    e2e_steps = max(2, min(args.steps, 5))
+    e2e_steps = max(2, min(args.steps, 10))
     # Double-buffered input pipeline: step k+1's gradients upload on a copy
     # stream into the other buffer set while step k runs; p.grad is pointed at
     # the step's buffer set (as a data loader would hand over a new batch).

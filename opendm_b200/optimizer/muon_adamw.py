@@ -319,10 +319,16 @@ class MuonAdamW(torch.optim.Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
+        # Muon groups first, then AdamW: the groups update disjoint parameters,
+        # so the order changes no result, and the AdamW group's per-step
+        # host-to-device table copy (its bias corrections change every step)
+        # then comes last, where waiting behind other host-to-device transfers
+        # (e.g. the next batch's upload) delays nothing after it.
         for group in self.param_groups:
             if group.get("use_muon", False):
                 self._muon_step(group)
-            else:
+        for group in self.param_groups:
+            if not group.get("use_muon", False):
                 self._adamw_step(group)
         return loss
 
