@@ -456,31 +456,36 @@ def run_ours(args):
     ready = [torch.cuda.Event() for _ in range(2)]
     free = [torch.cuda.Event() for _ in range(2)]
     cur = torch.cuda.current_stream(device)
+
+    def pipeline(n_steps):
+        copy_stream.wait_stream(cur)
+
+        def upload(k):
+            with torch.cuda.stream(copy_stream):
+                if k >= 2:
+                    copy_stream.wait_event(free[k % 2])  # step k-2 no longer reads this set
+                for i, hg in host_grads.items():
+                    gbufs[k % 2][i].copy_(hg, non_blocking=True)
+                ready[k % 2].record(copy_stream)
+
+        upload(0)
+        for k in range(n_steps):
+            cur.wait_event(ready[k % 2])
+            for i in needed:
+                params[i].grad = gbufs[k % 2][i]
+            opt.step()
+            free[k % 2].record(cur)
+            readback.copy_(probe.detach().reshape(-1)[: readback.numel()], non_blocking=True)
+            # queued after this step's own small host-to-device copies, so the
+            # copy engine serves those first and the next upload overlaps the step
+            if k + 1 < n_steps:
+                upload(k + 1)
+
+    pipeline(2)  # warm-up: one pass per buffer set (first-use host work, table uploads)
     sync_all()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record()
-    copy_stream.wait_stream(cur)
-
-    def upload(k):
-        with torch.cuda.stream(copy_stream):
-            if k >= 2:
-                copy_stream.wait_event(free[k % 2])  # step k-2 no longer reads this set
-            for i, hg in host_grads.items():
-                gbufs[k % 2][i].copy_(hg, non_blocking=True)
-            ready[k % 2].record(copy_stream)
-
-    upload(0)
-    for k in range(e2e_steps):
-        cur.wait_event(ready[k % 2])
-        for i in needed:
-            params[i].grad = gbufs[k % 2][i]
-        opt.step()
-        free[k % 2].record(cur)
-        readback.copy_(probe.detach().reshape(-1)[: readback.numel()], non_blocking=True)
-        # queued after this step's own small host-to-device copies, so the copy
-        # engine serves those first and the next upload overlaps the step
-        if k + 1 < e2e_steps:
-            upload(k + 1)
+    pipeline(e2e_steps)
     e_end.record()
     sync_all()
     e2e_ms = max_over_ranks(e_start.elapsed_time(e_end) / e2e_steps)
