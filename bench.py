@@ -23,9 +23,10 @@ Rank 0 prints one JSON line. `value` is the device time of one optimizer step
 same step measured through the public API with the gradients copied in from
 pinned host memory every step (double-buffered: the next step's upload runs
 on a copy stream during the current step) and a slice of the updated
-parameters read back. `roofline` is the Newton-Schulz GEMMs' dense FLOP rate against the
-measured bf16 tensor peak (plus the FLOPs the tiles actually execute:
-256 x 256 tiles, upper triangle of symmetric products). The timed steps sit
+parameters read back. `roofline` is the Newton-Schulz GEMMs' algorithmic rate (the reference
+algorithm's dense FLOP count per NS second) against the measured bf16 tensor
+peak, plus the rate of the FLOPs the tiles actually execute (256 x 256 tiles,
+upper triangle of symmetric products, gram form where chosen). The timed steps sit
 inside a CUDA profiler range (ncu --profile-from-start off captures only
 them). `cpu_baseline` (N = 1, rank 0) is the numpy oracle
 of the reference algorithm on the host cores, timed on one matrix of every
@@ -510,16 +511,17 @@ def run_ours(args):
             "e2e": {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches) * args.steps,
             "roofline": {"bound": "tensor", "kernel": f"ns_gemm ({ns_launches} grouped launches per step)",
-                         "achieved": round(ns_exec_tflops, 1), "peak": peak, "unit": "TFLOP/s",
-                         "frac": round(ns_exec_tflops / peak, 4), "peak_source": f"{peaks['source']} bf16 sustained",
-                         "flops": ("executed tensor-core work of the algorithm each class runs (256x256 tiles, "
-                                   "K padded to 64, upper-triangle tiles of symmetric products)"),
+                         "achieved": round(ns_tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(ns_tflops / peak, 4), "peak_source": f"{peaks['source']} bf16 sustained",
+                         "flops": ("algorithmic: the reference's dense count steps*(4 m^2 n + 2 m^3) per matrix / "
+                                   "NS time. Above 1.0 because the gram form and the symmetric products execute "
+                                   "fewer FLOPs than that count; the tensor-core efficiency is executed_frac"),
+                         "executed_tflops": round(ns_exec_tflops, 1),
+                         "executed_frac": round(ns_exec_tflops / peak, 4),
+                         "executed_flops": ("MMA work issued: 256x256 tiles, K padded to 64, upper-triangle tiles "
+                                            "of symmetric products, per the algorithm each class runs"),
                          "executed_tflop_per_step": round(my_exec / 1e12, 2),
                          "ns_algorithms": {f"{r}x{c}": a for (r, c), a in sorted(algo_of.items())},
-                         "reference_dense_tflops": round(ns_tflops, 1),
-                         "reference_dense_note": ("the reference algorithm's dense count steps*(4 m^2 n + 2 m^3) "
-                                                  "per matrix / NS time: above the peak where the gram form and "
-                                                  "the symmetric products avoid work, not a tensor-core rate"),
                          "frac_of_tf32_peak": round(ns_tflops / (peak / 2), 4) if args.precision == "tf32" else None,
                          "mma_kind": "kind::tf32" if args.precision == "tf32" else "kind::f16",
                          "traffic": (NS_TRAFFIC_PER_LAUNCH[cfg] if cfg in NS_TRAFFIC_PER_LAUNCH and world == 1
@@ -534,6 +536,9 @@ def run_ours(args):
             "collective": ({"allgather_bytes_received": ag_bytes,
                             "allgather_alone_ms": round(ag_ms, 3),
                             "allgather_alone_gbs": round(ag_bytes / (ag_ms * 1e-3) / 1e9, 1) if ag_ms > 0 else 0.0,
+                            "allgather_frac_of_nvlink": (round(ag_bytes / (ag_ms * 1e-3) / 900e9, 4)
+                                                         if ag_ms > 0 else 0.0),
+                            "nvlink_peak_gbs": 900.0,
                             "waves": bucket.n_waves if bucket is not None else 1,
                             "transport": opt.allgather,
                             "comm_sms": opt.comm_sms if opt.allgather == "nccl" else 0,

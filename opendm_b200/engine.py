@@ -480,6 +480,119 @@ class CudaMuonEngine:
                        scratch.data_ptr(), dir_dtype=N.MUON_F32)
         return out
 
+    def directions_into(self, items: list, out: torch.Tensor, offsets: list[int], *, momentum: float,
+                        nesterov: bool) -> None:
+        """Momentum update of flat shards ``(grad or None, exp_avg)``, writing
+        each fp32 direction into ``out[offsets[k]:]`` (one launch per grad
+        dtype): the send buffer of the owner-only Newton-Schulz exchange."""
+        if not items:
+            return
+        by_dtype: dict[int, list] = {}
+        for (grad, exp_avg), off in zip(items, offsets):
+            seg = N.MomentumSeg()
+            g = grad.reshape(-1).contiguous() if grad is not None else None
+            seg.grad = g.data_ptr() if g is not None else None
+            seg.exp_avg = exp_avg.data_ptr()
+            seg.direction = out.data_ptr() + 4 * int(off)
+            n = exp_avg.numel()
+            seg.rows, seg.cols, seg.ld = 1, n, n
+            by_dtype.setdefault(_dtype_code(g) if g is not None else N.MUON_F32, []).append(seg)
+        scratch = torch.empty(len(items), dtype=torch.float32, device=self.device)
+        for code, segs in by_dtype.items():
+            self._momentum(segs, code, momentum, nesterov, scratch.data_ptr(), dir_dtype=N.MUON_F32)
+
+    def orthogonalize_many(self, mats: list[torch.Tensor], out_dtypes: list[torch.dtype], steps: int = 5,
+                           eps: float = 1e-7) -> list[torch.Tensor]:
+        """zeropower_via_newtonschulz5 of several fp32 matrices in one grouped
+        plan (classes by shape and output dtype); each result is rounded to its
+        ``out_dtypes`` entry (bf16 or fp32) by the last epilogue."""
+        if not mats:
+            return []
+        if steps < 1:
+            return [self.orthogonalize(m, steps=steps, eps=eps).to(dt) for m, dt in zip(mats, out_dtypes)]
+        groups: dict[tuple, list[int]] = {}
+        for i, (m, dt) in enumerate(zip(mats, out_dtypes)):
+            if m.ndim != 2 or m.dtype != torch.float32 or not m.is_contiguous() or m.device != self.device:
+                raise RuntimeError("orthogonalize_many takes contiguous fp32 matrices on the engine's device")
+            groups.setdefault((int(m.shape[0]), int(m.shape[1]), dt), []).append(i)
+        f16 = self.op_dtype == N.MUON_F16
+        classes, segs, convs, outs = [], [], [], [None] * len(mats)
+        scales = torch.zeros(len(mats), dtype=torch.float32, device=self.device)
+        staging = torch.empty(sum(m.numel() for m in mats), dtype=torch.float32, device=self.device) if f16 else None
+        keep = []
+        first, soff, chunks = 0, 0, 0
+        for (rows, cols, dt), idxs in groups.items():
+            cs = _ClassState(rows, cols, dt, len(idxs), self.op_dtype, self.device, int(steps), self._class_algo())
+            ld_u = _pad16(cols, dt)
+            u_buf = torch.empty((len(idxs), rows, ld_u), dtype=dt, device=self.device)
+            cs.cls.u_dtype, cs.cls.u_out, cs.cls.ld_u = _dtype_code(u_buf), c_void_p(u_buf.data_ptr()), ld_u
+            cs.cls.scales = c_void_p(scales.data_ptr() + 4 * first)
+            for slot, i in enumerate(idxs):
+                # momentum 0 with exp_avg aliasing the input: exp_avg = d = input,
+                # i.e. a copy into the operand buffer plus the Frobenius norm
+                seg = N.MomentumSeg()
+                seg.grad, seg.exp_avg = mats[i].data_ptr(), mats[i].data_ptr()
+                seg.rows, seg.cols = rows, cols
+                if f16:
+                    seg.direction, seg.ld = staging.data_ptr() + 4 * soff, cols
+                    cv = N.ConvertSeg()
+                    cv.src, cv.dst = seg.direction, cs.cls.x0 + slot * cs.x_stride
+                    cv.rows, cv.cols, cv.ld_src, cv.ld_dst = rows, cols, cols, int(cs.cls.ld_x)
+                    cv.chunk_begin, cv.mul, cv.scale_index = chunks, cs.x0_scale, first + slot
+                    convs.append(cv)
+                    chunks += int(self.lib.muon_momentum_chunks(rows, cols))
+                    soff += rows * cols
+                else:
+                    seg.direction, seg.ld = cs.cls.x0 + slot * cs.x_stride, int(cs.cls.ld_x)
+                segs.append(seg)
+                outs[i] = u_buf[slot, :, :cols]
+            classes.append(cs)
+            keep += [cs.workspace, u_buf]
+            first += len(idxs)
+        self._momentum(segs, N.MUON_F32, 0.0, False, scales.data_ptr(), eps=eps)
+        if f16:
+            table = _upload(N.struct_bytes(convs), self.device)
+            N.check(self.lib.muon_convert_f16(c_void_p(table.data_ptr()), len(convs), chunks,
+                                              c_void_p(scales.data_ptr()), _stream_handle()), "muon_convert_f16")
+            self.kernel_launches += 1
+            keep += [table, staging]
+        arr = (N.NsClass * len(classes))(*[cs.cls for cs in classes])
+        plan = c_void_p()
+        N.check(self.lib.muon_ns_plan_create(arr, len(classes), self.op_dtype, int(steps), byref(plan)),
+                "muon_ns_plan_create")
+        try:
+            N.check(self.lib.muon_ns_plan_run(plan, c_void_p(self._err.data_ptr()), _stream_handle()),
+                    "muon_ns_plan_run")
+            self.kernel_launches += int(self.lib.muon_ns_plan_launches(plan))
+        finally:
+            self.lib.muon_ns_plan_destroy(plan)
+        self._record_error_check()
+        stream = torch.cuda.current_stream(self.device)
+        for t in keep:  # workspaces stay valid until the queued kernels have run
+            t.record_stream(stream)
+        return outs
+
+    def apply_update_flat(self, items: list, wd_factor: float) -> None:
+        """Weight decay + p -= eff * u for flat shards ``(param, u, eff)``,
+        u in the parameter dtype (one launch)."""
+        if not items:
+            return
+        segs, total = [], 0
+        for param, u, eff in items:
+            n = param.numel()
+            if u.numel() != n or u.dtype != param.dtype:
+                raise RuntimeError("update shard does not match its parameter shard")
+            sg = N.UpdateSeg()
+            sg.param, sg.update = param.data_ptr(), u.data_ptr()
+            sg.rows, sg.cols, sg.ld = 1, n, n
+            sg.chunk_begin, sg.eff, sg.param_dtype = total, float(eff), _dtype_code(param)
+            segs.append(sg)
+            total += int(self.lib.muon_momentum_chunks(1, n))
+        table = _upload(N.struct_bytes(segs), self.device)
+        N.check(self.lib.muon_apply_update(c_void_p(table.data_ptr()), len(segs), total, c_float(wd_factor),
+                                           _stream_handle()), "muon_apply_update")
+        self.kernel_launches += 1
+
     def orthogonalize(self, matrix: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch.Tensor:
         """zeropower_via_newtonschulz5 on the GPU (reference muon_adamw.py:101-128): fp32 result."""
         if matrix.ndim != 2:

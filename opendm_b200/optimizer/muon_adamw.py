@@ -41,6 +41,12 @@ The arithmetic runs in the sm_100a kernels of ``libopendm_muon.so`` through
 * ``comm_sms``: SMs the Newton-Schulz launches leave free while an NCCL
   all-gather overlaps them, and the CTA limit of the optimizer's own NCCL
   group for that all-gather (default 32).
+* ``fsdp_owner_ns``: True (default): a matrix split into FSDP flat shards
+  over several ranks is orthogonalised once, by one owner among its active
+  ranks (FLOP-balanced), instead of by every active rank as in the reference
+  (``:400-414``): the fp32 direction shards go to the owner in one
+  all-to-all, the update shards (in the parameter dtype) come back in a
+  second. Same arithmetic; False restores the reference's gather-everywhere.
 * ``allgather``: "nccl" (default) or "p2p": the flat parameter buckets live
   in peer-mapped memory and each rank pulls its peers' buckets with
   copy-engine memcpys ordered by cross-GPU flags (``opendm_b200.p2p``), so
@@ -184,7 +190,7 @@ class MuonAdamW(torch.optim.Optimizer):
                  precision: str = "fp16", scale_mode: str = "reference", sharding: str = "auto",
                  state_sharding: bool = False, process_group=None, ns_algo: str = "auto",
                  allgather_waves: int | None = None, comm_sms: int = 32, allgather: str = "nccl",
-                 _engine=None) -> None:
+                 fsdp_owner_ns: bool = True, _engine=None) -> None:
         adamw_params, muon_params, muon_shapes, muon_names = [], [], [], []
         for param in model.parameters():
             if not param.requires_grad:
@@ -235,6 +241,7 @@ class MuonAdamW(torch.optim.Optimizer):
         if allgather not in ("nccl", "p2p"):
             raise ValueError(f"allgather must be 'nccl' or 'p2p', got {allgather!r}")
         self.allgather = allgather
+        self.fsdp_owner_ns = bool(fsdp_owner_ns)
         self.allgather_waves = allgather_waves
         self.comm_sms = max(int(comm_sms), 0)
 
@@ -478,6 +485,7 @@ class MuonAdamW(torch.optim.Optimizer):
         n_waves = (max(waves) + 1) if waves else 1
         owned = [[] for _ in range(n_waves)]
         others, partial, step_tensors = [], [], []
+        partial_local: dict[int, tuple] = {}  # matrix index -> (param, grad, state, eff), local shards only
         for index, (param, shape, plan) in enumerate(zip(group["params"], group["muon_shapes"], plans, strict=True)):
             if plan.local_numel == 0:
                 continue
@@ -493,6 +501,7 @@ class MuonAdamW(torch.optim.Optimizer):
                                shape, self.scale_mode)
             if plan.kind == "partial":
                 partial.append((param, grad, state, shape, plan, eff))
+                partial_local[index] = (param, grad, state, eff)
                 continue
             item = MatrixItem(param.data.view(shape), grad.detach().view(shape) if grad is not None else None,
                               state["exp_avg"].view(shape), eff)
@@ -534,9 +543,12 @@ class MuonAdamW(torch.optim.Optimizer):
                 if overlap:
                     engine.sm_limit = 0
         engine.momentum_only(others, momentum=momentum, nesterov=nesterov)
-        for param, grad, state, shape, plan, eff in partial:
-            self._partial_update(engine, param, grad, state, shape, plan, eff, momentum, nesterov, wd_factor,
-                                 ns_steps)
+        if self.fsdp_owner_ns and any(p.kind == "partial" for p in plans):
+            self._partial_owner_ns(engine, group, plans, partial_local, momentum, nesterov, wd_factor, ns_steps)
+        else:
+            for param, grad, state, shape, plan, eff in partial:
+                self._partial_update(engine, param, grad, state, shape, plan, eff, momentum, nesterov, wd_factor,
+                                     ns_steps)
         if sharded:
             ev = engine._event_pair("allgather_wait") if getattr(engine, "profile_events", None) is not None \
                 else None
@@ -546,6 +558,109 @@ class MuonAdamW(torch.optim.Optimizer):
                 buckets.finish()
             if ev is not None:
                 engine._event_end(ev)
+
+    @staticmethod
+    def _partial_owners(plans: list[MuonShardPlan], shapes, idx: list[int], steps: int) -> dict[int, int]:
+        """Owner rank of each partial matrix: LPT by Newton-Schulz FLOPs over
+        the matrix's active ranks (deterministic, identical on every rank)."""
+        from ..sharding import ns_cost
+
+        load: dict[int, float] = {}
+        owners: dict[int, int] = {}
+        for j in sorted(idx, key=lambda j: (-ns_cost(shapes[j], steps), j)):
+            r = min(plans[j].active_ranks, key=lambda r: (load.get(r, 0.0), r))
+            owners[j] = r
+            load[r] = load.get(r, 0.0) + ns_cost(shapes[j], steps)
+        return owners
+
+    def _partial_owner_ns(self, engine, group: dict, plans: list[MuonShardPlan], local: dict, momentum: float,
+                          nesterov: bool, wd_factor: float, ns_steps: int) -> None:
+        """Owner-only Newton-Schulz for matrices split into flat shards over
+        several ranks (the reference's `partial` plans, :400-414, orthogonalise
+        the gathered matrix on every active rank). Every rank takes part in
+        both exchanges, including ranks without a shard of some matrix."""
+        world, rank = dist.get_world_size(), dist.get_rank()
+        shapes = group["muon_shapes"]
+        idx = [j for j, p in enumerate(plans) if p.kind == "partial"]
+        owners = self._partial_owners(plans, shapes, idx, max(ns_steps, 1))
+        params = group["params"]
+        device = self._device_for_params(params)
+
+        def pad4(n):  # fp32 elements, so every shard starts 16-byte aligned
+            return (n + 3) // 4 * 4
+
+        # 1. momentum on the local shards, straight into the send buffer, by owner
+        send_sizes, items, offsets, cur = [0] * world, [], [], 0
+        for d in range(world):
+            for j in idx:
+                n = plans[j].sizes[rank]
+                if owners[j] != d or n == 0:
+                    continue
+                param, grad, state, _ = local[j]
+                items.append((grad.detach() if grad is not None else None, state["exp_avg"].view(-1)))
+                offsets.append(cur)
+                cur += pad4(n)
+                send_sizes[d] += pad4(n)
+        recv_sizes = [sum(pad4(plans[j].sizes[s]) for j in idx if owners[j] == rank and plans[j].sizes[s] > 0)
+                      for s in range(world)]
+        send = torch.empty(max(cur, 1), dtype=torch.float32, device=device)
+        recv = torch.empty(max(sum(recv_sizes), 1), dtype=torch.float32, device=device)
+        engine.directions_into(items, send, offsets, momentum=momentum, nesterov=nesterov)
+        dist.all_to_all_single(recv[:sum(recv_sizes)], send[:cur], recv_sizes, send_sizes)
+
+        # 2. the owner assembles its matrices (shards in rank order) and orthogonalises them together
+        mine = [j for j in idx if owners[j] == rank]
+        src_off = [sum(recv_sizes[:s]) for s in range(world)]
+        fulls = []
+        for j in mine:
+            full = torch.empty(plans[j].full_numel, dtype=torch.float32, device=device)
+            pos = 0
+            for s in range(world):
+                n = plans[j].sizes[s]
+                if n:
+                    full[pos:pos + n].copy_(recv[src_off[s]:src_off[s] + n])
+                    src_off[s] += pad4(n)
+                    pos += n
+            fulls.append(full.view(shapes[j]))
+        updates = engine.orthogonalize_many(fulls, [params[j].dtype for j in mine], steps=ns_steps)
+
+        # 3. update shards (parameter dtype) back to their ranks, as bytes
+        def pad16(b):
+            return (b + 15) // 16 * 16
+
+        def shard_bytes(j, s):
+            return plans[j].sizes[s] * params[j].element_size()
+
+        send2_sizes = [sum(pad16(shard_bytes(j, s)) for j in mine if plans[j].sizes[s] > 0) for s in range(world)]
+        recv2_sizes = [sum(pad16(shard_bytes(j, rank)) for j in idx if owners[j] == o and plans[j].sizes[rank] > 0)
+                       for o in range(world)]
+        send2 = torch.empty(max(sum(send2_sizes), 16), dtype=torch.uint8, device=device)
+        recv2 = torch.empty(max(sum(recv2_sizes), 16), dtype=torch.uint8, device=device)
+        pos = 0
+        flat_u = [u.contiguous().view(-1) for u in updates]
+        for s in range(world):
+            for j, u in zip(mine, flat_u):
+                n = plans[j].sizes[s]
+                if n == 0:
+                    continue
+                off = sum(plans[j].sizes[:s])
+                nb = shard_bytes(j, s)
+                send2[pos:pos + nb].view(params[j].dtype).copy_(u[off:off + n])
+                pos += pad16(nb)
+        dist.all_to_all_single(recv2[:sum(recv2_sizes)], send2[:sum(send2_sizes)], recv2_sizes, send2_sizes)
+
+        # 4. weight decay + update of the local shards
+        upd, pos = [], 0
+        for o in range(world):
+            for j in idx:
+                n = plans[j].sizes[rank]
+                if owners[j] != o or n == 0:
+                    continue
+                param, _, _, eff = local[j]
+                nb = shard_bytes(j, rank)
+                upd.append((param.data.view(-1), recv2[pos:pos + nb].view(param.dtype), eff))
+                pos += pad16(nb)
+        engine.apply_update_flat(upd, wd_factor)
 
     def _partial_update(self, engine, param, grad, state, shape, plan, eff, momentum, nesterov, wd_factor,
                         ns_steps) -> None:

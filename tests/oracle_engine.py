@@ -50,6 +50,26 @@ class OracleEngine:
         exp_avg.copy_(torch.from_numpy(m))
         return torch.from_numpy(d)
 
+    def directions_into(self, items, out, offsets, *, momentum, nesterov):
+        self.calls["direction"] += len(items)
+        for (grad, exp_avg), off in zip(items, offsets):
+            g = None if grad is None else _np(grad).reshape(-1)
+            m, d = O.momentum_direction(g, _np(exp_avg).reshape(-1), momentum, nesterov)
+            exp_avg.copy_(torch.from_numpy(m).view_as(exp_avg))
+            out[off:off + d.size].copy_(torch.from_numpy(d))
+
+    def orthogonalize_many(self, mats, out_dtypes, steps=5, eps=1e-7):
+        self.calls["orthogonalize"] += len(mats)
+        self.matrices_seen += len(mats)
+        return [torch.from_numpy(O.zeropower_via_newtonschulz5(_np(m), steps=steps, eps=eps)).to(dt)
+                for m, dt in zip(mats, out_dtypes)]
+
+    def apply_update_flat(self, items, wd_factor):
+        for param, u, eff in items:
+            p = O.apply_update_factor(_np(param), _np(u), wd_factor=wd_factor, eff=eff,
+                                      param_dtype=_dtype_name(param), device_semantics=self.sem)
+            param.copy_(torch.from_numpy(p).to(param.dtype))
+
     def orthogonalize(self, matrix, steps=5, eps=1e-7):
         self.calls["orthogonalize"] += 1
         return torch.from_numpy(O.zeropower_via_newtonschulz5(_np(matrix), steps=steps, eps=eps))

@@ -77,7 +77,7 @@ def _worker(rank, port, scenario, muon, adam, steps, outdir):
                     t._opendm_muon_name = f"m{i}"
                 model.register_parameter(f"p{i}", t)
             slices = None
-        else:  # flat shards: concatenate the Muon matrices, split evenly over the ranks
+        else:  # flat shards ("flat", "flat_ref"): concatenate the Muon matrices, split evenly over the ranks
             sizes = [int(np.prod(s)) for s in muon]
             total = sum(sizes)
             per = (total + WORLD - 1) // WORLD
@@ -99,7 +99,8 @@ def _worker(rank, port, scenario, muon, adam, steps, outdir):
         engine = OracleEngine()
         opt = MuonAdamW(model, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, _engine=engine,
                         state_sharding=(scenario in ("state_sharding", "waves")),
-                        allgather_waves=3 if scenario == "waves" else None)
+                        allgather_waves=3 if scenario == "waves" else None,
+                        fsdp_owner_ns=(scenario != "flat_ref"))
         plist = list(model.parameters())
         for s in range(steps):
             if scenario == "fail" and rank == 1 and s == 1:
@@ -189,9 +190,20 @@ def test_owner_only_momentum_consolidates(tmp_path):
 
 
 def test_flat_shards_partial_and_owner_only(tmp_path):
+    """FSDP-style flat shards: each matrix split over both ranks is
+    orthogonalised once, by its owner (direction shards in, update shards
+    out through two all-to-alls); same result as the single-process oracle."""
     res = _run("flat", SMALL_MUON, SMALL_ADAM, 2, tmp_path)
     kinds = set(res[0]["kinds"]) | set(res[1]["kinds"])
     assert "partial" in kinds and ("owner_only" in kinds or "empty" in kinds)
+    _check(res, SMALL_MUON, SMALL_ADAM, 2)
+    assert res[0]["muon_calls"] + res[1]["muon_calls"] == len(SMALL_MUON) * 2  # once per matrix and step
+
+
+def test_flat_shards_reference_gather_everywhere(tmp_path):
+    """fsdp_owner_ns=False: the reference's schedule (every active rank
+    gathers the direction and orthogonalises the whole matrix)."""
+    res = _run("flat_ref", SMALL_MUON, SMALL_ADAM, 2, tmp_path)
     _check(res, SMALL_MUON, SMALL_ADAM, 2)
 
 

@@ -120,3 +120,86 @@ def test_two_gpu_sharded_equals_unsharded(tmp_path):
                 assert torch.equal(got, want), (r["rank"], name, "param", i)
             for i, (got, want) in enumerate(zip(run["exp_avg"], ref["exp_avg"])):
                 assert torch.equal(got, want), (r["rank"], name, "exp_avg", i)
+
+
+def _flat_worker(rank, port, outdir):
+    """Each rank holds FSDP-style flat shards (the concatenated Muon matrices
+    split evenly over the ranks): owner-only and reference (gather
+    everywhere) schedules, and the unsharded model for comparison."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from opendm_b200.optimizer import MuonAdamW
+
+    result = {"rank": rank}
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=timedelta(seconds=60), device_id=dev)
+        g = torch.Generator(device=dev).manual_seed(21)
+        full = [(torch.randn(s, generator=g, device=dev) * 0.02).to(torch.bfloat16) for s in MUON]
+        grads = [[(torch.randn(s, generator=g, device=dev) * 1e-3).to(torch.bfloat16) for s in MUON]
+                 for _ in range(STEPS)]
+        sizes = [int(torch.tensor(s).prod()) for s in MUON]
+        total = sum(sizes)
+        per = (total + WORLD - 1) // WORLD
+        lo, hi = rank * per, min((rank + 1) * per, total)
+        slices, off = [], 0
+        for n in sizes:
+            a, b = max(lo, off), min(hi, off + n)
+            slices.append((a - off, b - off) if b > a else (0, 0))
+            off += n
+        runs = {}
+        for name in ("owner", "reference", "full"):
+            model = torch.nn.Module()
+            for i, (t, shape) in enumerate(zip(full, MUON)):
+                a, b = slices[i]
+                data = t.clone() if name == "full" else t.reshape(-1)[a:b].clone()
+                prm = torch.nn.Parameter(data)
+                prm._opendm_muon_shape = tuple(shape)
+                prm._opendm_muon_name = f"m{i}"
+                model.register_parameter(f"p{i}", prm)
+            opt = MuonAdamW(model, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01,
+                            sharding="off", fsdp_owner_ns=(name == "owner"))
+            for s in range(STEPS):
+                for i, prm in enumerate(model.parameters()):
+                    a, b = slices[i]
+                    prm.grad = grads[s][i].clone() if name == "full" else grads[s][i].reshape(-1)[a:b].clone()
+                opt.step()
+            opt.check_device_errors()
+            kinds = [p.kind for p in opt._get_muon_shard_plans(opt.param_groups[1])]
+            runs[name] = {"params": [p.detach().reshape(-1).cpu() for p in model.parameters()], "kinds": kinds}
+        result.update(runs=runs, slices=slices)
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as exc:  # reported to the parent
+        result["error"] = f"{type(exc).__name__}: {exc}"
+        result["trace"] = traceback.format_exc()
+    torch.save(result, os.path.join(outdir, f"flat{rank}.pt"))
+
+
+def test_two_gpu_flat_shards_owner_ns_equals_unsharded(tmp_path):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
+        pytest.skip("needs two CUDA devices")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    port = _port()
+    procs = [ctx.Process(target=_flat_worker, args=(r, port, str(tmp_path))) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("rank did not finish")
+    res = [torch.load(os.path.join(tmp_path, f"flat{r}.pt"), weights_only=False) for r in range(WORLD)]
+    for r in res:
+        assert "error" not in r, r.get("trace")
+        assert "partial" in r["runs"]["owner"]["kinds"]
+        for name in ("owner", "reference"):
+            for i, (got, want) in enumerate(zip(r["runs"][name]["params"], r["runs"]["full"]["params"])):
+                a, b = r["slices"][i]
+                assert torch.equal(got, want[a:b]), (r["rank"], name, i)
