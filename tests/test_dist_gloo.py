@@ -54,7 +54,7 @@ def _oracle(muon, adam, steps):
     return final, exp_avg
 
 
-def _worker(rank, port, scenario, muon, adam, steps, outdir):
+def _worker(rank, port, scenario, muon, adam, steps, outdir, world=WORLD):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.set_num_threads(2)
@@ -65,7 +65,7 @@ def _worker(rank, port, scenario, muon, adam, steps, outdir):
 
     result = {"rank": rank}
     try:
-        dist.init_process_group("gloo", rank=rank, world_size=WORLD, timeout=timedelta(seconds=20))
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
         params, grads = _data(muon, adam, steps)
         model = torch.nn.Module()
         n_muon = len(muon)
@@ -80,7 +80,7 @@ def _worker(rank, port, scenario, muon, adam, steps, outdir):
         else:  # flat shards ("flat", "flat_ref"): concatenate the Muon matrices, split evenly over the ranks
             sizes = [int(np.prod(s)) for s in muon]
             total = sum(sizes)
-            per = (total + WORLD - 1) // WORLD
+            per = (total + world - 1) // world
             lo, hi = rank * per, min((rank + 1) * per, total)
             slices = []
             off = 0
@@ -119,7 +119,9 @@ def _worker(rank, port, scenario, muon, adam, steps, outdir):
                              else np.zeros(0, np.float32) for p in plist[:n_muon]]
         result["slices"] = slices
         result["muon_calls"] = engine.matrices_seen
-        result["kinds"] = [pl.kind for pl in opt._get_muon_shard_plans(opt.param_groups[1])]
+        plans = opt._get_muon_shard_plans(opt.param_groups[1])
+        result["kinds"] = [pl.kind for pl in plans]
+        result["partial_active"] = [len(pl.active_ranks) for pl in plans if pl.kind == "partial"]
         result["waves"] = opt._waves.get(id(opt.param_groups[1]))
         dist.barrier()
         dist.destroy_process_group()
@@ -131,11 +133,11 @@ def _worker(rank, port, scenario, muon, adam, steps, outdir):
     torch.save(result, os.path.join(outdir, f"rank{rank}.pt"))
 
 
-def _run(scenario, muon, adam, steps, tmp_path):
+def _run(scenario, muon, adam, steps, tmp_path, world=WORLD):
     ctx = mp.get_context("spawn")
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, port, scenario, muon, adam, steps, str(tmp_path)))
-             for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker, args=(r, port, scenario, muon, adam, steps, str(tmp_path), world))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -143,7 +145,7 @@ def _run(scenario, muon, adam, steps, tmp_path):
         if p.is_alive():
             p.kill()
             pytest.fail("rank did not finish")
-    return [torch.load(os.path.join(tmp_path, f"rank{r}.pt"), weights_only=False) for r in range(WORLD)]
+    return [torch.load(os.path.join(tmp_path, f"rank{r}.pt"), weights_only=False) for r in range(world)]
 
 
 def _check(res, muon, adam, steps, check_exp_avg=True):
@@ -198,6 +200,19 @@ def test_flat_shards_partial_and_owner_only(tmp_path):
     assert "partial" in kinds and ("owner_only" in kinds or "empty" in kinds)
     _check(res, SMALL_MUON, SMALL_ADAM, 2)
     assert res[0]["muon_calls"] + res[1]["muon_calls"] == len(SMALL_MUON) * 2  # once per matrix and step
+
+
+def test_flat_shards_three_ranks(tmp_path):
+    """World size 3: matrices split over two of the three ranks (the third
+    has no shard of them, and some ranks own nothing), plus whole-matrix
+    owners; every rank takes part in both all-to-alls."""
+    muon = SMALL_MUON + [(40, 90), (128, 64)]
+    res = _run("flat", muon, SMALL_ADAM, 2, tmp_path, world=3)
+    _check(res, muon, SMALL_ADAM, 2)
+    assert sum(r["muon_calls"] for r in res) == len(muon) * 2
+    kinds = set().union(*(set(r["kinds"]) for r in res))
+    assert {"partial", "owner_only"} <= kinds
+    assert min(res[0]["partial_active"]) < 3  # some split matrix has a rank without a shard
 
 
 def test_flat_shards_reference_gather_everywhere(tmp_path):
