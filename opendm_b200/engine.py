@@ -4,14 +4,19 @@ The optimizer (``opendm_b200.optimizer.MuonAdamW``) hands the engine lists of
 whole matrices it must update and the AdamW-group tensors. The engine
 
 * groups matrices by (rows, cols, param dtype) into shape classes; each class
-  owns one workspace holding the Newton-Schulz operands X (ping-pong), A' and
-  M for all its matrices, stacked so one grouped launch covers the class;
-* caches the Newton-Schulz plan (tensor maps, tile schedules) while the
-  parameters stay at the same addresses; only the gradient pointers change
-  between steps, so the per-step host work is one small segment table;
-* launches (a) momentum + Frobenius scale, (b) 3 x ns_steps grouped
-  tcgen05 GEMMs whose last epilogue applies (c) weight decay and the scaled
-  update in place, and the fused AdamW kernel, all on the current CUDA stream.
+  owns one workspace holding the Newton-Schulz operands (X ping-pong, A', B',
+  M, and for the gram form A, P A and Q) for all its matrices, stacked so one
+  grouped launch covers every class; the class's Newton-Schulz form (iterate
+  on X, or on the gram matrix) is the library's choice by executed FLOPs;
+* caches one plan state (workspaces, tensor maps, tile schedules) per matrix
+  set, e.g. per all-gather wave, while the parameters stay at the same
+  addresses, and device copies of segment tables while their bytes repeat,
+  so a steady-state step uploads only the AdamW table;
+* launches (a) momentum + Frobenius scale (+ the fp16 operand conversion),
+  (b) the grouped tcgen05 Newton-Schulz launches (3 per iteration, plus one
+  per gram segment) whose last epilogue writes U in the parameter dtype,
+  (c) weight decay + the scaled update, and the fused AdamW kernel, all on
+  the current CUDA stream.
 
 There is no fallback: every entry point raises if the library is missing or
 the tensors are not on an sm_100 device.
