@@ -534,14 +534,16 @@ class MuonAdamW(torch.optim.Optimizer):
                 ag_group = self._allgather_group(device)
                 overlap = device.type == "cuda" and n_waves > 1 and hasattr(engine, "sm_limit")
                 total_sms = torch.cuda.get_device_properties(device).multi_processor_count if overlap else 0
-                for w in range(n_waves):
+                try:
+                    for w in range(n_waves):
+                        if overlap:
+                            engine.sm_limit = max(total_sms - self.comm_sms, 2) if w > 0 else 0
+                        engine.muon_matrices(owned[w], momentum=momentum, nesterov=nesterov,
+                                             weight_decay_factor=wd_factor, ns_steps=ns_steps)
+                        handles += buckets.sync(wave=w, async_op=device.type == "cuda", group=ag_group)
+                finally:
                     if overlap:
-                        engine.sm_limit = max(total_sms - self.comm_sms, 2) if w > 0 else 0
-                    engine.muon_matrices(owned[w], momentum=momentum, nesterov=nesterov,
-                                         weight_decay_factor=wd_factor, ns_steps=ns_steps)
-                    handles += buckets.sync(wave=w, async_op=device.type == "cuda", group=ag_group)
-                if overlap:
-                    engine.sm_limit = 0
+                        engine.sm_limit = 0
         engine.momentum_only(others, momentum=momentum, nesterov=nesterov)
         if self.fsdp_owner_ns and any(p.kind == "partial" for p in plans):
             self._partial_owner_ns(engine, group, plans, partial_local, momentum, nesterov, wd_factor, ns_steps)
