@@ -263,6 +263,34 @@ int muon_ns_choose_algo(int32_t rows, int32_t cols, int op_dtype, int steps);
  * muon_ns_class_workspace_bytes() bytes. */
 int muon_ns_class_layout(muon_ns_class* cls, void* base, int op_dtype);
 
+/* ------------------------------------------- (e) gradient-norm clipping
+ * Replaces the clipping the reference's trainer runs before every step
+ * (opendm/trainer/trainer.py:213, max_grad_norm = 1.0, through
+ * torch.nn.utils.clip_grad_norm_), folded into the step: muon_clip_grad_norm
+ * reads the gradients once and computes, on the device, torch's total norm
+ * (per-tensor norms rounded to each gradient's dtype, their 2-norm rounded to
+ * bf16 when every gradient is bf16, else fp32) and the coefficient
+ * min(max_norm / (total + 1e-6), 1) with torch's rounding; out_dev[0] = total,
+ * out_dev[1] = coefficient. muon_momentum_scaled and muon_adamw_scaled then
+ * multiply each gradient by *grad_scale_dev as they read it (rounded to the
+ * gradient's dtype, as torch's in-place multiply rounds it), so the gradients
+ * are never rewritten. partials_dev: total_chunks floats (total_chunks = the
+ * sum of muon_norm_chunks(numel) over the segments; chunk_begin its prefix). */
+typedef struct muon_norm_seg {
+  const void* grad; /* numel elements of dtype */
+  int64_t numel;
+  int64_t chunk_begin;
+  int32_t dtype; /* MUON_BF16 or MUON_F32 */
+  int32_t reserved;
+} muon_norm_seg;
+
+int64_t muon_norm_chunks(int64_t numel);
+int muon_clip_grad_norm(const muon_norm_seg* segs_dev, int n_segs, int64_t total_chunks, float max_norm,
+                        float* partials_dev, float* out_dev, void* stream);
+int muon_momentum_scaled(const muon_momentum_seg* segs_dev, int n_segs, int64_t total_chunks, int grad_dtype,
+                         int dir_dtype, float momentum, int nesterov, float eps, float* partials_dev,
+                         float* scales_dev, const float* grad_scale_dev, void* stream);
+
 /* ------------------------------- (d') cross-GPU flags for the all-gather
  * The sharded step moves the owners' updated parameters between GPUs with
  * cudaMemcpyAsync over NVLink (copy engines, no SMs) out of peer-mapped
@@ -339,6 +367,11 @@ int64_t muon_adamw_chunks(int64_t numel);
 
 int muon_adamw(const muon_adamw_seg* segs_dev, int n_segs, int64_t total_chunks, double beta1,
                double beta2, float eps, float wd_factor, void* stream);
+
+/* muon_adamw with each gradient multiplied by *grad_scale_dev as it is read
+ * (gradient-norm clipping, section (e)). */
+int muon_adamw_scaled(const muon_adamw_seg* segs_dev, int n_segs, int64_t total_chunks, double beta1, double beta2,
+                      float eps, float wd_factor, const float* grad_scale_dev, void* stream);
 
 #ifdef __cplusplus
 }

@@ -89,6 +89,11 @@ class FlagList(Structure):
     _fields_ = [("ptr", c_void_p * MUON_MAX_FLAGS), ("n", c_int32)]
 
 
+class NormSeg(Structure):
+    _fields_ = [("grad", c_void_p), ("numel", c_int64), ("chunk_begin", c_int64), ("dtype", c_int32),
+                ("reserved", c_int32)]
+
+
 class UpdateSeg(Structure):
     _fields_ = [
         ("param", c_void_p),
@@ -138,6 +143,12 @@ SIGNATURES = {
     "muon_ns_plan_launches": (c_int, [c_void_p]),
     "muon_ns_plan_set_sm_limit": (c_int, [c_void_p, c_int]),
     "muon_flags_set": (c_int, [POINTER(FlagList), c_uint32, c_void_p]),
+    "muon_norm_chunks": (c_int64, [c_int64]),
+    "muon_clip_grad_norm": (c_int, [c_void_p, c_int, c_int64, c_float, c_void_p, c_void_p, c_void_p]),
+    "muon_momentum_scaled": (c_int, [c_void_p, c_int, c_int64, c_int, c_int, c_float, c_int, c_float, c_void_p,
+                                     c_void_p, c_void_p, c_void_p]),
+    "muon_adamw_scaled": (c_int, [c_void_p, c_int, c_int64, c_double, c_double, c_float, c_float, c_void_p,
+                                  c_void_p]),
     "muon_flags_wait": (c_int, [POINTER(FlagList), c_uint32, c_int64, c_void_p, c_void_p]),
     "muon_ns_class_workspace_bytes": (c_int64, [c_int32, c_int32, c_int32, c_int, c_int]),
     "muon_ns_choose_algo": (c_int, [c_int32, c_int32, c_int, c_int]),

@@ -47,9 +47,16 @@ __device__ __forceinline__ float adam_elem(float p, float g, float& m, float& v,
   return __fadd_rn(p, __fmul_rn(neg_step, __fdiv_rn(m, denom)));
 }
 
+// Gradient-norm clipping folded into the read (clip.cu): g' = g * coef,
+// rounded to the gradient's dtype.
+__device__ __forceinline__ float clip_grad_adam(float g, float coef, bool bf) {
+  return bf ? bf16_round(g * coef) : g * coef;
+}
+
 __global__ void __launch_bounds__(ADAM_THREADS) adamw_kernel(const muon_adamw_seg* __restrict__ segs, int n_segs,
                                                              float beta1w, float beta2, float one_minus_beta2,
-                                                             float eps, float wd_factor) {
+                                                             float eps, float wd_factor,
+                                                             const float* __restrict__ grad_scale) {
   const int64_t chunk = blockIdx.x;
   const muon_adamw_seg sg = segs[find_adam_segment(segs, n_segs, chunk)];
   const int64_t e0 = (chunk - sg.chunk_begin) * ADAM_CHUNK;
@@ -84,6 +91,11 @@ __global__ void __launch_bounds__(ADAM_THREADS) adamw_kernel(const muon_adamw_se
         const float4 a = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(sg.grad) + e));
         g[0] = a.x, g[1] = a.y, g[2] = a.z, g[3] = a.w;
       }
+      if (grad_scale != nullptr) {
+        const float coef = *grad_scale;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) g[i] = clip_grad_adam(g[i], coef, gbf);
+      }
       float4 m4 = *reinterpret_cast<float4*>(sg.exp_avg + e);
       float4 v4 = *reinterpret_cast<float4*>(sg.exp_avg_sq + e);
       float m[4] = {m4.x, m4.y, m4.z, m4.w}, v[4] = {v4.x, v4.y, v4.z, v4.w};
@@ -107,8 +119,9 @@ __global__ void __launch_bounds__(ADAM_THREADS) adamw_kernel(const muon_adamw_se
     for (int64_t e = e0 + threadIdx.x; e < e1; e += ADAM_THREADS) {
       float p = pbf ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sg.param)[e])
                     : reinterpret_cast<const float*>(sg.param)[e];
-      const float g = gbf ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sg.grad)[e])
-                          : reinterpret_cast<const float*>(sg.grad)[e];
+      float g = gbf ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sg.grad)[e])
+                    : reinterpret_cast<const float*>(sg.grad)[e];
+      if (grad_scale != nullptr) g = clip_grad_adam(g, *grad_scale, gbf);
       float m = sg.exp_avg[e], v = sg.exp_avg_sq[e];
       p = adam_elem(p, g, m, v, beta1w, beta2, one_minus_beta2, eps, wd_factor, neg_step, sg.bc2_sqrt, pbf);
       sg.exp_avg[e] = m;
@@ -122,7 +135,7 @@ __global__ void __launch_bounds__(ADAM_THREADS) adamw_kernel(const muon_adamw_se
 }
 
 int launch_adamw(const muon_adamw_seg* segs_dev, int n_segs, int64_t total_chunks, double beta1, double beta2,
-                 float eps, float wd_factor, cudaStream_t stream) {
+                 float eps, float wd_factor, const float* grad_scale, cudaStream_t stream) {
   if (n_segs <= 0 || total_chunks <= 0) return MUON_OK;
   if (!segs_dev) return set_error(MUON_ERR_ARG, "null AdamW segment table");
   if (total_chunks > 0x7fffffffLL) return set_error(MUON_ERR_ARG, "too many AdamW chunks");
@@ -131,7 +144,8 @@ int launch_adamw(const muon_adamw_seg* segs_dev, int n_segs, int64_t total_chunk
   const float beta1w = static_cast<float>(1.0 - beta1);
   const float omb2 = static_cast<float>(1.0 - beta2);
   adamw_kernel<<<static_cast<unsigned>(total_chunks), ADAM_THREADS, 0, stream>>>(segs_dev, n_segs, beta1w,
-                                                                                 static_cast<float>(beta2), omb2, eps, wd_factor);
+                                                                                 static_cast<float>(beta2), omb2, eps, wd_factor,
+                                                                                 grad_scale);
   if (check_cuda(cudaGetLastError(), "adamw launch")) return MUON_ERR_CUDA;
   return MUON_OK;
 }

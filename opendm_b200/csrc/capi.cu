@@ -95,7 +95,14 @@ int muon_momentum(const muon_momentum_seg* segs_dev, int n_segs, int64_t total_c
                   int dir_dtype, float momentum, int nesterov, float eps, float* partials_dev,
                   float* scales_dev, void* stream) {
   return muon::launch_momentum(segs_dev, n_segs, total_chunks, grad_dtype, dir_dtype, momentum, nesterov,
-                               eps, partials_dev, scales_dev, static_cast<cudaStream_t>(stream));
+                               eps, partials_dev, scales_dev, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int muon_momentum_scaled(const muon_momentum_seg* segs_dev, int n_segs, int64_t total_chunks, int grad_dtype,
+                         int dir_dtype, float momentum, int nesterov, float eps, float* partials_dev,
+                         float* scales_dev, const float* grad_scale_dev, void* stream) {
+  return muon::launch_momentum(segs_dev, n_segs, total_chunks, grad_dtype, dir_dtype, momentum, nesterov,
+                               eps, partials_dev, scales_dev, grad_scale_dev, static_cast<cudaStream_t>(stream));
 }
 
 int muon_momentum_single_noalloc(const void* grad, float* exp_avg, void* direction, int64_t rows, int64_t cols,
@@ -159,8 +166,22 @@ int64_t muon_adamw_chunks(int64_t numel) { return muon::adamw_chunks(numel); }
 
 int muon_adamw(const muon_adamw_seg* segs_dev, int n_segs, int64_t total_chunks, double beta1, double beta2,
                float eps, float wd_factor, void* stream) {
-  return muon::launch_adamw(segs_dev, n_segs, total_chunks, beta1, beta2, eps, wd_factor,
+  return muon::launch_adamw(segs_dev, n_segs, total_chunks, beta1, beta2, eps, wd_factor, nullptr,
                             static_cast<cudaStream_t>(stream));
+}
+
+int muon_adamw_scaled(const muon_adamw_seg* segs_dev, int n_segs, int64_t total_chunks, double beta1, double beta2,
+                      float eps, float wd_factor, const float* grad_scale_dev, void* stream) {
+  return muon::launch_adamw(segs_dev, n_segs, total_chunks, beta1, beta2, eps, wd_factor, grad_scale_dev,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int64_t muon_norm_chunks(int64_t numel) { return muon::norm_chunks(numel); }
+
+int muon_clip_grad_norm(const muon_norm_seg* segs_dev, int n_segs, int64_t total_chunks, float max_norm,
+                        float* partials_dev, float* out_dev, void* stream) {
+  return muon::launch_clip_grad_norm(segs_dev, n_segs, total_chunks, max_norm, partials_dev, out_dev,
+                                     static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

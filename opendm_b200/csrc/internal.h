@@ -16,14 +16,17 @@ int check_cuda(cudaError_t e, const char* what);
 
 int launch_momentum(const muon_momentum_seg* segs_dev, int n_segs, int64_t total_chunks,
                     int grad_dtype, int dir_dtype, float momentum, int nesterov, float eps,
-                    float* partials_dev, float* scales_dev, cudaStream_t stream);
+                    float* partials_dev, float* scales_dev, const float* grad_scale, cudaStream_t stream);
 int64_t momentum_chunks(int64_t rows, int64_t cols);
 int launch_momentum_single_noalloc(const void* grad, float* exp_avg, void* direction, int64_t rows, int64_t cols,
                                    int64_t ld, int grad_dtype, int dir_dtype, float momentum, int nesterov,
                                    float eps, float* scale_out, cudaStream_t stream);
 
 int launch_adamw(const muon_adamw_seg* segs_dev, int n_segs, int64_t total_chunks, double beta1,
-                 double beta2, float eps, float wd_factor, cudaStream_t stream);
+                 double beta2, float eps, float wd_factor, const float* grad_scale, cudaStream_t stream);
+int64_t norm_chunks(int64_t numel);
+int launch_clip_grad_norm(const muon_norm_seg* segs_dev, int n_segs, int64_t total_chunks, float max_norm,
+                          float* partials_dev, float* out_dev, cudaStream_t stream);
 int64_t adamw_chunks(int64_t numel);
 
 int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, int steps,

@@ -92,10 +92,18 @@ __device__ __forceinline__ void store_dir8(void* dir, int64_t e, const float (&d
   }
 }
 
+// Gradient-norm clipping folded into the read (clip.cu): g' = g * coef,
+// rounded to the gradient's dtype as torch's in-place multiply rounds it.
+template <int kGradDt>
+__device__ __forceinline__ float clip_grad(float g, float coef) {
+  return kGradDt == MUON_BF16 ? bf16_round(g * coef) : g * coef;
+}
+
 template <int kGradDt, int kDirDt>
 __global__ void __launch_bounds__(MOM_THREADS) momentum_kernel(const muon_momentum_seg* __restrict__ segs,
                                                                int n_segs, float mu, int nesterov,
-                                                               float* __restrict__ partials) {
+                                                               float* __restrict__ partials,
+                                                               const float* __restrict__ grad_scale) {
   __shared__ float red[MOM_THREADS / 32];
   const int64_t chunk = blockIdx.x;
   const int s = find_segment(segs, n_segs, chunk);
@@ -115,6 +123,11 @@ __global__ void __launch_bounds__(MOM_THREADS) momentum_kernel(const muon_moment
       if (e >= e1) break;
       float g[8];
       load_grad8<kGradDt, kDirDt>(sg.grad, e, g);
+      if (grad_scale != nullptr && sg.grad != nullptr) {
+        const float coef = *grad_scale;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) g[i] = clip_grad<kGradDt>(g[i], coef);
+      }
       float4* mp = reinterpret_cast<float4*>(sg.exp_avg + e);
       const float4 m0 = mp[0], m1 = mp[1];
       const float mo[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
@@ -138,6 +151,7 @@ __global__ void __launch_bounds__(MOM_THREADS) momentum_kernel(const muon_moment
           g = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sg.grad)[e]);
         else
           g = reinterpret_cast<const float*>(sg.grad)[e];
+        if (grad_scale != nullptr) g = clip_grad<kGradDt>(g, *grad_scale);
       }
       const MomOut o = mom_op(g, sg.exp_avg[e], mu, nest);
       sg.exp_avg[e] = o.m;
@@ -188,7 +202,7 @@ __global__ void momentum_scale_kernel(const muon_momentum_seg* __restrict__ segs
 
 int launch_momentum(const muon_momentum_seg* segs_dev, int n_segs, int64_t total_chunks, int grad_dtype,
                     int dir_dtype, float momentum, int nesterov, float eps, float* partials_dev,
-                    float* scales_dev, cudaStream_t stream) {
+                    float* scales_dev, const float* grad_scale, cudaStream_t stream) {
   if (n_segs <= 0) return MUON_OK;
   if (!segs_dev || !partials_dev || !scales_dev) return set_error(MUON_ERR_ARG, "null momentum buffer");
   if (grad_dtype != MUON_BF16 && grad_dtype != MUON_F32)
@@ -199,7 +213,8 @@ int launch_momentum(const muon_momentum_seg* segs_dev, int n_segs, int64_t total
   if (total_chunks > 0) {
     const dim3 grid(static_cast<unsigned>(total_chunks));
 #define MUON_MOM_LAUNCH(G, D) \
-  momentum_kernel<G, D><<<grid, MOM_THREADS, 0, stream>>>(segs_dev, n_segs, momentum, nesterov, partials_dev)
+  momentum_kernel<G, D><<<grid, MOM_THREADS, 0, stream>>>(segs_dev, n_segs, momentum, nesterov, partials_dev, \
+                                                          grad_scale)
     if (grad_dtype == MUON_BF16) {
       if (dir_dtype == MUON_BF16) MUON_MOM_LAUNCH(MUON_BF16, MUON_BF16);
       else if (dir_dtype == MUON_TF32) MUON_MOM_LAUNCH(MUON_BF16, MUON_TF32);

@@ -188,6 +188,9 @@ class CudaMuonEngine:
         self._err_host = torch.zeros(1, dtype=torch.int32).pin_memory()
         self._err_event = None
         self.kernel_launches = 0  # launches issued by this engine (for benchmarks)
+        # Device float (or None): gradient-norm clipping coefficient that the
+        # momentum and AdamW kernels apply to every gradient they read.
+        self.grad_scale: torch.Tensor | None = None
         self.ns_launches_per_run = 0  # Newton-Schulz launches of the last plan run
         # When a list, (name, start, end) CUDA events are appended around the
         # momentum, Newton-Schulz and AdamW launches (benchmark instrumentation).
@@ -325,7 +328,9 @@ class CudaMuonEngine:
 
     # --------------------------------------------------------------- launches
     def _momentum(self, segs: list, grad_dtype: int, momentum: float, nesterov: bool, scales_ptr: int,
-                  eps: float = 1e-7, dir_dtype: int | None = None) -> None:
+                  eps: float = 1e-7, dir_dtype: int | None = None, gradients: bool = True) -> None:
+        """One momentum launch; ``gradients`` False for inputs that are not
+        gradients (orthogonalize's copy), which the clip coefficient skips."""
         if not segs:
             return
         total = 0
@@ -336,10 +341,12 @@ class CudaMuonEngine:
         partials = torch.empty(max(total, 1), dtype=torch.float32, device=self.device)
         if dir_dtype is None:
             dir_dtype = N.MUON_F32 if self.op_dtype == N.MUON_F16 else self.op_dtype
-        N.check(self.lib.muon_momentum(c_void_p(table.data_ptr()), len(segs), total, grad_dtype, dir_dtype,
-                                       c_float(momentum), int(bool(nesterov)), c_float(eps),
-                                       c_void_p(partials.data_ptr()), c_void_p(scales_ptr), _stream_handle()),
-                "muon_momentum")
+        gs = self.grad_scale if gradients else None
+        N.check(self.lib.muon_momentum_scaled(c_void_p(table.data_ptr()), len(segs), total, grad_dtype, dir_dtype,
+                                              c_float(momentum), int(bool(nesterov)), c_float(eps),
+                                              c_void_p(partials.data_ptr()), c_void_p(scales_ptr),
+                                              c_void_p(gs.data_ptr() if gs is not None else None), _stream_handle()),
+                "muon_momentum_scaled")
         self.kernel_launches += 2 if total > 0 else 1
 
     def muon_matrices(self, items: list[MatrixItem], *, momentum: float, nesterov: bool, weight_decay_factor: float,
@@ -554,7 +561,7 @@ class CudaMuonEngine:
             classes.append(cs)
             keep += [cs.workspace, u_buf]
             first += len(idxs)
-        self._momentum(segs, N.MUON_F32, 0.0, False, scales.data_ptr(), eps=eps)
+        self._momentum(segs, N.MUON_F32, 0.0, False, scales.data_ptr(), eps=eps, gradients=False)
         if f16:
             table = _upload(N.struct_bytes(convs), self.device)
             N.check(self.lib.muon_convert_f16(c_void_p(table.data_ptr()), len(convs), chunks,
@@ -626,7 +633,7 @@ class CudaMuonEngine:
         else:
             seg.direction, seg.ld = cs.cls.x0, int(cs.cls.ld_x)
         # momentum 0, no Nesterov: exp_avg = g and d = g, i.e. a copy plus the norm.
-        self._momentum([seg], _dtype_code(src), 0.0, False, scales.data_ptr(), eps=eps)
+        self._momentum([seg], _dtype_code(src), 0.0, False, scales.data_ptr(), eps=eps, gradients=False)
         if f16:
             cv = N.ConvertSeg()
             cv.src, cv.dst = staging.data_ptr(), cs.cls.x0
@@ -688,10 +695,38 @@ class CudaMuonEngine:
         table = _upload(N.struct_bytes(segs), self.device)
         wd_factor = 1.0 - lr * weight_decay if weight_decay != 0 else 1.0
         ev = self._event_pair("adamw")
-        N.check(self.lib.muon_adamw(c_void_p(table.data_ptr()), len(segs), total, float(beta1), float(beta2),
-                                    c_float(eps), c_float(wd_factor), _stream_handle()), "muon_adamw")
+        gs = self.grad_scale
+        N.check(self.lib.muon_adamw_scaled(c_void_p(table.data_ptr()), len(segs), total, float(beta1), float(beta2),
+                                           c_float(eps), c_float(wd_factor),
+                                           c_void_p(gs.data_ptr() if gs is not None else None), _stream_handle()),
+                "muon_adamw_scaled")
         self._event_end(ev)
         self.kernel_launches += 1
+
+    def clip_grad_norm(self, grads: list[torch.Tensor], max_norm: float) -> torch.Tensor:
+        """torch.nn.utils.clip_grad_norm_'s total norm and coefficient (norm
+        type 2) of ``grads`` on the device: returns a float32 tensor [total,
+        coefficient]; nothing is rewritten (the coefficient is applied by the
+        kernels that read the gradients, via ``grad_scale``)."""
+        out = torch.zeros(2, dtype=torch.float32, device=self.device)
+        segs, total = [], 0
+        for g in grads:
+            if g.device != self.device:
+                raise RuntimeError("gradients must be on the engine's device")
+            g = g if g.is_contiguous() else g.contiguous()
+            if g.numel() == 0:
+                continue
+            sg = N.NormSeg()
+            sg.grad, sg.numel, sg.chunk_begin, sg.dtype = g.data_ptr(), g.numel(), total, _dtype_code(g)
+            segs.append(sg)
+            total += int(self.lib.muon_norm_chunks(g.numel()))
+        table = self._tables.get(N.struct_bytes(segs)) if segs else None
+        partials = torch.empty(max(total, 1), dtype=torch.float32, device=self.device)
+        N.check(self.lib.muon_clip_grad_norm(c_void_p(table.data_ptr() if table is not None else None), len(segs),
+                                             total, c_float(max_norm), c_void_p(partials.data_ptr()),
+                                             c_void_p(out.data_ptr()), _stream_handle()), "muon_clip_grad_norm")
+        self.kernel_launches += 2 if total > 0 else 1
+        return out
 
     def close(self) -> None:
         for st in self._plans.values():

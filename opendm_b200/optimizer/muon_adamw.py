@@ -47,6 +47,13 @@ The arithmetic runs in the sm_100a kernels of ``libopendm_muon.so`` through
   (``:400-414``): the fp32 direction shards go to the owner in one
   all-to-all, the update shards (in the parameter dtype) come back in a
   second. Same arithmetic; False restores the reference's gather-everywhere.
+* ``max_grad_norm``: None (default) or a float: clip the gradients at the
+  start of every ``step()`` as ``torch.nn.utils.clip_grad_norm_`` does (the
+  reference's trainer clips at 1.0 before each step, ``trainer.py:213``),
+  fused: one norm pass, and the coefficient is applied by the momentum and
+  AdamW kernels as they read the gradients (set the trainer's own
+  ``max_grad_norm`` to 0 when using it). ``clip_grad_norm_()`` does the same
+  on request; ``last_grad_norm`` holds the total norm of the last clip.
 * ``allgather``: "nccl" (default) or "p2p": the flat parameter buckets live
   in peer-mapped memory and each rank pulls its peers' buckets with
   copy-engine memcpys ordered by cross-GPU flags (``opendm_b200.p2p``), so
@@ -190,7 +197,7 @@ class MuonAdamW(torch.optim.Optimizer):
                  precision: str = "fp16", scale_mode: str = "reference", sharding: str = "auto",
                  state_sharding: bool = False, process_group=None, ns_algo: str = "auto",
                  allgather_waves: int | None = None, comm_sms: int = 32, allgather: str = "nccl",
-                 fsdp_owner_ns: bool = True, _engine=None) -> None:
+                 fsdp_owner_ns: bool = True, max_grad_norm: float | None = None, _engine=None) -> None:
         adamw_params, muon_params, muon_shapes, muon_names = [], [], [], []
         for param in model.parameters():
             if not param.requires_grad:
@@ -242,6 +249,9 @@ class MuonAdamW(torch.optim.Optimizer):
             raise ValueError(f"allgather must be 'nccl' or 'p2p', got {allgather!r}")
         self.allgather = allgather
         self.fsdp_owner_ns = bool(fsdp_owner_ns)
+        self.max_grad_norm = None if max_grad_norm is None else float(max_grad_norm)
+        self._pending_clip: torch.Tensor | None = None  # [total, coefficient] for the next step
+        self.last_grad_norm: torch.Tensor | None = None
         self.allgather_waves = allgather_waves
         self.comm_sms = max(int(comm_sms), 0)
 
@@ -320,12 +330,62 @@ class MuonAdamW(torch.optim.Optimizer):
             self._engine = _engine_for(device, self.precision, self.ns_algo)
         return self._engine
 
+    def _grads_for_clip(self) -> list[torch.Tensor]:
+        return [p.grad for g in self.param_groups for p in g["params"] if p.grad is not None]
+
+    @torch.no_grad()
+    def clip_grad_norm_(self, max_norm: float, norm_type: float = 2.0, error_if_nonfinite: bool = False,
+                        foreach: bool | None = None) -> torch.Tensor:
+        """``torch.nn.utils.clip_grad_norm_`` over this optimizer's parameters,
+        fused with the next ``step()``: the total norm and the coefficient
+        min(max_norm / (total + 1e-6), 1) are computed now, on the device,
+        with torch's arithmetic (norm type 2); the next ``step()`` scales every
+        gradient by the coefficient as its kernels read it, so ``p.grad``
+        keeps its unclipped values until then. Returns the total norm (a 0-d
+        tensor, bf16 when every gradient is bf16, as torch's). Other norm
+        types, or parameters split over ranks (FSDP, whose own
+        ``clip_grad_norm_`` reduces across ranks), run torch's function."""
+        grads = self._grads_for_clip()
+        if not grads:
+            return torch.tensor(0.0)
+        plans = [p for g in self.param_groups if g.get("use_muon", False) for p in self._get_muon_shard_plans(g)]
+        fused = (float(norm_type) == 2.0 and grads[0].device.type == "cuda"
+                 and all(pl.kind in ("local", "replicated", "empty") for pl in plans))
+        if not fused:
+            params = [p for g in self.param_groups for p in g["params"]]
+            return torch.nn.utils.clip_grad_norm_(params, max_norm, norm_type, error_if_nonfinite, foreach)
+        engine = self._get_engine(grads[0].device)
+        out = engine.clip_grad_norm(grads, float(max_norm))
+        res_dtype = torch.bfloat16 if all(g.dtype == torch.bfloat16 for g in grads) else torch.float32
+        total = out[0].to(res_dtype)
+        if error_if_nonfinite and not torch.isfinite(total).item():
+            raise RuntimeError(f"The total norm of order {float(norm_type)} for gradients from `parameters` is "
+                               "non-finite, so it cannot be clipped. To disable this error and scale the "
+                               "gradients by the non-finite norm anyway, set `error_if_nonfinite=False`")
+        self._pending_clip = out
+        self.last_grad_norm = total
+        return total
+
     @torch.no_grad()
     def step(self, closure=None):
         loss = None
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
+        if self.max_grad_norm is not None and self._pending_clip is None:
+            self.clip_grad_norm_(self.max_grad_norm)
+        pending, self._pending_clip = self._pending_clip, None
+        engine = self._engine if pending is not None else None
+        if engine is not None:
+            engine.grad_scale = pending[1:2]
+        try:
+            self._step_groups()
+        finally:
+            if engine is not None:
+                engine.grad_scale = None
+        return loss
+
+    def _step_groups(self) -> None:
         # Muon groups first, then AdamW: the groups update disjoint parameters,
         # so the order changes no result, and the AdamW group's per-step
         # host-to-device table copy (its bias corrections change every step)
@@ -337,7 +397,6 @@ class MuonAdamW(torch.optim.Optimizer):
         for group in self.param_groups:
             if not group.get("use_muon", False):
                 self._adamw_step(group)
-        return loss
 
     def _host_step(self, param, state) -> float:
         hs = self._host_steps.get(param)

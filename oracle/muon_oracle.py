@@ -200,6 +200,45 @@ class OracleMuonAdamW:
                                   param_dtype=param_dtype, device_semantics=device_semantics)
 
 
+def clip_grad_norm(grads: list, dtypes: list[str], max_norm: float):
+    """Gradient-norm clipping as the reference's trainer runs it before the
+    optimizer step (``trainer.py:213`` sets ``max_grad_norm=1.0``; the HF
+    trainer calls ``torch.nn.utils.clip_grad_norm_``, torch 2.11.0,
+    ``torch/nn/utils/clip_grad.py``: ``_get_total_norm`` then
+    ``_clip_grads_with_norm_``), norm type 2:
+
+    * per-tensor norms (``_foreach_norm``): fp32 sum of squares, sqrt, rounded
+      to the tensor's dtype;
+    * total norm: sqrt of the sum of the squared per-tensor norms, rounded to
+      the promoted dtype of all gradients (bf16 only if every gradient is bf16);
+    * ``max_norm / (total + 1e-6)`` as torch evaluates it for a tensor on the
+      right (``reciprocal() * max_norm``), each op rounded to that dtype, then
+      clamped to at most 1;
+    * every gradient multiplied in place, rounded to its dtype.
+
+    ``grads``: float32 arrays holding values of ``dtypes`` ("bfloat16" or
+    "float32"), ``None`` for absent gradients. Returns (clipped grads, total
+    norm, coefficient)."""
+    present = [(g, dt) for g, dt in zip(grads, dtypes) if g is not None]
+    if not present:
+        return list(grads), 0.0, 1.0
+    res_dt = "bfloat16" if all(dt == "bfloat16" for _, dt in present) else "float32"
+    norms = []
+    for g, dt in present:
+        s = np.float32(np.sum(np.square(g.astype(np.float64))))  # fp32-accurate sum
+        norms.append(cast_to(np.array([np.sqrt(np.float32(s))], dtype=np.float32), dt)[0])
+    n32 = np.array(norms, dtype=np.float32)
+    total = cast_to(np.array([np.sqrt(np.float32(np.sum(n32.astype(np.float64) ** 2)))], np.float32), res_dt)[0]
+    denom = cast_to(np.array([np.float32(total) + np.float32(1e-6)], np.float32), res_dt)[0]
+    recip = cast_to(np.array([np.float32(1.0) / denom], np.float32), res_dt)[0]
+    coef = cast_to(np.array([recip * np.float32(max_norm)], np.float32), res_dt)[0]
+    coef = min(float(coef), 1.0)
+    out = []
+    for g, dt in zip(grads, dtypes):
+        out.append(None if g is None else cast_to(g * np.float32(coef), dt))
+    return out, float(total), coef
+
+
 def rel_frobenius(a: np.ndarray, b: np.ndarray) -> float:
     """||a - b||_F / ||b||_F in float64 (0 when both are zero)."""
     a = np.asarray(a, np.float64)

@@ -13,7 +13,11 @@ Fixtures:
   step_bf16.npz          3 MuonAdamW steps, bf16 params
   step_nonesterov.npz    2 steps, nesterov=False, weight_decay=0
   state_layout.json      structure of the reference's state_dict() after a step
+  clip_cases.npz         torch.nn.utils.clip_grad_norm_ (torch 2.11.0, the call the
+                         reference's trainer makes before each step) on bf16,
+                         fp32 and mixed gradient sets, below and above max_norm
 bf16 tensors are stored as float32 holding the bf16 values.
+``--only clip`` writes clip_cases.npz alone (it needs no reference checkout).
 """
 
 from __future__ import annotations
@@ -129,10 +133,38 @@ def _ns_cases(ref) -> dict:
     return out
 
 
+def _clip_cases() -> dict:
+    """Gradient sets through torch.nn.utils.clip_grad_norm_(max_norm=1.0)."""
+    out = {}
+    shapes = [(64, 33), (1000,), (7,), (48, 96), (3, 5)]
+    kinds = [("bf16", [torch.bfloat16] * 5, 3.0), ("fp32", [torch.float32] * 5, 3.0),
+             ("mixed", [torch.float32, torch.bfloat16] * 2 + [torch.bfloat16], 3.0),
+             ("small_bf16", [torch.bfloat16] * 5, 1e-3), ("small_fp32", [torch.float32] * 5, 1e-3)]
+    g = torch.Generator().manual_seed(13)
+    out["cases"] = np.array([k for k, _, _ in kinds])
+    for name, dts, scale in kinds:
+        grads = [(torch.randn(s, generator=g) * scale).to(dt) for s, dt in zip(shapes, dts)]
+        params = [torch.nn.Parameter(torch.zeros_like(t)) for t in grads]
+        for p, t in zip(params, grads):
+            p.grad = t.clone()
+        total = torch.nn.utils.clip_grad_norm_(params, 1.0)
+        out[f"{name}/total"] = np.array(float(total), np.float32)
+        for i, (t, p) in enumerate(zip(grads, params)):
+            out[f"{name}/in{i}"] = _to_np(t)
+            out[f"{name}/out{i}"] = _to_np(p.grad)
+            out[f"{name}/dtype{i}"] = np.array("bfloat16" if t.dtype == torch.bfloat16 else "float32")
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("OPENDM_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", choices=["clip"], default=None)
     args = ap.parse_args()
+    np.savez_compressed(os.path.join(HERE, "clip_cases.npz"), **_clip_cases())
+    if args.only == "clip":
+        print("wrote clip_cases.npz to", HERE)
+        return
     sys.path.insert(0, args.reference)
     from opendm.optimizer import muon_adamw as ref  # noqa: E402
 

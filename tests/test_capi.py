@@ -96,6 +96,11 @@ def test_argument_validation_reports_errors(lib):
     fl.ptr[0] = 4096
     assert lib.muon_flags_wait(ctypes.byref(fl), 1, 0, ctypes.c_void_p(4096), None) == N.MUON_ERR_ARG
     assert lib.muon_flags_wait(None, 1, 1000, ctypes.c_void_p(4096), None) == N.MUON_ERR_ARG
+    # gradient-norm clipping: output and tables are checked before any launch
+    assert lib.muon_clip_grad_norm(None, 1, 4, ctypes.c_float(1.0), None, None, None) == N.MUON_ERR_ARG
+    assert lib.muon_clip_grad_norm(None, 1, 4, ctypes.c_float(1.0), None, ctypes.c_void_p(4096), None) == N.MUON_ERR_ARG
+    assert lib.muon_clip_grad_norm(None, -1, 0, ctypes.c_float(1.0), None, ctypes.c_void_p(4096), None) == N.MUON_ERR_ARG
+    assert lib.muon_norm_chunks(16384) == 1 and lib.muon_norm_chunks(16385) == 2 and lib.muon_norm_chunks(0) == 0
     with pytest.raises(RuntimeError, match="failed"):
         N.check(N.MUON_ERR_ARG, "probe")
 

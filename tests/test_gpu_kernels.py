@@ -318,3 +318,45 @@ def test_rejects_cpu_tensors():
 
     with pytest.raises(RuntimeError):
         CudaMuonEngine("cpu")
+
+
+@pytest.mark.parametrize("kind", ["bf16", "fp32", "mixed", "unclipped"])
+def test_clip_grad_norm_matches_torch(kind):
+    """The fused clip's total norm and coefficient against torch.nn.utils.
+    clip_grad_norm_ on the same GPU gradients, and momentum with the
+    coefficient applied on read against momentum on torch-clipped gradients."""
+    from opendm_b200.engine import CudaMuonEngine, MatrixItem
+
+    eng = _engine_for("fp16", "auto")
+    dev = eng.device
+    g = torch.Generator(device=dev).manual_seed(17)
+    shapes = [(300, 77), (2048,), (64, 64), (5,), (1000, 130)]
+    dts = {"bf16": [torch.bfloat16] * 5, "fp32": [torch.float32] * 5, "unclipped": [torch.bfloat16] * 5,
+           "mixed": [torch.bfloat16, torch.float32] * 2 + [torch.bfloat16]}[kind]
+    scale = 1e-4 if kind == "unclipped" else 1.0
+    grads = [(torch.randn(s, generator=g, device=dev) * scale).to(dt) for s, dt in zip(shapes, dts)]
+    out = eng.clip_grad_norm(grads, 1.0)
+    params = [torch.nn.Parameter(torch.zeros_like(t)) for t in grads]
+    for p, t in zip(params, grads):
+        p.grad = t.clone()
+    want_total = torch.nn.utils.clip_grad_norm_(params, 1.0)
+    total, coef = float(out[0]), float(out[1])
+    assert abs(total - float(want_total)) <= 1e-6 * float(want_total), (total, float(want_total))
+    if kind == "unclipped":
+        assert coef == 1.0
+    # momentum reading the gradients with the coefficient == momentum on torch's clipped gradients
+    ms = [s for s in shapes if len(s) == 2]
+    mats = [t for t in grads if t.ndim == 2]
+    clipped = [p.grad for p in params if p.grad.ndim == 2]
+    m_a = [torch.randn(s, generator=g, device=dev) * 1e-3 for s in ms]
+    m_b = [m.clone() for m in m_a]
+    eng.grad_scale = out[1:2]
+    try:
+        eng.momentum_only([MatrixItem(torch.empty(0), t, m, 0.0) for t, m in zip(mats, m_a)], momentum=0.95,
+                          nesterov=True)
+    finally:
+        eng.grad_scale = None
+    eng.momentum_only([MatrixItem(torch.empty(0), t, m, 0.0) for t, m in zip(clipped, m_b)], momentum=0.95,
+                      nesterov=True)
+    for a, b in zip(m_a, m_b):
+        assert (torch.linalg.norm(a - b) / torch.linalg.norm(b)).item() <= 1e-6

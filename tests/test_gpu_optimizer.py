@@ -279,3 +279,49 @@ def test_lr_schedule_changes_are_applied():
         g["lr"] = 0.0
     opt.step()
     torch.testing.assert_close(model.w, before, rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_max_grad_norm_matches_torch_clip_then_step(dtype):
+    """MuonAdamW(max_grad_norm=1.0) (norm pass + coefficient applied by the
+    momentum and AdamW kernels) against torch.nn.utils.clip_grad_norm_
+    followed by an unclipped step, over two steps with gradients large
+    enough to clip; the gradients themselves are left untouched."""
+    from opendm_b200.optimizer import MuonAdamW, mark_muon_parameters
+
+    dev = _dev()
+    g = torch.Generator(device=dev).manual_seed(23)
+    shapes = [(256, 512), (512, 256), (128, 128), (512,)]
+
+    def build():
+        gg = torch.Generator(device=dev).manual_seed(29)
+        model = torch.nn.Module()
+        for i, s in enumerate(shapes):
+            model.register_parameter(f"p{i}", torch.nn.Parameter((torch.randn(s, generator=gg, device=dev) * 0.02)
+                                                                 .to(dtype)))
+        mark_muon_parameters(model, predicate=lambda n, p: p.ndim == 2)
+        return model
+
+    fused_model, ref_model = build(), build()
+    fused = MuonAdamW(fused_model, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, max_grad_norm=1.0)
+    ref = MuonAdamW(ref_model, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01)
+    for _ in range(2):
+        grads = [(torch.randn(s, generator=g, device=dev) * 0.5).to(dtype) for s in shapes]
+        for p, t in zip(fused_model.parameters(), grads):
+            p.grad = t.clone()
+        for p, t in zip(ref_model.parameters(), grads):
+            p.grad = t.clone()
+        fused.step()
+        total = torch.nn.utils.clip_grad_norm_(list(ref_model.parameters()), 1.0)
+        ref.step()
+        assert float(total) > 1.0  # the step did clip
+        assert abs(float(fused.last_grad_norm) - float(total)) <= 1e-6 * float(total)
+        for p, t in zip(fused_model.parameters(), grads):
+            assert torch.equal(p.grad, t)  # gradients are not rewritten
+    fused.check_device_errors()
+    for a, b in zip(fused_model.parameters(), ref_model.parameters()):
+        err = (torch.linalg.norm(a.float() - b.float()) / torch.linalg.norm(b.float())).item()
+        assert err <= (1e-6 if dtype == torch.float32 else 4e-3), err
+    for a, b in zip(fused_model.parameters(), ref_model.parameters()):
+        ea, eb = fused.state[a]["exp_avg"], ref.state[b]["exp_avg"]
+        assert (torch.linalg.norm(ea - eb) / torch.linalg.norm(eb)).item() <= 1e-5

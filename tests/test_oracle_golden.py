@@ -96,3 +96,23 @@ def test_bf16_round_ties_to_even():
 def test_ns_flops_formula():
     assert O.ns_flops((2048, 8192)) == 5 * (4 * 2048 ** 2 * 8192 + 2 * 2048 ** 3)
     assert O.ns_flops((8192, 2048)) == O.ns_flops((2048, 8192))
+
+
+def test_clip_oracle_matches_torch_clip_grad_norm(golden_dir):
+    """The gradient-norm clipping restatement against torch.nn.utils.
+    clip_grad_norm_ (the call the reference's trainer makes before each
+    step): bit-exact whenever a bf16 gradient sets the arithmetic or no
+    clipping happens; fp32 within the last bit of the norm's reduction order."""
+    z = np.load(os.path.join(golden_dir, "clip_cases.npz"))
+    for case in z["cases"]:
+        n = len([k for k in z.files if k.startswith(f"{case}/in")])
+        grads = [z[f"{case}/in{i}"] for i in range(n)]
+        dtypes = [str(z[f"{case}/dtype{i}"]) for i in range(n)]
+        out, total, coef = O.clip_grad_norm(grads, dtypes, 1.0)
+        assert abs(total - float(z[f"{case}/total"])) <= 1e-6 * abs(float(z[f"{case}/total"])), case
+        for i, o in enumerate(out):
+            want = z[f"{case}/out{i}"]
+            if case == "fp32":
+                np.testing.assert_allclose(o, want, rtol=1e-6, atol=0)
+            else:
+                np.testing.assert_array_equal(o, want, err_msg=f"{case}/{i}")
