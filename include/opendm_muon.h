@@ -272,9 +272,10 @@ int muon_ns_class_layout(muon_ns_class* cls, void* base, int op_dtype);
  * bf16 when every gradient is bf16, else fp32) and the coefficient
  * min(max_norm / (total + 1e-6), 1) with torch's rounding; out_dev[0] = total,
  * out_dev[1] = coefficient. muon_momentum_scaled and muon_adamw_scaled then
- * multiply each gradient by *grad_scale_dev as they read it (rounded to the
- * gradient's dtype, as torch's in-place multiply rounds it), so the gradients
- * are never rewritten. partials_dev: total_chunks floats (total_chunks = the
+ * multiply each gradient by *grad_scale_dev as they read it (coefficient and
+ * product in the gradient's dtype, as torch's CUDA in-place multiply of a
+ * gradient list by a 0-d tensor computes it), so the gradients are never
+ * rewritten. partials_dev: total_chunks floats (total_chunks = the
  * sum of muon_norm_chunks(numel) over the segments; chunk_begin its prefix). */
 typedef struct muon_norm_seg {
   const void* grad; /* numel elements of dtype */

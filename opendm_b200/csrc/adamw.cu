@@ -47,10 +47,11 @@ __device__ __forceinline__ float adam_elem(float p, float g, float& m, float& v,
   return __fadd_rn(p, __fmul_rn(neg_step, __fdiv_rn(m, denom)));
 }
 
-// Gradient-norm clipping folded into the read (clip.cu): g' = g * coef,
-// rounded to the gradient's dtype.
+// Gradient-norm clipping folded into the read (clip.cu): g' = g * coef with
+// the coefficient and the product in the gradient's dtype (torch's CUDA
+// _foreach_mul_ with a 0-d coefficient tensor).
 __device__ __forceinline__ float clip_grad_adam(float g, float coef, bool bf) {
-  return bf ? bf16_round(g * coef) : g * coef;
+  return bf ? bf16_round(g * bf16_round(coef)) : g * coef;
 }
 
 __global__ void __launch_bounds__(ADAM_THREADS) adamw_kernel(const muon_adamw_seg* __restrict__ segs, int n_segs,

@@ -12,7 +12,8 @@
 //   total  = round_{R}(sqrt(sum norm_i^2))            (vector_norm of the stack)
 //   coef   = min(round_R(round_R(1 / round_R(total + 1e-6)) * max_norm), 1)
 //                                                     (max_norm / t is t.reciprocal() * max_norm)
-//   g'     = round_{dtype_i}(g * coef)                (_foreach_mul_)
+//   g'     = round_{dtype_i}(g * round_{dtype_i}(coef))  (CUDA _foreach_mul_ with a
+//                                                     0-d tensor: the coefficient in the list's dtype)
 // with R = bf16 when every gradient is bf16, else fp32. Sums accumulate in
 // fp32 in a fixed order (deterministic; torch's own order can differ in the
 // last fp32 bit).

@@ -92,11 +92,13 @@ __device__ __forceinline__ void store_dir8(void* dir, int64_t e, const float (&d
   }
 }
 
-// Gradient-norm clipping folded into the read (clip.cu): g' = g * coef,
-// rounded to the gradient's dtype as torch's in-place multiply rounds it.
+// Gradient-norm clipping folded into the read (clip.cu): g' = g * coef as
+// torch's CUDA _foreach_mul_ computes it for a gradient list and a 0-d
+// coefficient tensor: the coefficient in the gradient's dtype, the product
+// rounded to it.
 template <int kGradDt>
 __device__ __forceinline__ float clip_grad(float g, float coef) {
-  return kGradDt == MUON_BF16 ? bf16_round(g * coef) : g * coef;
+  return kGradDt == MUON_BF16 ? bf16_round(g * bf16_round(coef)) : g * coef;
 }
 
 template <int kGradDt, int kDirDt>

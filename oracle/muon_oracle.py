@@ -200,7 +200,7 @@ class OracleMuonAdamW:
                                   param_dtype=param_dtype, device_semantics=device_semantics)
 
 
-def clip_grad_norm(grads: list, dtypes: list[str], max_norm: float):
+def clip_grad_norm(grads: list, dtypes: list[str], max_norm: float, device_semantics: str = "cpu"):
     """Gradient-norm clipping as the reference's trainer runs it before the
     optimizer step (``trainer.py:213`` sets ``max_grad_norm=1.0``; the HF
     trainer calls ``torch.nn.utils.clip_grad_norm_``, torch 2.11.0,
@@ -214,7 +214,11 @@ def clip_grad_norm(grads: list, dtypes: list[str], max_norm: float):
     * ``max_norm / (total + 1e-6)`` as torch evaluates it for a tensor on the
       right (``reciprocal() * max_norm``), each op rounded to that dtype, then
       clamped to at most 1;
-    * every gradient multiplied in place, rounded to its dtype.
+    * every gradient multiplied in place, rounded to its dtype. torch's CPU
+      ``_foreach_mul_`` multiplies by the coefficient in the promoted dtype;
+      its CUDA kernel first casts the 0-d coefficient to each gradient's
+      dtype (``device_semantics="cuda"``), which differs for bf16 gradients
+      when some gradient is fp32.
 
     ``grads``: float32 arrays holding values of ``dtypes`` ("bfloat16" or
     "float32"), ``None`` for absent gradients. Returns (clipped grads, total
@@ -235,7 +239,8 @@ def clip_grad_norm(grads: list, dtypes: list[str], max_norm: float):
     coef = min(float(coef), 1.0)
     out = []
     for g, dt in zip(grads, dtypes):
-        out.append(None if g is None else cast_to(g * np.float32(coef), dt))
+        c = np.float32(coef) if device_semantics == "cpu" else cast_to(np.array([coef], np.float32), dt)[0]
+        out.append(None if g is None else cast_to(g * c, dt))
     return out, float(total), coef
 
 
