@@ -319,9 +319,12 @@ def test_max_grad_norm_matches_torch_clip_then_step(dtype):
         for p, t in zip(fused_model.parameters(), grads):
             assert torch.equal(p.grad, t)  # gradients are not rewritten
     fused.check_device_errors()
+    # The total norms agree to the last bit of their reduction order; through
+    # the fp16 Newton-Schulz operands such a difference can move parameters by
+    # ~1e-4, so parameters are held to the parity bar, momentum tightly.
     for a, b in zip(fused_model.parameters(), ref_model.parameters()):
         err = (torch.linalg.norm(a.float() - b.float()) / torch.linalg.norm(b.float())).item()
-        assert err <= (1e-6 if dtype == torch.float32 else 4e-3), err
+        assert err <= (PARAM_TOL if dtype == torch.float32 else 4e-3), err
     for a, b in zip(fused_model.parameters(), ref_model.parameters()):
         ea, eb = fused.state[a]["exp_avg"], ref.state[b]["exp_avg"]
         assert (torch.linalg.norm(ea - eb) / torch.linalg.norm(eb)).item() <= 1e-5
