@@ -429,8 +429,9 @@ def run_ours(args):
         a1.record()
         sync_all()
         ag_ms = max_over_ranks(a0.elapsed_time(a1))
-    # grad (bf16) + exp_avg read/write + direction write (+ the fp16 convert pass)
-    mom_bytes = my_elems * {"tf32": 2 + 4 + 4 + 4, "bf16": 2 + 4 + 4 + 2, "fp16": 2 + 8 + 4 + 4 + 2}[args.precision]
+    # grad (bf16) + exp_avg read/write + direction write; fp16: momentum pass
+    # (grad, exp_avg r/w) + the operand pass (grad, exp_avg, fp16 write)
+    mom_bytes = my_elems * {"tf32": 2 + 4 + 4 + 4, "bf16": 2 + 4 + 4 + 2, "fp16": 2 + 8 + 2 + 4 + 2}[args.precision]
     mom_gbs = mom_bytes / (mom_ms * 1e-3) / 1e9 if mom_ms > 0 else 0.0
     adam_elems = sum(math.prod(s) for n, s in spec if not is_muon(n, s))
     adam_gbs = adam_elems * (2 + 2 + 8 + 8 + 2) / (adam_ms * 1e-3) / 1e9 if adam_ms > 0 else 0.0

@@ -151,6 +151,31 @@ typedef struct muon_convert_seg {
 int muon_convert_f16(const muon_convert_seg* segs_dev, int n_segs, int64_t total_chunks,
                      const float* scales_dev, void* stream);
 
+/* fp16 operands without the fp32 direction: after muon_momentum ran with
+ * direction NULL (momentum and norm only), rebuild each direction from the
+ * gradient and the advanced exp_avg with the same operations (d = g +
+ * momentum * exp_avg when nesterov, else exp_avg; the gradient multiplied by
+ * *grad_scale_dev when it is not NULL, as muon_momentum_scaled does),
+ * normalise it with scales[scale_index] and scale it by `mul` into fp16, as
+ * muon_convert_f16 does. Bit-identical to muon_momentum (MUON_F32 direction)
+ * followed by muon_convert_f16, without the fp32 copy (4 bytes per element of
+ * memory and 8 of traffic fewer, 2 more read back from the gradient). */
+typedef struct muon_direction_f16_seg {
+  const void* grad;     /* [rows * cols] of the launch's grad dtype, or NULL */
+  const float* exp_avg; /* [rows * cols], already advanced this step */
+  void* dst;            /* [rows][ld_dst] fp16 */
+  int64_t rows;
+  int64_t cols;
+  int64_t ld_dst;
+  int64_t chunk_begin;  /* prefix sum of muon_momentum_chunks() */
+  float mul;
+  int32_t scale_index;
+} muon_direction_f16_seg;
+
+int muon_direction_f16(const muon_direction_f16_seg* segs_dev, int n_segs, int64_t total_chunks, int grad_dtype,
+                       float momentum, int nesterov, const float* scales_dev, const float* grad_scale_dev,
+                       void* stream);
+
 /* Power-of-two scale of the stored operand X at Newton-Schulz iteration
  * `iteration` for op_dtype MUON_F16 (1.0 for the other types). */
 float muon_ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dtype);

@@ -89,6 +89,11 @@ class FlagList(Structure):
     _fields_ = [("ptr", c_void_p * MUON_MAX_FLAGS), ("n", c_int32)]
 
 
+class DirectionF16Seg(Structure):
+    _fields_ = [("grad", c_void_p), ("exp_avg", c_void_p), ("dst", c_void_p), ("rows", c_int64), ("cols", c_int64),
+                ("ld_dst", c_int64), ("chunk_begin", c_int64), ("mul", c_float), ("scale_index", c_int32)]
+
+
 class NormSeg(Structure):
     _fields_ = [("grad", c_void_p), ("numel", c_int64), ("chunk_begin", c_int64), ("dtype", c_int32),
                 ("reserved", c_int32)]
@@ -144,6 +149,7 @@ SIGNATURES = {
     "muon_ns_plan_set_sm_limit": (c_int, [c_void_p, c_int]),
     "muon_flags_set": (c_int, [POINTER(FlagList), c_uint32, c_void_p]),
     "muon_norm_chunks": (c_int64, [c_int64]),
+    "muon_direction_f16": (c_int, [c_void_p, c_int, c_int64, c_int, c_float, c_int, c_void_p, c_void_p, c_void_p]),
     "muon_clip_grad_norm": (c_int, [c_void_p, c_int, c_int64, c_float, c_void_p, c_void_p, c_void_p]),
     "muon_momentum_scaled": (c_int, [c_void_p, c_int, c_int64, c_int, c_int, c_float, c_int, c_float, c_void_p,
                                      c_void_p, c_void_p, c_void_p]),

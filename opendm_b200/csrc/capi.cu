@@ -178,6 +178,13 @@ int muon_adamw_scaled(const muon_adamw_seg* segs_dev, int n_segs, int64_t total_
 
 int64_t muon_norm_chunks(int64_t numel) { return muon::norm_chunks(numel); }
 
+int muon_direction_f16(const muon_direction_f16_seg* segs_dev, int n_segs, int64_t total_chunks, int grad_dtype,
+                       float momentum, int nesterov, const float* scales_dev, const float* grad_scale_dev,
+                       void* stream) {
+  return muon::launch_direction_f16(segs_dev, n_segs, total_chunks, grad_dtype, momentum, nesterov, scales_dev,
+                                    grad_scale_dev, static_cast<cudaStream_t>(stream));
+}
+
 int muon_clip_grad_norm(const muon_norm_seg* segs_dev, int n_segs, int64_t total_chunks, float max_norm,
                         float* partials_dev, float* out_dev, void* stream) {
   return muon::launch_clip_grad_norm(segs_dev, n_segs, total_chunks, max_norm, partials_dev, out_dev,

@@ -143,7 +143,7 @@ class _ClassState:
 
 class _PlanState:
     """Everything cached for one set of matrices: shape classes with their
-    workspaces, the segment order, the fp16 staging table and the plan."""
+    workspaces, the segment order and the plan."""
 
     def __init__(self):
         self.plan = None
@@ -151,11 +151,6 @@ class _PlanState:
         self.order: list[tuple[int, int]] = []  # item index -> (class index, slot)
         self.seg_order: list[int] = []
         self.scales = None
-        self.staging = None
-        self.staging_off: dict[int, int] = {}
-        self.convert_table = None
-        self.convert_n = 0
-        self.convert_chunks = 0
         self.ns_launches = 0
         self.sm_limit = 0
 
@@ -296,27 +291,6 @@ class CudaMuonEngine:
             cs.first_seg = first
             cs.cls.scales = c_void_p(st.scales.data_ptr() + 4 * first)
             first += cs.count
-        if self.op_dtype == N.MUON_F16:
-            # fp32 directions, normalised into fp16 x0 by muon_convert_f16.
-            total = sum(cs.rows * cs.cols * cs.count for cs in st.classes)
-            st.staging = torch.empty(max(total, 1), dtype=torch.float32, device=self.device)
-            segs, off, chunks = [], 0, 0
-            for i in st.seg_order:
-                ci, slot = st.order[i]
-                cs = st.classes[ci]
-                st.staging_off[i] = off
-                cv = N.ConvertSeg()
-                cv.src = st.staging.data_ptr() + 4 * off
-                cv.dst = cs.cls.x0 + slot * cs.x_stride
-                cv.rows, cv.cols, cv.ld_src, cv.ld_dst = cs.rows, cs.cols, cs.cols, int(cs.cls.ld_x)
-                cv.chunk_begin = chunks
-                cv.mul = cs.x0_scale
-                cv.scale_index = cs.first_seg + slot
-                segs.append(cv)
-                off += cs.rows * cs.cols
-                chunks += int(self.lib.muon_momentum_chunks(cs.rows, cs.cols))
-            st.convert_table = _upload(N.struct_bytes(segs), self.device)
-            st.convert_n, st.convert_chunks = len(segs), chunks
         if ns_steps >= 1:
             arr = (N.NsClass * len(st.classes))(*[cs.cls for cs in st.classes])
             plan = c_void_p()
@@ -363,6 +337,7 @@ class CudaMuonEngine:
         grads = [it.grad for it in items]
         gdt = {_dtype_code(g) for g in grads if g is not None} or {N.MUON_F32}
         # Segments in class order: segment index == scale index.
+        f16 = self.op_dtype == N.MUON_F16
         by_dtype: dict[int, list] = {}
         for i in st.seg_order:
             it = items[i]
@@ -374,21 +349,29 @@ class CudaMuonEngine:
                 g = g.contiguous()
             seg.grad = g.data_ptr() if g is not None else None
             seg.exp_avg = it.exp_avg.data_ptr()
-            if st.staging is not None:
-                seg.direction = st.staging.data_ptr() + 4 * st.staging_off[i]
+            if f16:
+                # momentum and norm only; the fp16 operand is rebuilt below from
+                # the gradient and the advanced exp_avg (muon_direction_f16)
+                seg.direction = None
                 seg.rows, seg.cols, seg.ld = cs.rows, cs.cols, cs.cols
+                dseg = N.DirectionF16Seg()
+                dseg.grad, dseg.exp_avg = seg.grad, seg.exp_avg
+                dseg.dst = cs.cls.x0 + slot * cs.x_stride
+                dseg.rows, dseg.cols, dseg.ld_dst = cs.rows, cs.cols, int(cs.cls.ld_x)
+                dseg.mul, dseg.scale_index = cs.x0_scale, cs.first_seg + slot
             else:
                 seg.direction = cs.cls.x0 + slot * cs.x_stride
                 seg.rows, seg.cols, seg.ld = cs.rows, cs.cols, int(cs.cls.ld_x)
+                dseg = None
             code = _dtype_code(g) if g is not None else next(iter(gdt))
-            by_dtype.setdefault(code, []).append((cs.first_seg + slot, seg))
+            by_dtype.setdefault(code, []).append((cs.first_seg + slot, seg, dseg))
         ev = self._event_pair("momentum")
         for code, lst in by_dtype.items():
             # Each launch writes scales for a contiguous run; split into runs.
             lst.sort(key=lambda x: x[0])
             run: list = []
             start = None
-            for idx, seg in lst:
+            for idx, seg, _ in lst:
                 if run and idx != start + len(run):
                     self._momentum(run, code, momentum, nesterov, st.scales.data_ptr() + 4 * start)
                     run = []
@@ -397,11 +380,21 @@ class CudaMuonEngine:
                 run.append(seg)
             if run:
                 self._momentum(run, code, momentum, nesterov, st.scales.data_ptr() + 4 * start)
-        if st.convert_table is not None:
-            N.check(self.lib.muon_convert_f16(c_void_p(st.convert_table.data_ptr()), st.convert_n,
-                                              st.convert_chunks, c_void_p(st.scales.data_ptr()),
-                                              _stream_handle()), "muon_convert_f16")
-            self.kernel_launches += 1
+        if f16:
+            for code, lst in by_dtype.items():
+                dsegs, total = [], 0
+                for _, _, dseg in lst:
+                    dseg.chunk_begin = total
+                    total += int(self.lib.muon_momentum_chunks(dseg.rows, dseg.cols))
+                    dsegs.append(dseg)
+                table = self._tables.get(N.struct_bytes(dsegs))
+                gs = self.grad_scale
+                N.check(self.lib.muon_direction_f16(c_void_p(table.data_ptr()), len(dsegs), total, code,
+                                                    c_float(momentum), int(bool(nesterov)),
+                                                    c_void_p(st.scales.data_ptr()),
+                                                    c_void_p(gs.data_ptr() if gs is not None else None),
+                                                    _stream_handle()), "muon_direction_f16")
+                self.kernel_launches += 1
         self._event_end(ev)
         if ns_steps >= 1:
             ev = self._event_pair("ns")
