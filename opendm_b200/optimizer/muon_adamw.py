@@ -37,7 +37,8 @@ The arithmetic runs in the sm_100a kernels of ``libopendm_muon.so`` through
 * ``allgather_waves``: with sharding, each rank's matrices are processed in
   this many waves of decreasing size; the all-gather of a wave overlaps the
   Newton-Schulz of the next (default on CUDA with at least 6 matrices per
-  rank: 4 at 8 or more ranks, 3 below; else 1).
+  rank: 4 at 8 or more ranks carrying >= 16 dense TFLOP each, else 3;
+  1 otherwise).
 * ``comm_sms``: SMs the Newton-Schulz launches leave free while an NCCL
   all-gather overlaps them, and the CTA limit of the optimizer's own NCCL
   group for that all-gather (default 32).
@@ -470,12 +471,19 @@ class MuonAdamW(torch.optim.Optimizer):
         return all(p.kind == "replicated" for p in plans) and \
             all(p.is_contiguous() for p in group["params"])
 
-    def _n_waves(self, n_matrices: int, world: int, device: torch.device) -> int:
+    def _n_waves(self, shapes: list, world: int, device: torch.device, steps: int) -> int:
+        """Waves per step: one per ~1/3-1/4 of a rank's Newton-Schulz work.
+        Every wave adds a full set of Newton-Schulz launches (fixed fill and
+        drain time), so a fourth wave pays off only when each rank carries a
+        large share (>= 16 dense TFLOP), as at 8 ranks on BASELINE config 4."""
         if self.allgather_waves is not None:
             return int(self.allgather_waves)
-        if device.type != "cuda" or n_matrices < 6 * world:
+        if device.type != "cuda" or len(shapes) < 6 * world:
             return 1
-        return 4 if world >= 8 else 3
+        from ..sharding import ns_cost
+
+        per_rank = sum(ns_cost(s, steps) for s in shapes) / world
+        return 4 if world >= 8 and per_rank >= 16e12 else 3
 
     def _owners_for(self, group: dict) -> list[int]:
         key = id(group)
@@ -484,7 +492,7 @@ class MuonAdamW(torch.optim.Optimizer):
             world, rank = self._world()
             shapes, steps = group["muon_shapes"], int(group["muon_ns_steps"])
             owners = assign_owners(shapes, world, steps)
-            n_waves = self._n_waves(len(shapes), world, self._device_for_params(group["params"]))
+            n_waves = self._n_waves(shapes, world, self._device_for_params(group["params"]), steps)
             waves = assign_waves(shapes, owners, world, n_waves, steps)
             self._owners[key] = owners
             self._waves[key] = waves
