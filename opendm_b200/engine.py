@@ -338,6 +338,7 @@ class CudaMuonEngine:
         gdt = {_dtype_code(g) for g in grads if g is not None} or {N.MUON_F32}
         # Segments in class order: segment index == scale index.
         f16 = self.op_dtype == N.MUON_F16
+        keep: list[torch.Tensor] = []  # contiguous copies of strided gradients
         by_dtype: dict[int, list] = {}
         for i in st.seg_order:
             it = items[i]
@@ -347,6 +348,7 @@ class CudaMuonEngine:
             g = it.grad
             if g is not None and not g.is_contiguous():
                 g = g.contiguous()
+                keep.append(g)  # the copy must outlive the launches that read it
             seg.grad = g.data_ptr() if g is not None else None
             seg.exp_avg = it.exp_avg.data_ptr()
             if f16:
@@ -452,12 +454,14 @@ class CudaMuonEngine:
         """exp_avg update without a direction (matrices another rank orthogonalises)."""
         if not items:
             return
+        keep: list[torch.Tensor] = []  # contiguous copies of strided gradients
         by_dtype: dict[int, list] = {}
         for it in items:
             seg = N.MomentumSeg()
             g = it.grad
             if g is not None and not g.is_contiguous():
                 g = g.contiguous()
+                keep.append(g)  # the copy must outlive the launches that read it
             seg.grad = g.data_ptr() if g is not None else None
             seg.exp_avg = it.exp_avg.data_ptr()
             seg.direction = None
@@ -493,9 +497,12 @@ class CudaMuonEngine:
         if not items:
             return
         by_dtype: dict[int, list] = {}
+        keep: list[torch.Tensor] = []  # contiguous copies must outlive the launches
         for (grad, exp_avg), off in zip(items, offsets):
             seg = N.MomentumSeg()
             g = grad.reshape(-1).contiguous() if grad is not None else None
+            if g is not None:
+                keep.append(g)
             seg.grad = g.data_ptr() if g is not None else None
             seg.exp_avg = exp_avg.data_ptr()
             seg.direction = out.data_ptr() + 4 * int(off)
@@ -665,11 +672,13 @@ class CudaMuonEngine:
             return
         segs = []
         total = 0
+        keep: list[torch.Tensor] = []
         for it in items:
             for t in (it.param, it.grad, it.exp_avg, it.exp_avg_sq):
                 if t.device != self.device:
                     raise RuntimeError("AdamW tensors must be on the engine's device")
             g = it.grad if it.grad.is_contiguous() else it.grad.contiguous()
+            keep.append(g)  # a contiguous copy must outlive the launch that reads it
             if not it.param.is_contiguous():
                 raise RuntimeError("AdamW parameters must be contiguous")
             s = N.AdamwSeg()
@@ -703,10 +712,12 @@ class CudaMuonEngine:
         kernels that read the gradients, via ``grad_scale``)."""
         out = torch.zeros(2, dtype=torch.float32, device=self.device)
         segs, total = [], 0
+        keep: list[torch.Tensor] = []  # contiguous copies must outlive the launch
         for g in grads:
             if g.device != self.device:
                 raise RuntimeError("gradients must be on the engine's device")
             g = g if g.is_contiguous() else g.contiguous()
+            keep.append(g)
             if g.numel() == 0:
                 continue
             sg = N.NormSeg()

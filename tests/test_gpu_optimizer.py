@@ -328,3 +328,36 @@ def test_max_grad_norm_matches_torch_clip_then_step(dtype):
     for a, b in zip(fused_model.parameters(), ref_model.parameters()):
         ea, eb = fused.state[a]["exp_avg"], ref.state[b]["exp_avg"]
         assert (torch.linalg.norm(ea - eb) / torch.linalg.norm(eb)).item() <= 1e-5
+
+
+def test_strided_gradients_match_contiguous():
+    """Gradients that are strided views (here transposes) are copied to
+    contiguous memory for the kernels; several in one step must not share a
+    recycled copy: the result equals the same step with contiguous gradients."""
+    from opendm_b200.optimizer import MuonAdamW, mark_muon_parameters
+
+    dev = _dev()
+    shapes = [(128, 256), (256, 128), (128, 256), (96, 96), (64, 48)]
+
+    def build():
+        gg = torch.Generator(device=dev).manual_seed(31)
+        model = torch.nn.Module()
+        for i, s in enumerate(shapes):
+            model.register_parameter(f"p{i}", torch.nn.Parameter(torch.randn(s, generator=gg, device=dev) * 0.02))
+        mark_muon_parameters(model, predicate=lambda n, p: int(n[1:]) < 3)
+        return model, MuonAdamW(model, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01)
+
+    ma, oa = build()
+    mb, ob = build()
+    g = torch.Generator(device=dev).manual_seed(37)
+    for _ in range(2):
+        grads = [torch.randn(s[::-1], generator=g, device=dev) * 1e-3 for s in shapes]
+        for p, t in zip(ma.parameters(), grads):
+            p.grad = t.t()  # strided view
+            assert not p.grad.is_contiguous()
+        for p, t in zip(mb.parameters(), grads):
+            p.grad = t.t().contiguous()
+        oa.step()
+        ob.step()
+    for a, b in zip(ma.parameters(), mb.parameters()):
+        assert torch.equal(a, b)
