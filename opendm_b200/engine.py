@@ -146,7 +146,7 @@ class _PlanState:
     workspaces, the segment order and the plan."""
 
     def __init__(self):
-        self.plan = None
+        self.plans: list = []  # one library plan per group of up to PLAN_CLASSES classes
         self.classes: list[_ClassState] = []
         self.order: list[tuple[int, int]] = []  # item index -> (class index, slot)
         self.seg_order: list[int] = []
@@ -159,6 +159,7 @@ class CudaMuonEngine:
     """Runs the Muon and AdamW kernels on one CUDA device."""
 
     MAX_PLANS = 16  # cached matrix sets (e.g. the waves of a sharded step)
+    PLAN_CLASSES = 16  # shape classes one library plan takes (two problems per class in a 32-problem launch)
 
     def __init__(self, device: torch.device | str | int, precision: str = "fp16", ns_algo: str = "auto"):
         if precision not in PRECISIONS:
@@ -247,11 +248,12 @@ class CudaMuonEngine:
             st = self._build(items, ns_steps)
             while len(self._plans) >= self.MAX_PLANS:
                 old = self._plans.pop(next(iter(self._plans)))
-                if old.plan is not None:
-                    self.lib.muon_ns_plan_destroy(old.plan)
+                for plan in old.plans:
+                    self.lib.muon_ns_plan_destroy(plan)
         self._plans[key] = st  # most recently used last
-        if st.plan is not None and st.sm_limit != self.sm_limit:
-            N.check(self.lib.muon_ns_plan_set_sm_limit(st.plan, int(self.sm_limit)), "muon_ns_plan_set_sm_limit")
+        if st.plans and st.sm_limit != self.sm_limit:
+            for plan in st.plans:
+                N.check(self.lib.muon_ns_plan_set_sm_limit(plan, int(self.sm_limit)), "muon_ns_plan_set_sm_limit")
             st.sm_limit = self.sm_limit
         return st
 
@@ -292,13 +294,31 @@ class CudaMuonEngine:
             cs.cls.scales = c_void_p(st.scales.data_ptr() + 4 * first)
             first += cs.count
         if ns_steps >= 1:
-            arr = (N.NsClass * len(st.classes))(*[cs.cls for cs in st.classes])
-            plan = c_void_p()
-            N.check(self.lib.muon_ns_plan_create(arr, len(st.classes), self.op_dtype, ns_steps, byref(plan)),
-                    "muon_ns_plan_create")
-            st.plan = plan
-            st.ns_launches = int(self.lib.muon_ns_plan_launches(plan))
+            st.plans = self._create_plans([cs.cls for cs in st.classes], ns_steps)
+            st.ns_launches = sum(int(self.lib.muon_ns_plan_launches(p)) for p in st.plans)
         return st
+
+    def _create_plans(self, classes: list, steps: int) -> list:
+        """Library plans for `classes`, PLAN_CLASSES per plan (run one after the other)."""
+        plans = []
+        try:
+            for i in range(0, len(classes), self.PLAN_CLASSES):
+                part = classes[i:i + self.PLAN_CLASSES]
+                arr = (N.NsClass * len(part))(*part)
+                plan = c_void_p()
+                N.check(self.lib.muon_ns_plan_create(arr, len(part), self.op_dtype, int(steps), byref(plan)),
+                        "muon_ns_plan_create")
+                plans.append(plan)
+        except Exception:
+            for plan in plans:
+                self.lib.muon_ns_plan_destroy(plan)
+            raise
+        return plans
+
+    def _run_plans(self, plans: list) -> None:
+        for plan in plans:
+            N.check(self.lib.muon_ns_plan_run(plan, c_void_p(self._err.data_ptr()), _stream_handle()),
+                    "muon_ns_plan_run")
 
     # --------------------------------------------------------------- launches
     def _momentum(self, segs: list, grad_dtype: int, momentum: float, nesterov: bool, scales_ptr: int,
@@ -400,8 +420,7 @@ class CudaMuonEngine:
         self._event_end(ev)
         if ns_steps >= 1:
             ev = self._event_pair("ns")
-            N.check(self.lib.muon_ns_plan_run(st.plan, c_void_p(self._err.data_ptr()), _stream_handle()),
-                    "muon_ns_plan_run")
+            self._run_plans(st.plans)
             self._event_end(ev)
             self.ns_launches_per_run = st.ns_launches
             self.kernel_launches += st.ns_launches
@@ -568,16 +587,13 @@ class CudaMuonEngine:
                                               c_void_p(scales.data_ptr()), _stream_handle()), "muon_convert_f16")
             self.kernel_launches += 1
             keep += [table, staging]
-        arr = (N.NsClass * len(classes))(*[cs.cls for cs in classes])
-        plan = c_void_p()
-        N.check(self.lib.muon_ns_plan_create(arr, len(classes), self.op_dtype, int(steps), byref(plan)),
-                "muon_ns_plan_create")
+        plans = self._create_plans([cs.cls for cs in classes], steps)
         try:
-            N.check(self.lib.muon_ns_plan_run(plan, c_void_p(self._err.data_ptr()), _stream_handle()),
-                    "muon_ns_plan_run")
-            self.kernel_launches += int(self.lib.muon_ns_plan_launches(plan))
+            self._run_plans(plans)
+            self.kernel_launches += sum(int(self.lib.muon_ns_plan_launches(p)) for p in plans)
         finally:
-            self.lib.muon_ns_plan_destroy(plan)
+            for plan in plans:
+                self.lib.muon_ns_plan_destroy(plan)
         self._record_error_check()
         stream = torch.cuda.current_stream(self.device)
         for t in keep:  # workspaces stay valid until the queued kernels have run
@@ -734,9 +750,9 @@ class CudaMuonEngine:
 
     def close(self) -> None:
         for st in self._plans.values():
-            if st.plan is not None:
-                self.lib.muon_ns_plan_destroy(st.plan)
-                st.plan = None
+            for plan in st.plans:
+                self.lib.muon_ns_plan_destroy(plan)
+            st.plans = []
         self._plans.clear()
 
     def __del__(self):  # pragma: no cover - interpreter teardown order varies

@@ -360,3 +360,26 @@ def test_clip_grad_norm_matches_torch(kind):
                       nesterov=True)
     for a, b in zip(m_a, m_b):
         assert (torch.linalg.norm(a - b) / torch.linalg.norm(b)).item() <= 1e-6
+
+
+def test_more_shape_classes_than_one_plan_holds():
+    """20 distinct shapes (one plan takes 16 classes): the engine splits them
+    over plans; the grouped step and orthogonalize_many stay exact."""
+    eng = _engine_for("fp16", "auto")
+    shapes = [(64 + 16 * k, 96 + 32 * (k % 5)) for k in range(20)]
+    items, host = _items(shapes, torch.float32, 70, eng.device)
+    eng.muon_matrices(items, momentum=0.95, nesterov=True, weight_decay_factor=1.0, ns_steps=5)
+    torch.cuda.synchronize()
+    eng.check_errors(block=True)
+    assert len(eng._plans[next(reversed(eng._plans))].plans) == 2
+    for it, (p, g, m) in zip(items, host):
+        m_ref, d = O.momentum_direction(g, m, 0.95, True)
+        np.testing.assert_array_equal(it.exp_avg.cpu().numpy(), m_ref)
+        u = O.zeropower_via_newtonschulz5(d)
+        p_ref = O.apply_update(p, u, lr=0.02, weight_decay=0.0, eff=it.eff, param_dtype="float32",
+                               device_semantics="cuda")
+        assert O.rel_frobenius(it.param.cpu().numpy(), p_ref) < 1e-3
+    mats = [_rand(s, 90 + k).to(eng.device) for k, s in enumerate(shapes)]
+    outs = eng.orthogonalize_many(mats, [torch.float32] * len(mats))
+    for x, u in zip(mats, outs):
+        assert O.rel_frobenius(u.cpu().numpy(), O.zeropower_via_newtonschulz5(x.cpu().numpy())) < TF32_TOL
