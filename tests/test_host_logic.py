@@ -338,3 +338,56 @@ def test_waves_follow_geometric_flop_shares():
                                                  -ns_cost(shapes[i]), i))
             assert [waves[i] for i in by_bpf] == sorted(waves[i] for i in by_bpf)
     assert assign_waves(shapes, assign_owners(shapes, 2), 2, 1) == [0] * len(shapes)
+
+
+def test_partial_owner_choice_is_active_and_balanced():
+    """FSDP owner-only Newton-Schulz: each split matrix goes to one of its
+    active ranks, by LPT on FLOPs, identically on every rank."""
+    from opendm_b200.optimizer.muon_adamw import MuonAdamW, MuonShardPlan
+
+    shapes = [(512, 512), (256, 1024), (1024, 256), (128, 128), (64, 640), (640, 64)]
+    plans, idx = [], []
+    for j, s in enumerate(shapes):
+        n = s[0] * s[1]
+        active = (0, 1, 2) if j % 2 == 0 else (1, 2)
+        sizes = tuple(n // len(active) + (n % len(active) if r == active[-1] else 0) if r in active else 0
+                      for r in range(3))
+        plans.append(MuonShardPlan("partial", n, sizes[0], sizes, active, 0))
+        idx.append(j)
+    owners = MuonAdamW._partial_owners(plans, shapes, idx, 5)
+    assert owners == MuonAdamW._partial_owners(plans, shapes, idx, 5)
+    for j in idx:
+        assert owners[j] in plans[j].active_ranks
+    load = [0.0] * 3
+    for j, r in owners.items():
+        load[r] += ns_cost(shapes[j])
+    # greedy list scheduling's bound: the busiest rank carries at most the mean plus the largest job
+    assert max(load) <= sum(load) / 3 + max(ns_cost(s) for s in shapes)
+
+
+def test_flat_buckets_layout_repoints_parameters():
+    """Owned matrices are laid out per (wave, dtype) as [rank 0 | rank 1 | ...]
+    buckets of equal, 128-element-aligned size; parameters become views of
+    them with their values kept."""
+    from opendm_b200.sharding import FlatParamBuckets
+
+    torch.manual_seed(0)
+    shapes = [(8, 16), (4, 4), (16, 8), (3, 5), (10, 10)]
+    params = [torch.nn.Parameter(torch.randn(s)) for s in shapes]
+    before = [p.detach().clone() for p in params]
+    owners = [0, 1, 1, 0, 1]
+    waves = [0, 0, 1, 1, 0]
+    b = FlatParamBuckets(params, owners, 2, 0, None, waves)
+    assert b.n_waves == 2
+    for flat, bucket, wave in b.buffers:
+        assert bucket % 128 == 0 and flat.numel() == 2 * bucket
+        for i, p in enumerate(params):
+            if waves[i] != wave:
+                continue
+            off = p.data.storage_offset() - flat.storage_offset()
+            assert p.data.untyped_storage().data_ptr() == flat.untyped_storage().data_ptr()
+            assert owners[i] * bucket <= off < (owners[i] + 1) * bucket  # inside its owner's bucket
+    for p, w in zip(params, before):
+        assert torch.equal(p.detach(), w)
+    expect = sum(bucket * 4 for flat, bucket, _ in b.buffers)  # fp32, one peer's bucket per wave
+    assert b.nbytes_received() == expect
