@@ -5,7 +5,7 @@ dexmal/opendm, imported from a local checkout) on seeded inputs and stores its
 outputs as ``.npz`` files next to this script. Run it where the reference
 checkout exists (it is not needed at test time):
 
-    python tests/golden/make_golden.py [--reference PATH]
+    python tests/golden/make_golden.py --reference PATH   (or OPENDM_REFERENCE=PATH)
 
 Fixtures:
   ns_cases.npz           zeropower_via_newtonschulz5 on assorted shapes/steps
@@ -158,13 +158,16 @@ def _clip_cases() -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("OPENDM_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("OPENDM_REFERENCE"),
+                    help="checkout of dexmal/opendm (default: $OPENDM_REFERENCE)")
     ap.add_argument("--only", choices=["clip"], default=None)
     args = ap.parse_args()
     np.savez_compressed(os.path.join(HERE, "clip_cases.npz"), **_clip_cases())
     if args.only == "clip":
         print("wrote clip_cases.npz to", HERE)
         return
+    if not args.reference:
+        ap.error("the reference fixtures need --reference PATH (or OPENDM_REFERENCE)")
     sys.path.insert(0, args.reference)
     from opendm.optimizer import muon_adamw as ref  # noqa: E402
 
