@@ -328,7 +328,8 @@ def run_ours(args):
     mark_muon_parameters(model, predicate=lambda n, p: is_muon(*keymap[n]))
     opt = MuonAdamW(model, lr=LR, betas=BETAS, eps=EPS, weight_decay=WD, muon_momentum=MOMENTUM,
                     muon_ns_steps=NS_STEPS, precision=args.precision, state_sharding=world > 1,
-                    allgather=args.allgather, comm_sms=args.comm_sms)
+                    allgather=args.allgather, comm_sms=args.comm_sms,
+                    adamw_sharding=args.adamw_sharding and world > 1)
     params = list(model.parameters())
     ggen = torch.Generator(device=device).manual_seed(1)
     grads = []
@@ -434,6 +435,9 @@ def run_ours(args):
     mom_bytes = my_elems * {"tf32": 2 + 4 + 4 + 4, "bf16": 2 + 4 + 4 + 2, "fp16": 2 + 8 + 2 + 4 + 2}[args.precision]
     mom_gbs = mom_bytes / (mom_ms * 1e-3) / 1e9 if mom_ms > 0 else 0.0
     adam_elems = sum(math.prod(s) for n, s in spec if not is_muon(n, s))
+    adam_shards = opt._adam_shards.get(id(opt.param_groups[0]))
+    if adam_shards is not None:  # this rank's element ranges only
+        adam_elems = sum(n for _, _, n in adam_shards.owned(list(opt.param_groups[0]["params"])))
     adam_gbs = adam_elems * (2 + 2 + 8 + 8 + 2) / (adam_ms * 1e-3) / 1e9 if adam_ms > 0 else 0.0
 
     # ---- end-to-end through the public API with host-resident gradients
@@ -507,7 +511,9 @@ def run_ours(args):
             "config": {"workload": cfg, "description": DESCRIPTIONS[cfg], "muon_matrices": len(muon_shapes),
                        "ns_tflop_per_step": round(total_flops / 1e12, 2), "precision": args.precision,
                        "parallelism": f"dp{world}" + (" (FLOP-balanced NS owners, bf16 param all-gather,"
-                                                      " owner-only momentum)" if world > 1 else ""),
+                                                      " owner-only momentum"
+                                                      + (", AdamW element ranges per rank" if args.adamw_sharding
+                                                         else "") + ")" if world > 1 else ""),
                        "l2": "inputs larger than L2 (params+grads+state >> 126 MB)"},
             "e2e": {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches) * args.steps,
@@ -543,7 +549,9 @@ def run_ours(args):
                             "waves": bucket.n_waves if bucket is not None else 1,
                             "transport": opt.allgather,
                             "comm_sms": opt.comm_sms if opt.allgather == "nccl" else 0,
-                            "exposed_wait_ms": round(ag_wait_ms, 3)}
+                            "exposed_wait_ms": round(ag_wait_ms, 3),
+                            "adamw_allgather_bytes_received": (adam_shards.nbytes_received()
+                                                               if adam_shards is not None else 0)}
                            if world > 1 else None),
             "clocks": clocks,
             "cpu_baseline": cpu,
@@ -566,6 +574,8 @@ def main(argv=None):
     ap.add_argument("--allgather", default="nccl", choices=["nccl", "p2p"],
                     help="parameter all-gather of the sharded step (N > 1)")
     ap.add_argument("--comm-sms", type=int, default=32, help="SMs left to an overlapping NCCL all-gather")
+    ap.add_argument("--adamw-sharding", action="store_true",
+                    help="N > 1: each rank updates an equal range of the AdamW parameters, then all-gather")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3

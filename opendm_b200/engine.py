@@ -25,7 +25,7 @@ the tensors are not on an sm_100 device.
 from __future__ import annotations
 
 import math
-from ctypes import byref, c_float, c_int, c_void_p
+from ctypes import byref, c_float, c_int, c_void_p, sizeof
 from dataclasses import dataclass
 
 import torch
@@ -91,13 +91,15 @@ class _TableCache:
         self.device, self.capacity = device, capacity
         self._tables: dict[bytes, torch.Tensor] = {}
 
-    def get(self, raw: bytes) -> torch.Tensor:
-        t = self._tables.pop(raw, None)
+    def get(self, raw: bytes, key: bytes | None = None) -> torch.Tensor:
+        """The device copy of `raw`, cached under `key` (default: `raw`)."""
+        key = raw if key is None else key
+        t = self._tables.pop(key, None)
         if t is None:
             t = _upload(raw, self.device)
             while len(self._tables) >= self.capacity:
                 self._tables.pop(next(iter(self._tables)))
-        self._tables[raw] = t  # most recently used last
+        self._tables[key] = t  # most recently used last
         t.record_stream(torch.cuda.current_stream(self.device))  # reused later by kernels on this stream
         return t
 
@@ -177,6 +179,7 @@ class CudaMuonEngine:
         N.check(self.lib.muon_device_check(idx), "muon_device_check")
         self._plans: dict = {}  # matrix-set key -> _PlanState, least recently used first
         self._tables = _TableCache(self.device)
+        self._adam_tables = _TableCache(self.device, capacity=8)  # per-step scalars rewritten in place
         # At most this many SMs per Newton-Schulz launch (0: all), leaving the
         # rest to a collective that overlaps it.
         self.sm_limit = 0
@@ -689,6 +692,11 @@ class CudaMuonEngine:
         segs = []
         total = 0
         keep: list[torch.Tensor] = []
+        # With one step count for all items (the usual case) the table holds
+        # only pointers and sizes and stays cached on the device; the step
+        # size and bias correction are written into it by two fill kernels,
+        # so a steady-state step issues no host-to-device copy.
+        uniform = len({it.step for it in items}) == 1
         for it in items:
             for t in (it.param, it.grad, it.exp_avg, it.exp_avg_sq):
                 if t.device != self.device:
@@ -705,12 +713,22 @@ class CudaMuonEngine:
             total += int(self.lib.muon_adamw_chunks(s.numel))
             bc1 = 1 - beta1 ** it.step
             bc2 = 1 - beta2 ** it.step
-            s.step_size = lr / bc1
-            s.bc2_sqrt = bc2 ** 0.5
+            step_size, bc2_sqrt = lr / bc1, bc2 ** 0.5
+            if not uniform:
+                s.step_size, s.bc2_sqrt = step_size, bc2_sqrt
             s.param_dtype = _dtype_code(it.param)
             s.grad_dtype = _dtype_code(g)
             segs.append(s)
-        table = _upload(N.struct_bytes(segs), self.device)
+        raw = N.struct_bytes(segs)
+        if uniform:
+            stream = torch.cuda.current_stream(self.device)
+            table = self._adam_tables.get(raw, raw + stream.cuda_stream.to_bytes(8, "little"))
+            words = table.view(torch.float32).view(len(segs), sizeof(N.AdamwSeg) // 4)
+            # float32 rounding of the Python values, as the c_float fields would round them
+            words[:, N.AdamwSeg.step_size.offset // 4].fill_(step_size)
+            words[:, N.AdamwSeg.bc2_sqrt.offset // 4].fill_(bc2_sqrt)
+        else:
+            table = _upload(raw, self.device)
         wd_factor = 1.0 - lr * weight_decay if weight_decay != 0 else 1.0
         ev = self._event_pair("adamw")
         gs = self.grad_scale

@@ -59,6 +59,13 @@ The arithmetic runs in the sm_100a kernels of ``libopendm_muon.so`` through
   in peer-mapped memory and each rank pulls its peers' buckets with
   copy-engine memcpys ordered by cross-GPU flags (``opendm_b200.p2p``), so
   the Newton-Schulz keeps every SM.
+* ``adamw_sharding``: False (default: every rank runs the whole AdamW group,
+  as the reference does) or True (needs ``state_sharding=True`` and AdamW
+  parameters replicated on every rank, which the first step checks): the
+  AdamW parameters are split into equal contiguous element ranges, one per
+  rank; each rank updates its range and the ranges are all-gathered while
+  the Muon group's Newton-Schulz runs. ``consolidate_state_dict()`` brings
+  the AdamW moments together too.
 """
 
 from __future__ import annotations
@@ -71,7 +78,7 @@ import torch
 import torch.distributed as dist
 
 from ..engine import AdamItem, CudaMuonEngine, MatrixItem, effective_lr
-from ..sharding import FlatParamBuckets, assign_owners, assign_waves
+from ..sharding import FlatAdamShards, FlatParamBuckets, assign_owners, assign_waves
 
 _MUON_SHAPE = "_opendm_muon_shape"
 _MUON_NAME = "_opendm_muon_name"
@@ -198,7 +205,8 @@ class MuonAdamW(torch.optim.Optimizer):
                  precision: str = "fp16", scale_mode: str = "reference", sharding: str = "auto",
                  state_sharding: bool = False, process_group=None, ns_algo: str = "auto",
                  allgather_waves: int | None = None, comm_sms: int = 32, allgather: str = "nccl",
-                 fsdp_owner_ns: bool = True, max_grad_norm: float | None = None, _engine=None) -> None:
+                 fsdp_owner_ns: bool = True, max_grad_norm: float | None = None, adamw_sharding: bool = False,
+                 _engine=None) -> None:
         adamw_params, muon_params, muon_shapes, muon_names = [], [], [], []
         for param in model.parameters():
             if not param.requires_grad:
@@ -250,6 +258,11 @@ class MuonAdamW(torch.optim.Optimizer):
             raise ValueError(f"allgather must be 'nccl' or 'p2p', got {allgather!r}")
         self.allgather = allgather
         self.fsdp_owner_ns = bool(fsdp_owner_ns)
+        if adamw_sharding and not self.state_sharding:
+            raise ValueError("adamw_sharding needs state_sharding=True (each rank keeps only its range of the "
+                             "AdamW moments current)")
+        self.adamw_sharding = bool(adamw_sharding)
+        self._adam_shards: dict[int, FlatAdamShards | None] = {}
         self.max_grad_norm = None if max_grad_norm is None else float(max_grad_norm)
         self._pending_clip: torch.Tensor | None = None  # [total, coefficient] for the next step
         self.last_grad_norm: torch.Tensor | None = None
@@ -388,16 +401,26 @@ class MuonAdamW(torch.optim.Optimizer):
 
     def _step_groups(self) -> None:
         # Muon groups first, then AdamW: the groups update disjoint parameters,
-        # so the order changes no result, and the AdamW group's per-step
-        # host-to-device table copy (its bias corrections change every step)
-        # then comes last, where waiting behind other host-to-device transfers
-        # (e.g. the next batch's upload) delays nothing after it.
+        # so the order changes no result, and an AdamW host-to-device table
+        # copy (only when its parameters' step counts differ) then comes last,
+        # where waiting behind other host-to-device transfers (e.g. the next
+        # batch's upload) delays nothing after it.
+        # A sharded AdamW group goes first instead: its all-gather is queued
+        # ahead of the Muon waves' on the collective's stream and overlaps
+        # their Newton-Schulz (from wave 1 on, where SMs are left free for it).
+        adam = [g for g in self.param_groups if not g.get("use_muon", False)]
+        sharded = [g for g in adam if self._adam_shards_for(g) is not None]
+        handles = []
+        for group in sharded:
+            handles += self._adamw_step(group)
         for group in self.param_groups:
             if group.get("use_muon", False):
                 self._muon_step(group)
-        for group in self.param_groups:
-            if not group.get("use_muon", False):
+        for group in adam:
+            if not any(group is g for g in sharded):
                 self._adamw_step(group)
+        for h in handles:
+            h.wait()
 
     def _host_step(self, param, state) -> float:
         hs = self._host_steps.get(param)
@@ -405,9 +428,20 @@ class MuonAdamW(torch.optim.Optimizer):
             hs = float(state["step"].item())
         return hs
 
-    def _adamw_step(self, group: dict) -> None:
+    def _adamw_step(self, group: dict) -> list:
+        """AdamW over the group (reference :333-343); with AdamW sharding,
+        over this rank's ranges only, followed by the all-gather of the
+        ranges (its handles are returned; every rank joins it, with or
+        without gradients)."""
+        shards = self._adam_shards_for(group)
+        params = list(group["params"])
+        pieces: dict[int, list[tuple[int, int]]] | None = None
+        if shards is not None:
+            pieces = {}
+            for i, start, length in shards.owned(params):
+                pieces.setdefault(i, []).append((start, length))
         items, step_tensors = [], []
-        for param in group["params"]:
+        for index, param in enumerate(params):
             grad = param.grad
             if grad is None:
                 continue
@@ -417,14 +451,53 @@ class MuonAdamW(torch.optim.Optimizer):
             hs = self._host_step(param, state) + 1.0
             self._host_steps[param] = hs
             step_tensors.append(state["step"])
-            items.append(AdamItem(param.data, grad.detach(), state["exp_avg"], state["exp_avg_sq"], hs))
-        if not items:
-            return
-        torch._foreach_add_(step_tensors, 1.0)
-        beta1, beta2 = group["betas"]
-        self._get_engine(items[0].param.device).adamw(
-            items, lr=float(group["lr"]), beta1=float(beta1), beta2=float(beta2), eps=float(group["eps"]),
-            weight_decay=float(group.get("weight_decay", 0.0) or 0.0))
+            if pieces is None:
+                items.append(AdamItem(param.data, grad.detach(), state["exp_avg"], state["exp_avg_sq"], hs))
+                continue
+            if grad.numel() != param.numel():
+                raise RuntimeError("AdamW gradient shape mismatch.")
+            for key in ("exp_avg", "exp_avg_sq"):  # updated in place through flat views
+                if not state[key].is_contiguous():
+                    state[key] = state[key].contiguous()
+            flat = [t.reshape(-1) for t in (param.data, grad.detach(), state["exp_avg"], state["exp_avg_sq"])]
+            for start, length in pieces.get(index, ()):
+                items.append(AdamItem(*(t[start:start + length] for t in flat), hs))
+        if step_tensors:
+            torch._foreach_add_(step_tensors, 1.0)
+        if items:
+            beta1, beta2 = group["betas"]
+            self._get_engine(items[0].param.device).adamw(
+                items, lr=float(group["lr"]), beta1=float(beta1), beta2=float(beta2), eps=float(group["eps"]),
+                weight_decay=float(group.get("weight_decay", 0.0) or 0.0))
+        if shards is None:
+            return []
+        device = shards.buffers[0][0].device
+        return shards.sync(async_op=device.type == "cuda", group=self._allgather_group(device))
+
+    def _adam_shards_for(self, group: dict) -> FlatAdamShards | None:
+        """The group's flat AdamW ranges when AdamW sharding applies: on
+        first use (collective, on every rank) the parameters are checked to
+        be replicated (same sizes and the same float64 checksum everywhere)
+        and re-pointed into the flat buffers."""
+        key = id(group)
+        if key in self._adam_shards:
+            return self._adam_shards[key]
+        world, rank = self._world()
+        params = list(group["params"])
+        shards = None
+        if self.adamw_sharding and world > 1 and self.sharding != "off" and params:
+            device = self._device_for_params(params)
+            sizes = torch.tensor([float(p.numel()) for p in params], dtype=torch.float64, device=device)
+            sums = torch.stack([p.detach().sum(dtype=torch.float64) for p in params])
+            sig = torch.stack([sizes, sums]).view(torch.int64)  # compared bit for bit
+            everyone = [torch.empty_like(sig) for _ in range(world)]
+            dist.all_gather(everyone, sig, group=self.process_group)
+            if any(not torch.equal(e, everyone[0]) for e in everyone[1:]):
+                raise RuntimeError("adamw_sharding needs the AdamW parameters replicated on every rank "
+                                   "(DDP); they differ between ranks (FSDP shards?).")
+            shards = FlatAdamShards(params, world, rank, self.process_group)
+        self._adam_shards[key] = shards
+        return shards
 
     @staticmethod
     def _device_for_params(params: list[torch.Tensor]) -> torch.device:
@@ -833,12 +906,25 @@ class MuonAdamW(torch.optim.Optimizer):
     # ----------------------------------------------------------- checkpoints
     def consolidate_state_dict(self) -> None:
         """With ``state_sharding=True``: bring every momentum buffer from its
-        owner to all ranks (collective; call on every rank before saving)."""
+        owner to all ranks, and with ``adamw_sharding`` every AdamW moment
+        range from its rank (collective; call on every rank before saving)."""
         world, _ = self._world()
         if world <= 1 or not self.state_sharding:
             return
         for group in self.param_groups:
             if not group.get("use_muon", False):
+                shards = self._adam_shards.get(id(group))
+                if shards is None:
+                    continue
+                params = list(group["params"])
+                for index, owner, start, length in shards.ranges(params):
+                    state = self._state_for_param(params[index], self.state[params[index]])
+                    src = dist.get_global_rank(self.process_group, owner) if self.process_group is not None \
+                        else owner
+                    for key in ("exp_avg", "exp_avg_sq"):
+                        if not state[key].is_contiguous():
+                            state[key] = state[key].contiguous()
+                        dist.broadcast(state[key].view(-1)[start:start + length], src=src, group=self.process_group)
                 continue
             owners = self._owners.get(id(group))
             if owners is None:

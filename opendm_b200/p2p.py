@@ -57,8 +57,8 @@ class P2PFlatBuckets:
         self.n_waves = max(waves, default=0) + 1
         device = params[0].device
         self.device = device
-        # (flat, bucket elements, wave, peer views)
-        self.buffers: list[tuple[torch.Tensor, int, int, list]] = []
+        # (flat, bucket elements, wave, peer views, symmetric-memory handle)
+        self.buffers: list[tuple[torch.Tensor, int, int, list, object]] = []
         by_key: dict[tuple, list[int]] = {}
         for i, p in enumerate(params):
             by_key.setdefault((waves[i], str(p.dtype)), []).append(i)

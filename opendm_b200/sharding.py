@@ -162,3 +162,91 @@ class FlatParamBuckets:
     def nbytes_received(self) -> int:
         """Bytes each rank receives per sync."""
         return sum(b * flat.element_size() * (self.world_size - 1) for flat, b, _ in self.buffers)
+
+
+class FlatAdamShards:
+    """AdamW parameters replicated on every rank (DDP), re-pointed once into
+    one flat buffer per dtype and split into equal contiguous ranges, one per
+    rank (ZeRO-1 style). AdamW is elementwise, so a rank updates its range of
+    every parameter it overlaps, whole tensors or not: the reference runs the
+    full AdamW on every rank (muon_adamw.py:333-343), and a single embedding
+    (e.g. 151936 x 2048) dominates the group, so owners of whole tensors
+    would not balance. One ``all_gather_into_tensor`` per dtype then gives
+    every rank every range.
+
+    Layout per dtype: parameters back to back, each starting on a multiple of
+    ``ALIGN`` elements; the buffer is ``world_size`` ranges of ``range_numel``
+    elements (a multiple of ``ALIGN``), so every range and every sub-range a
+    rank updates starts 128-byte aligned or better."""
+
+    ALIGN = 64
+
+    def __init__(self, params: list[torch.Tensor], world_size: int, rank: int, process_group=None):
+        self.world_size = world_size
+        self.rank = rank
+        self.group = process_group
+        # (flat buffer, range elements, [(param index, flat offset)])
+        self.buffers: list[tuple[torch.Tensor, int, list[tuple[int, int]]]] = []
+        by_dtype: dict[str, list[int]] = {}
+        for i, p in enumerate(params):
+            by_dtype.setdefault(str(p.dtype), []).append(i)
+        for _, idxs in sorted(by_dtype.items()):
+            placed, total = [], 0
+            for i in idxs:
+                placed.append((i, total))
+                total += (params[i].numel() + self.ALIGN - 1) // self.ALIGN * self.ALIGN
+            per_rank = (total + world_size - 1) // world_size
+            per_rank = (per_rank + self.ALIGN - 1) // self.ALIGN * self.ALIGN
+            if per_rank == 0:
+                continue
+            dtype, device = params[idxs[0]].dtype, params[idxs[0]].device
+            flat = torch.zeros(per_rank * world_size, dtype=dtype, device=device)
+            for i, off in placed:
+                p = params[i]
+                view = flat[off:off + p.numel()].view(p.shape)
+                view.copy_(p.data)
+                p.data = view
+            self.buffers.append((flat, per_rank, placed))
+
+    def ranges(self, params: list[torch.Tensor]) -> list[tuple[int, int, int, int]]:
+        """Every (param index, owner rank, start, length) piece: the
+        intersection of each parameter with each rank's range, in element
+        offsets within the flattened parameter."""
+        out = []
+        for _, per_rank, placed in self.buffers:
+            for i, off in placed:
+                n = params[i].numel()
+                r0, r1 = off // per_rank, (off + max(n, 1) - 1) // per_rank
+                for r in range(r0, min(r1, self.world_size - 1) + 1):
+                    lo, hi = max(off, r * per_rank), min(off + n, (r + 1) * per_rank)
+                    if hi > lo:
+                        out.append((i, r, lo - off, hi - lo))
+        return out
+
+    def owned(self, params: list[torch.Tensor]) -> list[tuple[int, int, int]]:
+        """This rank's pieces: (param index, start, length)."""
+        return [(i, s, n) for i, r, s, n in self.ranges(params) if r == self.rank]
+
+    def sync(self, async_op: bool = False, group=None) -> list:
+        """All-gather every rank's range into all ranks (in place); with
+        ``async_op`` (CUDA only) the handles are returned, as in
+        ``FlatParamBuckets.sync``."""
+        handles = []
+        group = group if group is not None else self.group
+        for flat, per_rank, _ in self.buffers:
+            mine = flat[self.rank * per_rank:(self.rank + 1) * per_rank]
+            if flat.device.type == "cuda":
+                h = dist.all_gather_into_tensor(flat, mine, group=group, async_op=async_op)
+                if async_op:
+                    handles.append(h)
+            else:
+                parts = [torch.empty_like(mine) for _ in range(self.world_size)]
+                dist.all_gather(parts, mine.clone(), group=self.group)
+                for r, part in enumerate(parts):
+                    if r != self.rank:
+                        flat[r * per_rank:(r + 1) * per_rank].copy_(part)
+        return handles
+
+    def nbytes_received(self) -> int:
+        """Bytes each rank receives per sync."""
+        return sum(b * flat.element_size() * (self.world_size - 1) for flat, b, _ in self.buffers)

@@ -54,6 +54,20 @@ def _oracle(muon, adam, steps):
     return final, exp_avg
 
 
+def _oracle_adam_moments(muon, adam, steps):
+    """The oracle's AdamW (exp_avg, exp_avg_sq) per AdamW parameter."""
+    params, grads = _data(muon, adam, steps)
+    opt = O.OracleMuonAdamW(lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01)
+    mp_ = {str(i): params[i].copy() for i in range(len(muon))}
+    ap_ = {str(i): params[i].copy() for i in range(len(muon), len(params))}
+    for s in range(steps):
+        g = grads[s]
+        opt.step(mp_, {str(i): g[i] for i in range(len(muon))}, ap_,
+                 {str(i): g[i] for i in range(len(muon), len(params))})
+    return [(opt.adamw_state[str(i)].exp_avg, opt.adamw_state[str(i)].exp_avg_sq)
+            for i in range(len(muon), len(params))]
+
+
 def _worker(rank, port, scenario, muon, adam, steps, outdir, world=WORLD):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -69,7 +83,7 @@ def _worker(rank, port, scenario, muon, adam, steps, outdir, world=WORLD):
         params, grads = _data(muon, adam, steps)
         model = torch.nn.Module()
         n_muon = len(muon)
-        if scenario in ("replicated", "state_sharding", "fail", "waves"):
+        if scenario in ("replicated", "state_sharding", "fail", "waves", "adam_sharded"):
             for i, p in enumerate(params):
                 t = torch.nn.Parameter(torch.from_numpy(p.copy()))
                 if i < n_muon:
@@ -98,7 +112,8 @@ def _worker(rank, port, scenario, muon, adam, steps, outdir, world=WORLD):
                 model.register_parameter(f"p{i}", torch.nn.Parameter(torch.from_numpy(params[i].copy())))
         engine = OracleEngine()
         opt = MuonAdamW(model, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, _engine=engine,
-                        state_sharding=(scenario in ("state_sharding", "waves")),
+                        state_sharding=(scenario in ("state_sharding", "waves", "adam_sharded")),
+                        adamw_sharding=(scenario == "adam_sharded"),
                         allgather_waves=3 if scenario == "waves" else None,
                         fsdp_owner_ns=(scenario != "flat_ref"))
         plist = list(model.parameters())
@@ -112,11 +127,15 @@ def _worker(rank, port, scenario, muon, adam, steps, outdir, world=WORLD):
                     g = g.reshape(-1)[a:b]
                 p.grad = torch.from_numpy(g.copy())
             opt.step()
-        if scenario in ("state_sharding", "waves"):
+        if scenario == "adam_sharded":  # before consolidation: each rank's own ranges only
+            result["adam_pieces"] = opt._adam_shards[id(opt.param_groups[0])].owned(list(opt.param_groups[0]["params"]))
+        if scenario in ("state_sharding", "waves", "adam_sharded"):
             opt.consolidate_state_dict()
         result["params"] = [p.detach().numpy().copy() for p in plist]
         result["exp_avg"] = [opt.state[p]["exp_avg"].numpy().copy() if "exp_avg" in opt.state[p]
                              else np.zeros(0, np.float32) for p in plist[:n_muon]]
+        result["adam_moments"] = [(opt.state[p]["exp_avg"].numpy().copy(), opt.state[p]["exp_avg_sq"].numpy().copy())
+                                  for p in plist[n_muon:]]
         result["slices"] = slices
         result["muon_calls"] = engine.matrices_seen
         plans = opt._get_muon_shard_plans(opt.param_groups[1])
@@ -189,6 +208,32 @@ def test_allgather_waves_two_ranks(tmp_path):
 def test_owner_only_momentum_consolidates(tmp_path):
     res = _run("state_sharding", SMALL_MUON, SMALL_ADAM, 3, tmp_path)
     _check(res, SMALL_MUON, SMALL_ADAM, 3)
+
+
+def test_adamw_sharding_two_and_three_ranks(tmp_path):
+    """adamw_sharding: each rank updates an equal contiguous range of the
+    flat AdamW parameters (a vector split between ranks, whole small ones),
+    the ranges are all-gathered, and consolidation brings the moments
+    together; parameters and moments equal the single-process oracle."""
+    adam = [(5000,), (10,), (700,), (3,)]
+    for world in (2, 3):
+        res = _run("adam_sharded", SMALL_MUON, adam, 3, tmp_path, world=world)
+        _check(res, SMALL_MUON, adam, 3)
+        want = _oracle_adam_moments(SMALL_MUON, adam, 3)
+        for r in res:
+            for (m, v), (wm, wv) in zip(r["adam_moments"], want, strict=True):
+                assert O.rel_frobenius(m, wm) < 1e-6 and O.rel_frobenius(v, wv) < 1e-6, r["rank"]
+        pieces = [r["adam_pieces"] for r in res]
+        assert all(pieces)  # every rank owns a range
+        covered = {}
+        for ps in pieces:
+            for i, start, length in ps:
+                covered.setdefault(i, []).append((start, length))
+        for i, shape in enumerate(adam):  # the ranges tile every parameter exactly once
+            spans = sorted(covered[i])
+            assert spans[0][0] == 0 and sum(n for _, n in spans) == shape[0]
+            assert all(a + n == b for (a, n), (b, _) in zip(spans, spans[1:]))
+        assert len(covered[0]) >= 2  # the long vector is split between ranks
 
 
 def test_flat_shards_partial_and_owner_only(tmp_path):

@@ -313,6 +313,47 @@ def test_adamw_matches_oracle(engine, pdt, gdt):
         assert O.rel_frobenius(it.param.float().cpu().numpy(), p_ref) < (1e-3 if pdt == torch.bfloat16 else 1e-6)
 
 
+def test_adamw_cached_table_over_steps(engine):
+    """Three AdamW steps with a changing lr: items sharing one step count use
+    the device-cached table with the step size and bias correction filled in
+    place; the same items next to one a step ahead use an uploaded table.
+    Bit-identical every step, and equal to the oracle at the end."""
+    from opendm_b200.engine import AdamItem
+
+    shapes = [(1000,), (64, 33), (4096,), (7,)]
+    init = [(_rand(s, 500 + i, 0.02).to(torch.bfloat16), _rand(s, 600 + i, 1e-3).to(torch.bfloat16))
+            for i, s in enumerate(shapes)]
+
+    def fresh():
+        return [[p.to(engine.device), g.to(engine.device), torch.zeros(p.shape, device=engine.device),
+                 torch.zeros(p.shape, device=engine.device)] for p, g in init]
+
+    a, b = fresh(), fresh()
+    extra = [t.clone() for t in a[0]]
+    host = [(p.float().numpy(), g.float().numpy(), np.zeros(p.shape, np.float32), np.zeros(p.shape, np.float32))
+            for p, g in init]
+    for step in (1, 2, 3):
+        lr = 1e-3 * step
+        engine.adamw([AdamItem(*t, float(step)) for t in a], lr=lr, beta1=0.9, beta2=0.95, eps=1e-8,
+                     weight_decay=0.01)
+        engine.adamw([AdamItem(*t, float(step)) for t in b] + [AdamItem(*extra, float(step + 1))], lr=lr,
+                     beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.01)
+        torch.cuda.synchronize()
+        for ta, tb in zip(a, b):
+            for x, y in zip(ta, tb):
+                assert torch.equal(x, y), step
+        nxt = []
+        for p, g, m, v in host:
+            p, m, v, _ = O.adamw_step(p, g, m, v, step - 1.0, lr=lr, beta1=0.9, beta2=0.95, eps=1e-8,
+                                      weight_decay=0.01, param_dtype="bfloat16")
+            nxt.append((p, g, m, v))
+        host = nxt
+    for t, (p, _, m, v) in zip(a, host):
+        assert O.rel_frobenius(t[2].cpu().numpy(), m) < 1e-6
+        assert O.rel_frobenius(t[3].cpu().numpy(), v) < 1e-6
+        assert O.rel_frobenius(t[0].float().cpu().numpy(), p) < 1e-3
+
+
 def test_rejects_cpu_tensors():
     from opendm_b200.engine import CudaMuonEngine
 

@@ -5,7 +5,8 @@ every matrix (sharding="off", the reference's redundant schedule), with every
 momentum buffer current (state_sharding=False), with owner-only momentum
 consolidated afterwards (state_sharding=True), with the all-gather split
 into waves that overlap the Newton-Schulz of the next wave, over NCCL or over
-copy engines out of peer-mapped buffers (allgather="p2p").
+copy engines out of peer-mapped buffers (allgather="p2p"), and with the
+AdamW group split into per-rank element ranges (adamw_sharding=True).
 
 Bitwise equality holds because each matrix's kernels see the same inputs in
 both schedules and every reduction (momentum norm partials, tile K order) is
@@ -27,6 +28,15 @@ MUON = [(2048, 2048), (256, 2048), (256, 2048), (2048, 2048), (8192, 2048), (819
         (1000, 300), (72, 130)]
 ADAM = [(2048,), (2048,), (37,)]
 STEPS = 2
+# (name, sharding, state_sharding, waves, allgather); "adamw_sharded" also
+# splits the AdamW parameters into per-rank element ranges.
+RUNS = (("off", "off", False, None, "nccl"),
+        ("auto", "auto", False, None, "nccl"),
+        ("auto_owner", "auto", True, None, "nccl"),
+        ("waves", "auto", True, 3, "nccl"),
+        ("p2p", "auto", True, 3, "p2p"),
+        ("p2p_replicated_state", "auto", False, 2, "p2p"),
+        ("adamw_sharded", "auto", True, 3, "nccl"))
 
 
 def _port():
@@ -37,7 +47,7 @@ def _port():
     return port
 
 
-def _build(dev, sharding, state_sharding, waves=None, allgather="nccl"):
+def _build(dev, sharding, state_sharding, waves=None, allgather="nccl", adamw_sharding=False):
     from opendm_b200.optimizer import MuonAdamW
 
     g = torch.Generator(device=dev).manual_seed(11)
@@ -49,7 +59,8 @@ def _build(dev, sharding, state_sharding, waves=None, allgather="nccl"):
             t._opendm_muon_name = f"m{i}"
         model.register_parameter(f"p{i}", t)
     opt = MuonAdamW(model, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, sharding=sharding,
-                    state_sharding=state_sharding, allgather_waves=waves, allgather=allgather)
+                    state_sharding=state_sharding, allgather_waves=waves, allgather=allgather,
+                    adamw_sharding=adamw_sharding)
     return model, opt
 
 
@@ -65,13 +76,8 @@ def _worker(rank, port, outdir):
         dev = torch.device("cuda", rank)
         dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=timedelta(seconds=60), device_id=dev)
         runs = {}
-        for name, sharding, state_sharding, waves, ag in (("off", "off", False, None, "nccl"),
-                                                          ("auto", "auto", False, None, "nccl"),
-                                                          ("auto_owner", "auto", True, None, "nccl"),
-                                                          ("waves", "auto", True, 3, "nccl"),
-                                                          ("p2p", "auto", True, 3, "p2p"),
-                                                          ("p2p_replicated_state", "auto", False, 2, "p2p")):
-            model, opt = _build(dev, sharding, state_sharding, waves, ag)
+        for name, sharding, state_sharding, waves, ag in RUNS:
+            model, opt = _build(dev, sharding, state_sharding, waves, ag, adamw_sharding=name == "adamw_sharded")
             gg = torch.Generator(device=dev).manual_seed(12)
             for _ in range(STEPS):
                 for p in model.parameters():
@@ -82,6 +88,8 @@ def _worker(rank, port, outdir):
             owners = opt._owners.get(id(opt.param_groups[1]))
             runs[name] = {"params": [p.detach().cpu() for p in model.parameters()],
                           "exp_avg": [opt.state[p]["exp_avg"].cpu() for p in opt.param_groups[1]["params"]],
+                          "adam_moments": [(opt.state[p]["exp_avg"].cpu(), opt.state[p]["exp_avg_sq"].cpu())
+                                           for p in opt.param_groups[0]["params"]],
                           "owners": owners}
         result["runs"] = runs
         dist.barrier()
@@ -114,12 +122,14 @@ def test_two_gpu_sharded_equals_unsharded(tmp_path):
     owners = res[0]["runs"]["auto"]["owners"]
     assert owners is not None and set(owners) == {0, 1}  # both ranks own work
     for r in res:
-        for name in ("off", "auto", "auto_owner", "waves", "p2p", "p2p_replicated_state"):
+        for name, *_ in RUNS:
             run = r["runs"][name]
             for i, (got, want) in enumerate(zip(run["params"], ref["params"])):
                 assert torch.equal(got, want), (r["rank"], name, "param", i)
             for i, (got, want) in enumerate(zip(run["exp_avg"], ref["exp_avg"])):
                 assert torch.equal(got, want), (r["rank"], name, "exp_avg", i)
+            for i, (got, want) in enumerate(zip(run["adam_moments"], ref["adam_moments"])):
+                assert torch.equal(got[0], want[0]) and torch.equal(got[1], want[1]), (r["rank"], name, "adam", i)
 
 
 def _flat_worker(rank, port, outdir):

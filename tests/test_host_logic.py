@@ -391,3 +391,52 @@ def test_flat_buckets_layout_repoints_parameters():
         assert torch.equal(p.detach(), w)
     expect = sum(bucket * 4 for flat, bucket, _ in b.buffers)  # fp32, one peer's bucket per wave
     assert b.nbytes_received() == expect
+
+
+def test_flat_adam_shards_ranges_tile_and_align():
+    """AdamW sharding layout: per dtype, parameters back to back at
+    64-element boundaries, the flat buffer cut into equal 64-aligned ranges;
+    every parameter is covered exactly once by the ranks' pieces, each piece
+    starts aligned, parameters become views with their values kept, and the
+    dtypes get separate buffers."""
+    from opendm_b200.sharding import FlatAdamShards
+
+    torch.manual_seed(0)
+    shapes = [(1000,), (7,), (64, 33), (130,), (5,)]
+    dtypes = [torch.float32, torch.float32, torch.bfloat16, torch.float32, torch.bfloat16]
+    for world in (1, 2, 3, 4, 8):
+        params = [torch.nn.Parameter(torch.randn(s).to(d)) for s, d in zip(shapes, dtypes)]
+        before = [p.detach().clone() for p in params]
+        sh = FlatAdamShards(params, world, 0)
+        assert len(sh.buffers) == 2
+        for flat, per_rank, placed in sh.buffers:
+            assert per_rank % FlatAdamShards.ALIGN == 0 and flat.numel() == per_rank * world
+            for i, off in placed:
+                assert off % FlatAdamShards.ALIGN == 0 and params[i].dtype == flat.dtype
+                assert params[i].data.untyped_storage().data_ptr() == flat.untyped_storage().data_ptr()
+                assert params[i].data.storage_offset() - flat.storage_offset() == off
+        for p, w in zip(params, before):
+            assert torch.equal(p.detach(), w)
+        covered = {i: [] for i in range(len(shapes))}
+        for i, r, start, length in sh.ranges(params):
+            assert 0 <= r < world and length > 0
+            off = dict(sh.buffers[0][2] + sh.buffers[1][2])[i]
+            per_rank = next(b for _, b, pl in sh.buffers if any(j == i for j, _ in pl))
+            assert (off + start) % FlatAdamShards.ALIGN == 0  # piece starts 64-element aligned in the buffer
+            assert r * per_rank <= off + start and off + start + length <= (r + 1) * per_rank
+            covered[i].append((start, length))
+        for i, spans in covered.items():
+            spans.sort()
+            assert spans[0][0] == 0 and sum(n for _, n in spans) == params[i].numel()
+            assert all(a + n == b for (a, n), (b, _) in zip(spans, spans[1:]))
+        mine = sh.owned(params)
+        assert all((i, 0, s, n) in [(j, r, a, b) for j, r, a, b in sh.ranges(params)] for i, s, n in mine)
+        assert sh.nbytes_received() == sum(b * flat.element_size() * (world - 1) for flat, b, _ in sh.buffers)
+
+
+def test_adamw_sharding_needs_state_sharding():
+    model = torch.nn.Linear(8, 8, bias=True)
+    mark_muon_parameters(model, lambda n, p: p.ndim == 2)
+    with pytest.raises(ValueError, match="state_sharding"):
+        MuonAdamW(model, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, adamw_sharding=True,
+                  _engine=OracleEngine())
