@@ -309,7 +309,12 @@ class MuonAdamW(torch.optim.Optimizer):
         ``exp_avg``/``exp_avg_sq`` are fp32 on the parameter's device."""
         if "momentum_buffer" in state:
             state.setdefault("exp_avg", state.pop("momentum_buffer"))
-        step = state.get("step")
+        step, m, v = state.get("step"), state.get("exp_avg"), state.get("exp_avg_sq")
+        if (m is not None and v is not None and torch.is_tensor(step) and step.ndim == 0
+                and step.dtype is torch.float32 and m.dtype is torch.float32 and v.dtype is torch.float32):
+            dev = param.device
+            if step.device == dev and m.device == dev and v.device == dev:
+                return state  # already in the layout below (every step after the first)
         if step is None:
             state["step"] = torch.zeros((), dtype=torch.float32, device=param.device)
         elif not torch.is_tensor(step):
@@ -626,6 +631,7 @@ class MuonAdamW(torch.optim.Optimizer):
         owned = [[] for _ in range(n_waves)]
         others, partial, step_tensors = [], [], []
         partial_local: dict[int, tuple] = {}  # matrix index -> (param, grad, state, eff), local shards only
+        lr_scale, moonlight = float(group["muon_lr_scale"]), float(group["muon_moonlight_coefficient"])
         for index, (param, shape, plan) in enumerate(zip(group["params"], group["muon_shapes"], plans, strict=True)):
             if plan.local_numel == 0:
                 continue
@@ -637,19 +643,22 @@ class MuonAdamW(torch.optim.Optimizer):
                 raise RuntimeError(f"Muon gradient shape mismatch for {name}.")
             state = self._state_for_param(param, self.state[param])
             step_tensors.append(state["step"])
-            eff = effective_lr(lr, float(group["muon_lr_scale"]), float(group["muon_moonlight_coefficient"]),
-                               shape, self.scale_mode)
+            other = plan.kind != "partial" and owners is not None and owners[index] != rank
+            if other and self.state_sharding:
+                continue  # the owner advances this matrix's momentum; the all-gather brings the parameter
+            if other:  # momentum only
+                others.append(MatrixItem(param.data.view(shape),
+                                         grad.detach().view(shape) if grad is not None else None,
+                                         state["exp_avg"].view(shape)))
+                continue
+            eff = effective_lr(lr, lr_scale, moonlight, shape, self.scale_mode)
             if plan.kind == "partial":
                 partial.append((param, grad, state, shape, plan, eff))
                 partial_local[index] = (param, grad, state, eff)
                 continue
             item = MatrixItem(param.data.view(shape), grad.detach().view(shape) if grad is not None else None,
                               state["exp_avg"].view(shape), eff)
-            if owners is not None and owners[index] != rank:
-                if not self.state_sharding:
-                    others.append(item)
-            else:
-                owned[waves[index] if waves else 0].append(item)
+            owned[waves[index] if waves else 0].append(item)
         if step_tensors:
             torch._foreach_add_(step_tensors, 1.0)
         device = self._device_for_params(group["params"])
