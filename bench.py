@@ -384,6 +384,16 @@ def run_ours(args):
     events = engine.profile_events
     engine.profile_events = None
     opt.check_device_errors()
+    # host time to enqueue one step, each from an idle GPU (median of 3, max
+    # over ranks): the step is host-bound when this reaches the device time
+    host_times = []
+    for _ in range(3):
+        sync_all()
+        h0 = time.perf_counter()
+        opt.step()
+        host_times.append((time.perf_counter() - h0) * 1e3)
+    sync_all()
+    host_ms = max_over_ranks(sorted(host_times)[1])
     per = {}
     for name, s, e in events:
         per.setdefault(name, []).append(s.elapsed_time(e))
@@ -517,6 +527,7 @@ def run_ours(args):
                        "l2": "inputs larger than L2 (params+grads+state >> 126 MB)"},
             "e2e": {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches) * args.steps,
+            "host_enqueue_ms_per_step": round(host_ms, 3),
             "roofline": {"bound": "tensor", "kernel": f"ns_gemm ({ns_launches} grouped launches per step)",
                          "achieved": round(ns_tflops, 1), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(ns_tflops / peak, 4), "peak_source": f"{peaks['source']} bf16 sustained",
