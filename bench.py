@@ -458,10 +458,21 @@ def run_ours(args):
         owned_ids = {id(p) for p, o in zip(opt.param_groups[1]["params"], owners) if o == rank}
         muon_ids = {id(p) for p in opt.param_groups[1]["params"]}
         needed = [i for i, p in enumerate(params) if id(p) not in muon_ids or id(p) in owned_ids]
-    host_grads = {i: grads[i].cpu().pin_memory() for i in needed}
+    # Element ranges read per gradient: whole tensors, except that with AdamW
+    # sharding a rank reads only its ranges of the AdamW gradients.
+    spans = {i: [(0, params[i].numel())] for i in needed}
+    if adam_shards is not None:
+        aparams = list(opt.param_groups[0]["params"])
+        index_of = {id(p): i for i, p in enumerate(params)}
+        for p in aparams:
+            spans[index_of[id(p)]] = []
+        for j, start, length in adam_shards.owned(aparams):
+            spans[index_of[id(aparams[j])]].append((start, length))
+    host_grads = {i: [(a, n, grads[i].reshape(-1)[a:a + n].cpu().pin_memory()) for a, n in sp]
+                  for i, sp in spans.items()}
     probe = params[-1] if params[-1].ndim == 1 else params[0]
     readback = torch.empty(min(probe.numel(), 4096), dtype=probe.dtype).pin_memory()
-    h2d = sum(g.numel() * g.element_size() for g in host_grads.values())
+    h2d = sum(t.numel() * t.element_size() for lst in host_grads.values() for *_, t in lst)
     d2h = readback.numel() * readback.element_size()
     e2e_steps = max(2, min(args.steps, 10))
     # Double-buffered input pipeline: step k+1's gradients upload on a copy
@@ -480,8 +491,10 @@ def run_ours(args):
             with torch.cuda.stream(copy_stream):
                 if k >= 2:
                     copy_stream.wait_event(free[k % 2])  # step k-2 no longer reads this set
-                for i, hg in host_grads.items():
-                    gbufs[k % 2][i].copy_(hg, non_blocking=True)
+                for i, lst in host_grads.items():
+                    flat = gbufs[k % 2][i].view(-1)
+                    for a, n, hg in lst:
+                        flat[a:a + n].copy_(hg, non_blocking=True)
                 ready[k % 2].record(copy_stream)
 
         upload(0)

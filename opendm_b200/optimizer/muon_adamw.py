@@ -263,6 +263,8 @@ class MuonAdamW(torch.optim.Optimizer):
                              "AdamW moments current)")
         self.adamw_sharding = bool(adamw_sharding)
         self._adam_shards: dict[int, FlatAdamShards | None] = {}
+        self._adam_pending: list[FlatAdamShards] = []  # ranges updated this step, all-gather not yet queued
+        self._adam_handles: list = []
         self.max_grad_norm = None if max_grad_norm is None else float(max_grad_norm)
         self._pending_clip: torch.Tensor | None = None  # [total, coefficient] for the next step
         self.last_grad_norm: torch.Tensor | None = None
@@ -410,22 +412,38 @@ class MuonAdamW(torch.optim.Optimizer):
         # copy (only when its parameters' step counts differ) then comes last,
         # where waiting behind other host-to-device transfers (e.g. the next
         # batch's upload) delays nothing after it.
-        # A sharded AdamW group goes first instead: its all-gather is queued
-        # ahead of the Muon waves' on the collective's stream and overlaps
-        # their Newton-Schulz (from wave 1 on, where SMs are left free for it).
+        # A sharded AdamW group goes first instead, and the all-gather of its
+        # ranges is queued right after the first Muon wave's (_flush_adam_sync):
+        # it then overlaps the Newton-Schulz of wave 1 on, which leaves SMs
+        # free for collectives. Issued earlier it would hold SMs that wave 0's
+        # persistent CTAs wait for.
         adam = [g for g in self.param_groups if not g.get("use_muon", False)]
         sharded = [g for g in adam if self._adam_shards_for(g) is not None]
-        handles = []
-        for group in sharded:
-            handles += self._adamw_step(group)
-        for group in self.param_groups:
-            if group.get("use_muon", False):
-                self._muon_step(group)
-        for group in adam:
-            if not any(group is g for g in sharded):
+        self._adam_handles = []
+        self._adam_pending = []
+        try:
+            for group in sharded:
                 self._adamw_step(group)
-        for h in handles:
-            h.wait()
+                self._adam_pending.append(self._adam_shards[id(group)])
+            for group in self.param_groups:
+                if group.get("use_muon", False):
+                    self._muon_step(group)
+            self._flush_adam_sync()
+            for group in adam:
+                if not any(group is g for g in sharded):
+                    self._adamw_step(group)
+            for h in self._adam_handles:
+                h.wait()
+        finally:
+            self._adam_pending, self._adam_handles = [], []
+
+    def _flush_adam_sync(self) -> None:
+        """Queue the all-gather of the sharded AdamW ranges updated this step
+        (once; every rank reaches it at the same point of the step)."""
+        pending, self._adam_pending = self._adam_pending, []
+        for shards in pending:
+            device = shards.buffers[0][0].device
+            self._adam_handles += shards.sync(async_op=device.type == "cuda", group=self._allgather_group(device))
 
     def _host_step(self, param, state) -> float:
         hs = self._host_steps.get(param)
@@ -433,11 +451,10 @@ class MuonAdamW(torch.optim.Optimizer):
             hs = float(state["step"].item())
         return hs
 
-    def _adamw_step(self, group: dict) -> list:
+    def _adamw_step(self, group: dict) -> None:
         """AdamW over the group (reference :333-343); with AdamW sharding,
-        over this rank's ranges only, followed by the all-gather of the
-        ranges (its handles are returned; every rank joins it, with or
-        without gradients)."""
+        over this rank's ranges only (the caller queues the all-gather of the
+        ranges, which every rank joins, with or without gradients)."""
         shards = self._adam_shards_for(group)
         params = list(group["params"])
         pieces: dict[int, list[tuple[int, int]]] | None = None
@@ -474,10 +491,6 @@ class MuonAdamW(torch.optim.Optimizer):
             self._get_engine(items[0].param.device).adamw(
                 items, lr=float(group["lr"]), beta1=float(beta1), beta2=float(beta2), eps=float(group["eps"]),
                 weight_decay=float(group.get("weight_decay", 0.0) or 0.0))
-        if shards is None:
-            return []
-        device = shards.buffers[0][0].device
-        return shards.sync(async_op=device.type == "cuda", group=self._allgather_group(device))
 
     def _adam_shards_for(self, group: dict) -> FlatAdamShards | None:
         """The group's flat AdamW ranges when AdamW sharding applies: on
@@ -679,6 +692,8 @@ class MuonAdamW(torch.optim.Optimizer):
                     engine.muon_matrices(owned[w], momentum=momentum, nesterov=nesterov,
                                          weight_decay_factor=wd_factor, ns_steps=ns_steps)
                     buckets.wave_done(w)
+                    if w == 0:
+                        self._flush_adam_sync()
             else:
                 ag_group = self._allgather_group(device)
                 overlap = device.type == "cuda" and n_waves > 1 and hasattr(engine, "sm_limit")
@@ -690,6 +705,8 @@ class MuonAdamW(torch.optim.Optimizer):
                         engine.muon_matrices(owned[w], momentum=momentum, nesterov=nesterov,
                                              weight_decay_factor=wd_factor, ns_steps=ns_steps)
                         handles += buckets.sync(wave=w, async_op=device.type == "cuda", group=ag_group)
+                        if w == 0:
+                            self._flush_adam_sync()
                 finally:
                     if overlap:
                         engine.sm_limit = 0

@@ -114,10 +114,24 @@ def _worker(rank, port, scenario, muon, adam, steps, outdir, world=WORLD):
         opt = MuonAdamW(model, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, _engine=engine,
                         state_sharding=(scenario in ("state_sharding", "waves", "adam_sharded")),
                         adamw_sharding=(scenario == "adam_sharded"),
-                        allgather_waves=3 if scenario == "waves" else None,
+                        allgather_waves=3 if scenario in ("waves", "adam_sharded") else None,
                         fsdp_owner_ns=(scenario != "flat_ref"))
         plist = list(model.parameters())
+        order = []  # collective order of the last step (scenario adam_sharded)
+        if scenario == "adam_sharded":
+            from opendm_b200 import sharding as S
+
+            def rec(cls, tag):
+                orig = cls.sync
+
+                def sync(self, *a, **kw):
+                    order.append(tag(kw))
+                    return orig(self, *a, **kw)
+                cls.sync = sync
+            rec(S.FlatParamBuckets, lambda kw: f"wave{kw.get('wave')}")
+            rec(S.FlatAdamShards, lambda kw: "adamw")
         for s in range(steps):
+            order.clear()
             if scenario == "fail" and rank == 1 and s == 1:
                 raise SystemExit(3)  # this rank dies between steps
             for i, p in enumerate(plist):
@@ -134,6 +148,7 @@ def _worker(rank, port, scenario, muon, adam, steps, outdir, world=WORLD):
         result["params"] = [p.detach().numpy().copy() for p in plist]
         result["exp_avg"] = [opt.state[p]["exp_avg"].numpy().copy() if "exp_avg" in opt.state[p]
                              else np.zeros(0, np.float32) for p in plist[:n_muon]]
+        result["order"] = list(order)
         result["adam_moments"] = [(opt.state[p]["exp_avg"].numpy().copy(), opt.state[p]["exp_avg_sq"].numpy().copy())
                                   for p in plist[n_muon:]]
         result["slices"] = slices
@@ -216,10 +231,15 @@ def test_adamw_sharding_two_and_three_ranks(tmp_path):
     the ranges are all-gathered, and consolidation brings the moments
     together; parameters and moments equal the single-process oracle."""
     adam = [(5000,), (10,), (700,), (3,)]
+    muon = C1_MUON[:4] + SMALL_MUON  # three Muon waves: the ranges' all-gather goes between waves 0 and 1
     for world in (2, 3):
-        res = _run("adam_sharded", SMALL_MUON, adam, 3, tmp_path, world=world)
-        _check(res, SMALL_MUON, adam, 3)
-        want = _oracle_adam_moments(SMALL_MUON, adam, 3)
+        res = _run("adam_sharded", muon, adam, 3, tmp_path, world=world)
+        _check(res, muon, adam, 3)
+        assert len(set(res[0]["waves"])) >= 2
+        for r in res:  # the ranges' all-gather is queued right after wave 0's
+            assert r["order"][0] == "wave0" and r["order"][1] == "adamw", r["order"]
+            assert r["order"].count("adamw") == 1
+        want = _oracle_adam_moments(muon, adam, 3)
         for r in res:
             for (m, v), (wm, wv) in zip(r["adam_moments"], want, strict=True):
                 assert O.rel_frobenius(m, wm) < 1e-6 and O.rel_frobenius(v, wv) < 1e-6, r["rank"]
