@@ -415,6 +415,18 @@ def run_ours(args):
     else:
         mine = muon_shapes
     my_flops = sum(ns_flops(s) for s in mine)
+    owner_balance = None
+    if owners is not None:  # Newton-Schulz FLOPs per rank, max / mean (dense count and executed)
+        from opendm_b200.sharding import load_balance
+
+        shapes_all = opt.param_groups[1]["muon_shapes"]
+        dense = round(load_balance(shapes_all, owners, world, NS_STEPS)["max_over_mean"], 4)
+        loads = [0.0] * world  # executed FLOPs, with the form the library picks for each shape
+        for shp, o in zip(shapes_all, owners):
+            form = engine.lib.muon_ns_choose_algo(shp[0], shp[1], engine.op_dtype, NS_STEPS)
+            loads[o] += ns_executed_flops(shp, algo="gram" if form == 1 else "standard")
+        executed = round(max(loads) / (sum(loads) / world), 4) if sum(loads) > 0 else 1.0
+        owner_balance = {"dense": dense, "executed": executed}
     # the algorithm each shape class ran (the engine's classes, as planned)
     algo_of = {(cs.rows, cs.cols): ("gram" if int(cs.cls.algo) == 1 else "standard") for cs in engine.classes}
     my_exec = sum(ns_executed_flops(s, algo=algo_of.get(tuple(s), "standard")) for s in mine)
@@ -575,7 +587,8 @@ def run_ours(args):
                             "comm_sms": opt.comm_sms if opt.allgather == "nccl" else 0,
                             "exposed_wait_ms": round(ag_wait_ms, 3),
                             "adamw_allgather_bytes_received": (adam_shards.nbytes_received()
-                                                               if adam_shards is not None else 0)}
+                                                               if adam_shards is not None else 0),
+                            "owner_load_max_over_mean": owner_balance}
                            if world > 1 else None),
             "clocks": clocks,
             "cpu_baseline": cpu,
