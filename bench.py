@@ -9,7 +9,9 @@ metric is quoted on):
   c2  2B-class decoder, 28 layers, hidden 2048, GQA q/o 2048x2048, k/v 256x2048,
       SwiGLU gate/up 8192x2048, down 2048x8192 (196 Muon matrices) + norms and a
       151936x2048 embedding on AdamW. Default; at N > 1 the same model is
-      sharded over the ranks (strong scaling).
+      sharded over the ranks (strong scaling): Newton-Schulz owners with
+      owner-only momentum, and the AdamW group split into per-rank element
+      ranges (--no-adamw-sharding keeps the whole AdamW group on every rank).
   c4  ~4B VLA stack: ViT 27x (1152, MLP 4304) + LM 36x (2560, kv 512, MLP 9728)
       + action expert 18x (1024, MLP 4096), 540 Muon matrices + norms.
   c5  7B-class decoder, 32 layers, hidden 4096, MLP 11008 (224 Muon matrices),
@@ -611,8 +613,9 @@ def main(argv=None):
     ap.add_argument("--allgather", default="nccl", choices=["nccl", "p2p"],
                     help="parameter all-gather of the sharded step (N > 1)")
     ap.add_argument("--comm-sms", type=int, default=32, help="SMs left to an overlapping NCCL all-gather")
-    ap.add_argument("--adamw-sharding", action="store_true",
-                    help="N > 1: each rank updates an equal range of the AdamW parameters, then all-gather")
+    ap.add_argument("--adamw-sharding", action=argparse.BooleanOptionalAction, default=True,
+                    help="N > 1: each rank updates an equal range of the AdamW parameters, then all-gather "
+                         "(default on; --no-adamw-sharding runs the whole AdamW group on every rank)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
