@@ -504,6 +504,11 @@ class MuonAdamW(torch.optim.Optimizer):
         params = list(group["params"])
         shards = None
         if self.adamw_sharding and world > 1 and self.sharding != "off" and params:
+            for g in self.param_groups:  # a model in FSDP shards has non-replicated Muon plans
+                if g.get("use_muon", False) and g["params"] and \
+                        any(p.kind != "replicated" for p in self._get_muon_shard_plans(g)):
+                    raise RuntimeError("adamw_sharding needs replicated parameters (DDP); the Muon matrices "
+                                       "are sharded here (FSDP?).")
             device = self._device_for_params(params)
             sizes = torch.tensor([float(p.numel()) for p in params], dtype=torch.float64, device=device)
             sums = torch.stack([p.detach().sum(dtype=torch.float64) for p in params])

@@ -112,8 +112,8 @@ def _worker(rank, port, scenario, muon, adam, steps, outdir, world=WORLD):
                 model.register_parameter(f"p{i}", torch.nn.Parameter(torch.from_numpy(params[i].copy())))
         engine = OracleEngine()
         opt = MuonAdamW(model, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, _engine=engine,
-                        state_sharding=(scenario in ("state_sharding", "waves", "adam_sharded")),
-                        adamw_sharding=(scenario == "adam_sharded"),
+                        state_sharding=(scenario in ("state_sharding", "waves", "adam_sharded", "flat_adam")),
+                        adamw_sharding=(scenario in ("adam_sharded", "flat_adam")),
                         allgather_waves=3 if scenario in ("waves", "adam_sharded") else None,
                         fsdp_owner_ns=(scenario != "flat_ref"))
         plist = list(model.parameters())
@@ -254,6 +254,15 @@ def test_adamw_sharding_two_and_three_ranks(tmp_path):
             assert spans[0][0] == 0 and sum(n for _, n in spans) == shape[0]
             assert all(a + n == b for (a, n), (b, _) in zip(spans, spans[1:]))
         assert len(covered[0]) >= 2  # the long vector is split between ranks
+
+
+def test_adamw_sharding_refuses_fsdp_shards(tmp_path):
+    """adamw_sharding with Muon matrices in FSDP-style flat shards: the first
+    step raises on every rank (the AdamW parameters may be shards too, even
+    where their sizes and checksums agree)."""
+    res = _run("flat_adam", SMALL_MUON, SMALL_ADAM, 1, tmp_path)
+    for r in res:
+        assert "adamw_sharding needs replicated parameters" in r.get("error", ""), r
 
 
 def test_flat_shards_partial_and_owner_only(tmp_path):
