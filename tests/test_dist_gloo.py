@@ -302,3 +302,44 @@ def test_rank_failure_surfaces_as_error(tmp_path):
     res = _run("fail", SMALL_MUON, SMALL_ADAM, 3, tmp_path)
     assert res[1].get("exited")
     assert "error" in res[0], "surviving rank should report a collective error"
+
+
+def _bad_shards_worker(rank, port, outdir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+
+    from opendm_b200.optimizer import MuonAdamW
+    from tests.oracle_engine import OracleEngine
+
+    result = {"rank": rank}
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=2, timeout=timedelta(seconds=20))
+        model = torch.nn.Module()
+        p = torch.nn.Parameter(torch.zeros(6))  # 6 + 6 elements of a 4 x 4 matrix: neither shards nor copies
+        p._opendm_muon_shape, p._opendm_muon_name = (4, 4), "w"
+        model.register_parameter("w", p)
+        opt = MuonAdamW(model, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0, _engine=OracleEngine())
+        p.grad = torch.zeros(6)
+        opt.step()
+    except Exception as exc:
+        result["error"] = f"{type(exc).__name__}: {exc}"
+    torch.save(result, os.path.join(outdir, f"rank{rank}.pt"))
+
+
+def test_unreconstructable_shard_sizes_raise(tmp_path):
+    """Reference :487-491: local sizes that are neither a split of the matrix
+    nor full copies raise on every rank."""
+    ctx = mp.get_context("spawn")
+    port = _port()
+    procs = [ctx.Process(target=_bad_shards_worker, args=(r, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("rank did not finish")
+    for r in range(2):
+        res = torch.load(os.path.join(tmp_path, f"rank{r}.pt"), weights_only=False)
+        assert "cannot be reconstructed from local shard sizes (6, 6)" in res.get("error", ""), res

@@ -440,3 +440,33 @@ def test_adamw_sharding_needs_state_sharding():
     with pytest.raises(ValueError, match="state_sharding"):
         MuonAdamW(model, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, adamw_sharding=True,
                   _engine=OracleEngine())
+
+
+def test_more_option_validation():
+    m = Tiny()
+    mark_muon_parameters(m)
+    for kw in ({"ns_algo": "fast"}, {"allgather_waves": 0}, {"allgather": "mpi"}):
+        with pytest.raises(ValueError):
+            MuonAdamW(m, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0, _engine=OracleEngine(), **kw)
+
+
+def test_shard_plan_errors_single_process():
+    """Reference :443-535 error paths: a local tensor larger than the marked
+    matrix, a partial tensor without a process group, a local tensor that no
+    longer matches its plan, and an unknown plan kind."""
+    from opendm_b200.optimizer.muon_adamw import MuonShardPlan as Plan
+
+    for numel, match in ((32, "has only 16 elements"), (8, "expected 0 or 16")):
+        model = torch.nn.Module()
+        p = torch.nn.Parameter(torch.zeros(numel))
+        p._opendm_muon_shape, p._opendm_muon_name = (4, 4), "w"
+        model.register_parameter("w", p)
+        opt = MuonAdamW(model, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0, _engine=OracleEngine())
+        p.grad = torch.zeros(numel)
+        with pytest.raises(RuntimeError, match=match):
+            opt.step()
+    plan = Plan("local", 16, 16, (16,), (0,), 0)
+    with pytest.raises(RuntimeError, match="no longer matches"):
+        MuonAdamW._gather_matrix(torch.zeros(8), plan)
+    with pytest.raises(RuntimeError, match="Unknown Muon shard plan kind"):
+        MuonAdamW._gather_matrix(torch.zeros(16), Plan("striped", 16, 16, (16,), (0,), 0))
