@@ -1,0 +1,137 @@
+"""TEST INFRASTRUCTURE, not part of the product: a numpy emulation of the
+arithmetic of the Newton-Schulz kernels (opendm_b200/csrc/ns_gemm.cu) in
+fp16 mode, used by tests/test_ns_emulation.py to check the numerics design on
+the CPU against the fp32 oracle of the reference algorithm
+(muon_oracle.zeropower_via_newtonschulz5, reference muon_adamw.py:101-128).
+
+Modelled: every stored operand rounded to fp16 (subnormals included) after a
+power-of-two scale; products accumulated exactly and rounded once to fp32
+(the tensor cores accumulate in fp32 in a different order, so this is an
+approximation of the accumulation error, not of the operand rounding);
+epilogue arithmetic in fp32. Two forms:
+
+* standard: the reference's iteration on X in the shifted form
+  X <- (alpha I + A' B') X with A' = X X^T - I, B' = gamma A' + beta I;
+* gram: the iteration on A = X X^T, A <- P (P A) with P = alpha I + A' B',
+  accumulating Q = P ... P and applying X <- Q X every `restart` iterations.
+
+Scales (as the kernels choose them): X at iteration 0 times 2^round(log2
+sqrt(m n)), later times 2^round(log2 sqrt(n)); gram-form A, P and P A times
+2^round(log2(m / 4)), Q times 2^round(log2(m / 64)).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+NS_A, NS_B, NS_C = 3.4445, -4.7750, 2.0315  # reference muon_adamw.py:123
+ALPHA, BETA, GAMMA = NS_A + NS_B + NS_C, NS_B + 2 * NS_C, NS_C
+
+
+def _f16(x: np.ndarray) -> np.ndarray:
+    return np.asarray(x, np.float64).astype(np.float16).astype(np.float64)
+
+
+def _f32(x: np.ndarray) -> np.ndarray:
+    return np.asarray(x, np.float64).astype(np.float32).astype(np.float64)
+
+
+def _pow2(x: float) -> float:
+    """The power of two nearest to x in the log domain, halves rounded away
+    from zero (C's lround, as the library rounds)."""
+    e = math.log2(x)
+    return 2.0 ** int(math.floor(e + 0.5) if e >= 0 else -math.floor(-e + 0.5))
+
+
+def x_scale(m: int, n: int, iteration: int) -> float:
+    """Power-of-two scale of the stored X at `iteration` (m <= n): the
+    unit-norm input's entries are ~1/sqrt(m n), later iterates' ~1/sqrt(n)."""
+    return _pow2(math.sqrt(m * n)) if iteration == 0 else _pow2(math.sqrt(n))
+
+
+def _prepare(g: np.ndarray, eps: float = 1e-7) -> tuple[np.ndarray, bool]:
+    """Frobenius-normalised input, wide orientation (m <= n)."""
+    x = np.asarray(g, np.float64)
+    norm = math.sqrt(float(np.sum(_f32(x) ** 2)))
+    tall = x.shape[0] > x.shape[1]
+    if tall:
+        x = x.T
+    return x / max(norm, eps), tall
+
+
+def emulate_standard(g: np.ndarray, steps: int = 5) -> np.ndarray:
+    """The standard (iterate-on-X) form as the fp16 kernels compute it."""
+    x, tall = _prepare(g)
+    m, n = x.shape
+    eye = np.eye(m)
+    s = x_scale(m, n, 0)
+    xs = _f16(x * s)
+    for it in range(steps):
+        a = _f32(xs @ xs.T) / (s * s)
+        ap = a - eye
+        bp = GAMMA * ap + BETA * eye
+        mm = _f16(_f32(_f16(ap) @ _f16(bp)) + ALPHA * eye)
+        last = it == steps - 1
+        s_next = 1.0 if last else x_scale(m, n, it + 1)
+        acc = _f32(mm @ xs) * (s_next / s)
+        xs = _f32(acc) if last else _f16(acc)
+        s = s_next
+    return (xs.T if tall else xs).astype(np.float32)
+
+
+def emulate_gram(g: np.ndarray, steps: int = 5, restart: int = 3) -> np.ndarray:
+    """The gram form (iterate on X X^T, restart every `restart` iterations)
+    as the fp16 kernels compute it."""
+    x, tall = _prepare(g)
+    m, n = x.shape
+    eye = np.eye(m)
+    s = x_scale(m, n, 0)
+    xs = _f16(x * s)
+    sa, sq = _pow2(m / 4.0), _pow2(m / 64.0)
+    bounds = list(range(0, steps, restart)) + [steps]
+    for s0, s1 in zip(bounds, bounds[1:]):
+        p = pa = q = None
+        for j in range(s0, s1):
+            a = _f32(xs @ xs.T) / (s * s) if j == s0 else _f32(p @ pa) / (sa * sa)
+            ap = a - eye
+            bp = GAMMA * ap + BETA * eye
+            p_true = _f32(_f16(ap * sa) @ _f16(bp * sa)) / (sa * sa) + ALPHA * eye
+            p = _f16(p_true * sa)
+            q = _f16(p_true * sq) if j == s0 else _f16(_f32(p @ q) / sa)
+            if j < s1 - 1:
+                pa = _f16(_f32(p @ _f16(a * sa)) / sa)
+        last = s1 == steps
+        s_next = 1.0 if last else x_scale(m, n, s1)
+        acc = _f32(q @ xs) * (s_next / (sq * s))
+        xs = _f32(acc) if last else _f16(acc)
+        s = s_next
+    return (xs.T if tall else xs).astype(np.float32)
+
+
+def structured_input(shape: tuple[int, int], kind: str, seed: int = 0) -> np.ndarray:
+    """Seeded test matrices with the spectra the numerics notes discuss:
+    "gauss", "lowrank_noise" (rank 4 plus 10% noise), "heavytail" (1% of
+    entries x100), "powerlaw" (singular values 1/k), "expdecay" (e^(-10 k/r)),
+    "rank1"."""
+    rng = np.random.default_rng(seed)
+    m, n = shape
+    g = rng.standard_normal(shape)
+    if kind == "gauss":
+        out = g
+    elif kind == "lowrank_noise":
+        out = 0.1 * g + rng.standard_normal((m, 4)) @ rng.standard_normal((4, n))
+    elif kind == "heavytail":
+        out = np.where(rng.random(shape) < 0.01, g * 100.0, g)
+    elif kind == "rank1":
+        out = np.outer(rng.standard_normal(m), rng.standard_normal(n))
+    elif kind in ("powerlaw", "expdecay"):
+        k = min(shape)
+        u, _ = np.linalg.qr(rng.standard_normal((m, k)))
+        v, _ = np.linalg.qr(rng.standard_normal((n, k)))
+        sv = np.arange(1, k + 1) ** -1.0 if kind == "powerlaw" else np.exp(-10.0 * np.arange(k) / k)
+        out = (u * sv) @ v.T
+    else:
+        raise ValueError(f"unknown input kind {kind!r}")
+    return out.astype(np.float32)

@@ -1,0 +1,60 @@
+"""The Newton-Schulz numerics design checked on the CPU (no GPU): an emulation
+of the fp16 kernels' operand rounding (oracle/ns_emulation.py) against the
+fp32 oracle of the reference algorithm (reference muon_adamw.py:101-128).
+
+* both forms, the shifted standard iteration and the gram iteration with a
+  restart every 3 iterations, stay within the 1e-2 update bar on Gaussian,
+  heavy-tailed, low-rank-plus-noise, power-law and e^-10-decaying spectra, and
+  the gram form stays within 2x of the standard form (the GPU tests check the
+  same bars on the kernels themselves, test_gpu_kernels.py);
+* a rank-1 input exceeds the bar in both forms: rounding noise in the null
+  space is amplified by the quintic (~a^5), which any 11-bit operand type
+  (TF32 included) shares;
+* the emulation's operand scales are the library's own
+  (muon_ns_operand_scale through the C ABI, host-only).
+"""
+
+import itertools
+
+import pytest
+
+from oracle import muon_oracle as O
+from oracle import ns_emulation as E
+
+BAR = 1e-2
+
+
+def _errors(x):
+    ref = O.zeropower_via_newtonschulz5(x, 5)
+    return O.rel_frobenius(E.emulate_standard(x), ref), O.rel_frobenius(E.emulate_gram(x), ref)
+
+
+@pytest.mark.parametrize("kind", ["lowrank_noise", "powerlaw", "expdecay"])
+@pytest.mark.parametrize("shape", [(512, 2048), (2048, 512)])
+def test_structured_spectra_within_bar(kind, shape):
+    std, gram = _errors(E.structured_input(shape, kind, 21))
+    assert std < BAR and gram < BAR, (std, gram)
+    assert gram < 2 * std + 1e-3, (std, gram)
+
+
+@pytest.mark.parametrize("kind", ["gauss", "heavytail"])
+@pytest.mark.parametrize("shape", [(128, 512), (512, 128), (256, 256)])
+def test_full_rank_inputs_far_below_bar(kind, shape):
+    std, gram = _errors(E.structured_input(shape, kind, 3))
+    assert std < 3e-3 and gram < 3e-3, (std, gram)
+
+
+def test_rank_one_input_exceeds_bar_in_both_forms():
+    std, gram = _errors(E.structured_input((256, 640), "rank1", 3))
+    assert std > 0.1 and gram > 0.1, (std, gram)
+
+
+def test_emulation_uses_the_library_operand_scales():
+    from opendm_b200 import _native as N
+
+    lib = N.lib()
+    sizes = [1, 16, 33, 70, 256, 1152, 2048, 2560, 4304, 8192, 11008, 32768]
+    for r, c in itertools.product(sizes, repeat=2):
+        m, n = min(r, c), max(r, c)
+        for it in range(3):
+            assert lib.muon_ns_operand_scale(r, c, it, N.MUON_F16) == E.x_scale(m, n, it), (r, c, it)
