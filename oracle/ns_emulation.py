@@ -5,7 +5,8 @@ the CPU against the fp32 oracle of the reference algorithm
 (muon_oracle.zeropower_via_newtonschulz5, reference muon_adamw.py:101-128).
 
 Modelled: every stored operand rounded to fp16 (subnormals included) after a
-power-of-two scale; products accumulated exactly and rounded once to fp32
+power-of-two scale, or to tf32 (ties away from zero) or bf16 (ties to even)
+without one; products accumulated exactly and rounded once to fp32
 (the tensor cores accumulate in fp32 in a different order, so this is an
 approximation of the accumulation error, not of the operand rounding);
 epilogue arithmetic in fp32. Two forms:
@@ -38,6 +39,24 @@ def _f32(x: np.ndarray) -> np.ndarray:
     return np.asarray(x, np.float64).astype(np.float32).astype(np.float64)
 
 
+def _tf32(x: np.ndarray) -> np.ndarray:
+    """fp32 rounded to tf32's 10 stored mantissa bits, ties away from zero
+    (the kernels' cvt.rna)."""
+    u = np.ascontiguousarray(np.asarray(x, np.float64).astype(np.float32)).view(np.uint32).astype(np.uint64)
+    r = ((u + 0x1000) & 0xFFFFE000).astype(np.uint32)
+    return r.view(np.float32).astype(np.float64)
+
+
+def _bf16(x: np.ndarray) -> np.ndarray:
+    """fp32 rounded to bfloat16, ties to even."""
+    u = np.ascontiguousarray(np.asarray(x, np.float64).astype(np.float32)).view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    return r.view(np.float32).astype(np.float64)
+
+
+_ROUND = {"fp16": _f16, "tf32": _tf32, "bf16": _bf16}
+
+
 def _pow2(x: float) -> float:
     """The power of two nearest to x in the log domain, halves rounded away
     from zero (C's lround, as the library rounds)."""
@@ -45,9 +64,12 @@ def _pow2(x: float) -> float:
     return 2.0 ** int(math.floor(e + 0.5) if e >= 0 else -math.floor(-e + 0.5))
 
 
-def x_scale(m: int, n: int, iteration: int) -> float:
+def x_scale(m: int, n: int, iteration: int, op: str = "fp16") -> float:
     """Power-of-two scale of the stored X at `iteration` (m <= n): the
-    unit-norm input's entries are ~1/sqrt(m n), later iterates' ~1/sqrt(n)."""
+    unit-norm input's entries are ~1/sqrt(m n), later iterates' ~1/sqrt(n).
+    Only fp16 needs one (1.0 for tf32 and bf16, which have fp32's range)."""
+    if op != "fp16":
+        return 1.0
     return _pow2(math.sqrt(m * n)) if iteration == 0 else _pow2(math.sqrt(n))
 
 
@@ -61,35 +83,48 @@ def _prepare(g: np.ndarray, eps: float = 1e-7) -> tuple[np.ndarray, bool]:
     return x / max(norm, eps), tall
 
 
-def emulate_standard(g: np.ndarray, steps: int = 5) -> np.ndarray:
-    """The standard (iterate-on-X) form as the fp16 kernels compute it."""
+def emulate_standard(g: np.ndarray, steps: int = 5, op: str = "fp16", shifted: bool = True) -> np.ndarray:
+    """The standard (iterate-on-X) form with operands of type `op` ("fp16",
+    "tf32" or "bf16"). shifted=False evaluates the reference's own grouping,
+    X <- a X + (b A + c A A) X, with the same operand rounding, for
+    comparison."""
+    rnd = _ROUND[op]
     x, tall = _prepare(g)
     m, n = x.shape
     eye = np.eye(m)
-    s = x_scale(m, n, 0)
-    xs = _f16(x * s)
+    s = x_scale(m, n, 0, op)
+    xs = rnd(x * s)
     for it in range(steps):
-        a = _f32(xs @ xs.T) / (s * s)
-        ap = a - eye
-        bp = GAMMA * ap + BETA * eye
-        mm = _f16(_f32(_f16(ap) @ _f16(bp)) + ALPHA * eye)
         last = it == steps - 1
-        s_next = 1.0 if last else x_scale(m, n, it + 1)
-        acc = _f32(mm @ xs) * (s_next / s)
-        xs = _f32(acc) if last else _f16(acc)
+        s_next = 1.0 if last else x_scale(m, n, it + 1, op)
+        if shifted:
+            a = _f32(xs @ xs.T) / (s * s)
+            ap = a - eye
+            bp = GAMMA * ap + BETA * eye
+            mm = rnd(_f32(rnd(ap) @ rnd(bp)) + ALPHA * eye)
+            acc = _f32(mm @ xs) * (s_next / s)
+        else:
+            a = rnd(_f32(xs @ xs.T) / (s * s))
+            b = rnd(NS_B * a + NS_C * _f32(a @ a))
+            acc = _f32(NS_A * xs + _f32(b @ xs)) * (s_next / s)
+        xs = _f32(acc) if last else rnd(acc)
         s = s_next
     return (xs.T if tall else xs).astype(np.float32)
 
 
-def emulate_gram(g: np.ndarray, steps: int = 5, restart: int = 3) -> np.ndarray:
+def emulate_gram(g: np.ndarray, steps: int = 5, restart: int = 3, op: str = "fp16") -> np.ndarray:
     """The gram form (iterate on X X^T, restart every `restart` iterations)
-    as the fp16 kernels compute it."""
+    with operands of type `op` ("fp16" or "tf32", the types the library runs
+    it in)."""
+    if op not in ("fp16", "tf32"):
+        raise ValueError("the gram form runs with fp16 or tf32 operands")
+    rnd = _ROUND[op]
     x, tall = _prepare(g)
     m, n = x.shape
     eye = np.eye(m)
-    s = x_scale(m, n, 0)
-    xs = _f16(x * s)
-    sa, sq = _pow2(m / 4.0), _pow2(m / 64.0)
+    s = x_scale(m, n, 0, op)
+    xs = rnd(x * s)
+    sa, sq = (_pow2(m / 4.0), _pow2(m / 64.0)) if op == "fp16" else (1.0, 1.0)
     bounds = list(range(0, steps, restart)) + [steps]
     for s0, s1 in zip(bounds, bounds[1:]):
         p = pa = q = None
@@ -97,15 +132,15 @@ def emulate_gram(g: np.ndarray, steps: int = 5, restart: int = 3) -> np.ndarray:
             a = _f32(xs @ xs.T) / (s * s) if j == s0 else _f32(p @ pa) / (sa * sa)
             ap = a - eye
             bp = GAMMA * ap + BETA * eye
-            p_true = _f32(_f16(ap * sa) @ _f16(bp * sa)) / (sa * sa) + ALPHA * eye
-            p = _f16(p_true * sa)
-            q = _f16(p_true * sq) if j == s0 else _f16(_f32(p @ q) / sa)
+            p_true = _f32(rnd(ap * sa) @ rnd(bp * sa)) / (sa * sa) + ALPHA * eye
+            p = rnd(p_true * sa)
+            q = rnd(p_true * sq) if j == s0 else rnd(_f32(p @ q) / sa)
             if j < s1 - 1:
-                pa = _f16(_f32(p @ _f16(a * sa)) / sa)
+                pa = rnd(_f32(p @ rnd(a * sa)) / sa)
         last = s1 == steps
-        s_next = 1.0 if last else x_scale(m, n, s1)
+        s_next = 1.0 if last else x_scale(m, n, s1, op)
         acc = _f32(q @ xs) * (s_next / (sq * s))
-        xs = _f32(acc) if last else _f16(acc)
+        xs = _f32(acc) if last else rnd(acc)
         s = s_next
     return (xs.T if tall else xs).astype(np.float32)
 

@@ -11,7 +11,9 @@ fp32 oracle of the reference algorithm (reference muon_adamw.py:101-128).
   space is amplified by the quintic (~a^5), which any 11-bit operand type
   (TF32 included) shares;
 * the emulation's operand scales are the library's own
-  (muon_ns_operand_scale through the C ABI, host-only).
+  (muon_ns_operand_scale through the C ABI, host-only);
+* the operand choice: fp16 and tf32 equal, bf16 ~8x worse (at the bar), the
+  shifted grouping no worse than the reference's.
 """
 
 import itertools
@@ -58,3 +60,29 @@ def test_emulation_uses_the_library_operand_scales():
         m, n = min(r, c), max(r, c)
         for it in range(3):
             assert lib.muon_ns_operand_scale(r, c, it, N.MUON_F16) == E.x_scale(m, n, it), (r, c, it)
+
+
+@pytest.mark.parametrize("shape", [(256, 1024), (1024, 256), (512, 512)])
+def test_operand_types_and_the_shifted_form(shape):
+    """The operand choice of the design: fp16 (power-of-two scaled) and tf32
+    give the same error (both 11-bit significands); bf16 operands are ~8x
+    worse and sit at the bar; the shifted grouping is no worse than the
+    reference's a X + (b A + c A^2) X with the same operands, and the gram form
+    runs in tf32 as well as in fp16."""
+    x = E.structured_input(shape, "gauss", 5)
+    ref = O.zeropower_via_newtonschulz5(x, 5)
+    err = {op: O.rel_frobenius(E.emulate_standard(x, op=op), ref) for op in ("fp16", "tf32", "bf16")}
+    ref_form = O.rel_frobenius(E.emulate_standard(x, op="tf32", shifted=False), ref)
+    gram_tf32 = O.rel_frobenius(E.emulate_gram(x, op="tf32"), ref)
+    assert abs(err["fp16"] - err["tf32"]) < 0.2 * err["tf32"], err
+    assert err["bf16"] > 5 * err["fp16"] and err["bf16"] > 5e-3, err
+    assert err["tf32"] <= 1.05 * ref_form, (err, ref_form)
+    assert gram_tf32 < 3e-3, gram_tf32
+
+
+def test_tf32_rounding_ties_away_from_zero():
+    import numpy as np
+
+    x = np.array([1.0, 1.0 + 2 ** -11, 1.0 + 3 * 2 ** -11, -1.0 - 2 ** -11, 1.0 + 2 ** -12], np.float32)
+    want = [1.0, 1.0 + 2 ** -10, 1.0 + 2 ** -9, -1.0 - 2 ** -10, 1.0]
+    assert E._tf32(x).tolist() == want
