@@ -86,3 +86,16 @@ def test_tf32_rounding_ties_away_from_zero():
     x = np.array([1.0, 1.0 + 2 ** -11, 1.0 + 3 * 2 ** -11, -1.0 - 2 ** -11, 1.0 + 2 ** -12], np.float32)
     want = [1.0, 1.0 + 2 ** -10, 1.0 + 2 ** -9, -1.0 - 2 ** -10, 1.0]
     assert E._tf32(x).tolist() == want
+
+
+@pytest.mark.parametrize("kind", ["lowrank_noise", "powerlaw", "expdecay"])
+def test_gram_form_needs_its_restart(kind):
+    """Why X is re-formed every 3 iterations: iterating on X X^T alone for all
+    5 steps lets the m x m products' rounding grow along the small singular
+    directions (several times the bar on structured spectra); the restart
+    every 3 iterations keeps the gram form under the bar."""
+    x = E.structured_input((256, 1024), kind, 21)
+    ref = O.zeropower_via_newtonschulz5(x, 5)
+    restarted = O.rel_frobenius(E.emulate_gram(x, restart=3), ref)
+    pure = O.rel_frobenius(E.emulate_gram(x, restart=5), ref)
+    assert restarted < BAR < 5 * BAR < pure, (restarted, pure)
