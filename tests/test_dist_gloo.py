@@ -225,14 +225,14 @@ def test_owner_only_momentum_consolidates(tmp_path):
     _check(res, SMALL_MUON, SMALL_ADAM, 3)
 
 
-def test_adamw_sharding_two_and_three_ranks(tmp_path):
+def test_adamw_sharding_two_three_and_four_ranks(tmp_path):
     """adamw_sharding: each rank updates an equal contiguous range of the
     flat AdamW parameters (a vector split between ranks, whole small ones),
     the ranges are all-gathered, and consolidation brings the moments
     together; parameters and moments equal the single-process oracle."""
     adam = [(5000,), (10,), (700,), (3,)]
     muon = C1_MUON[:4] + SMALL_MUON  # three Muon waves: the ranges' all-gather goes between waves 0 and 1
-    for world in (2, 3):
+    for world in (2, 3, 4):
         res = _run("adam_sharded", muon, adam, 3, tmp_path, world=world)
         _check(res, muon, adam, 3)
         assert len(set(res[0]["waves"])) >= 2
