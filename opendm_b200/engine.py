@@ -10,8 +10,9 @@ whole matrices it must update and the AdamW-group tensors. The engine
   on X, or on the gram matrix) is the library's choice by executed FLOPs;
 * caches one plan state (workspaces, tensor maps, tile schedules) per matrix
   set, e.g. per all-gather wave, while the parameters stay at the same
-  addresses, and device copies of segment tables while their bytes repeat,
-  so a steady-state step uploads only the AdamW table;
+  addresses, and device copies of segment tables while their bytes repeat
+  (the AdamW table's per-step step size and bias correction are written on
+  the device), so a steady-state step copies nothing host to device;
 * launches (a) momentum + Frobenius scale (+ the fp16 operand conversion),
   (b) the grouped tcgen05 Newton-Schulz launches (3 per iteration, plus one
   per gram segment) whose last epilogue writes U in the parameter dtype,
