@@ -12,7 +12,8 @@ whole matrices it must update and the AdamW-group tensors. The engine
   set, e.g. per all-gather wave, while the parameters stay at the same
   addresses, and device copies of segment tables while their bytes repeat
   (the AdamW table's per-step step size and bias correction are written on
-  the device), so a steady-state step copies nothing host to device;
+  the device), so a steady-state step at a constant learning rate copies
+  nothing host to device (a new rate re-uploads the small update tables);
 * launches (a) momentum + Frobenius scale (+ the fp16 operand conversion),
   (b) the grouped tcgen05 Newton-Schulz launches (3 per iteration, plus one
   per gram segment) whose last epilogue writes U in the parameter dtype,
