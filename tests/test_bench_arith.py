@@ -1,0 +1,65 @@
+"""The arithmetic behind bench.py's roofline fields, on the CPU:
+
+* the configurations' Muon element counts and the reference's dense
+  Newton-Schulz FLOP count, steps * (4 m^2 n + 2 m^3) per matrix, equal the
+  figures the benchmark is specified with (config 2: 196 matrices, 1.674 G
+  elements, 79.53 TFLOP; config 4: 540, 3.969 G, 212.61; config 5: 224,
+  6.476 G, 684.45);
+* the executed-FLOP model (`roofline.executed_tflops`) gives 59.5 -> 39.7
+  TFLOP for config 2 and 159.7 -> 109.3 for config 4 with the library's
+  choice of form per shape;
+* that model is the one the library decides with: over a sweep of shapes and
+  step counts, muon_ns_choose_algo (C ABI, host-only) picks the gram form
+  exactly where the model's gram count is below 0.9x the standard count
+  (with at least one 3-iteration segment).
+"""
+
+import itertools
+import math
+
+import pytest
+
+import bench
+
+
+def _muon_shapes(cfg):
+    return [s for n, s in bench.config_params(cfg) if bench.is_muon(n, s)]
+
+
+@pytest.mark.parametrize("cfg,count,gel,tflop", [("c2", 196, 1.674, 79.53), ("c4", 540, 3.969, 212.61),
+                                                  ("c5", 224, 6.476, 684.45)])
+def test_config_sizes_and_dense_flops(cfg, count, gel, tflop):
+    shapes = _muon_shapes(cfg)
+    assert len(shapes) == count
+    assert round(sum(math.prod(s) for s in shapes) / 1e9, 3) == gel
+    assert round(sum(bench.ns_flops(s) for s in shapes) / 1e12, 2) == tflop
+    m, n = 2048, 8192
+    assert bench.ns_flops((n, m)) == bench.ns_flops((m, n)) == 5 * (4 * m * m * n + 2 * m ** 3)
+
+
+def _lib_algo(lib, N, s, steps=5):
+    return "gram" if lib.muon_ns_choose_algo(s[0], s[1], N.MUON_F16, steps) == N.MUON_NS_GRAM else "standard"
+
+
+@pytest.mark.parametrize("cfg,standard,chosen", [("c2", 59.5, 39.7), ("c4", 159.7, 109.3)])
+def test_executed_flops_with_the_library_choice(cfg, standard, chosen):
+    from opendm_b200 import _native as N
+
+    lib = N.lib()
+    shapes = _muon_shapes(cfg)
+    assert round(sum(bench.ns_executed_flops(s, 5, "standard") for s in shapes) / 1e12, 1) == standard
+    got = sum(bench.ns_executed_flops(s, 5, _lib_algo(lib, N, s)) for s in shapes)
+    assert round(got / 1e12, 1) == chosen
+
+
+def test_library_choice_follows_the_executed_flop_model():
+    from opendm_b200 import _native as N
+
+    lib = N.lib()
+    sizes = [16, 128, 200, 256, 300, 640, 1000, 1152, 1300, 2048, 3000, 4304, 8192, 11008]
+    for r, c in itertools.product(sizes, repeat=2):
+        for steps in (1, 2, 3, 5, 7):
+            gram = bench.ns_executed_flops((r, c), steps, "gram")
+            std = bench.ns_executed_flops((r, c), steps, "standard")
+            want = "gram" if steps >= bench.GRAM_SEGMENT and gram < 0.9 * std else "standard"
+            assert _lib_algo(lib, N, (r, c), steps) == want, (r, c, steps)
