@@ -54,7 +54,9 @@ The arithmetic runs in the sm_100a kernels of ``libopendm_muon.so`` through
   fused: one norm pass, and the coefficient is applied by the momentum and
   AdamW kernels as they read the gradients (set the trainer's own
   ``max_grad_norm`` to 0 when using it). ``clip_grad_norm_()`` does the same
-  on request; ``last_grad_norm`` holds the total norm of the last clip.
+  on request; ``last_grad_norm`` holds the total norm of the last clip. With
+  Muon matrices in FSDP shards ``step()`` refuses ``max_grad_norm``: the norm
+  must then be reduced across ranks, which FSDP's own ``clip_grad_norm_`` does.
 * ``allgather``: "nccl" (default) or "p2p": the flat parameter buckets live
   in peer-mapped memory and each rank pulls its peers' buckets with
   copy-engine memcpys ordered by cross-GPU flags (``opendm_b200.p2p``), so
@@ -369,9 +371,7 @@ class MuonAdamW(torch.optim.Optimizer):
         grads = self._grads_for_clip()
         if not grads:
             return torch.tensor(0.0)
-        plans = [p for g in self.param_groups if g.get("use_muon", False) for p in self._get_muon_shard_plans(g)]
-        fused = (float(norm_type) == 2.0 and grads[0].device.type == "cuda"
-                 and all(pl.kind in ("local", "replicated", "empty") for pl in plans))
+        fused = float(norm_type) == 2.0 and grads[0].device.type == "cuda" and not self._split_over_ranks()
         if not fused:
             params = [p for g in self.param_groups for p in g["params"]]
             return torch.nn.utils.clip_grad_norm_(params, max_norm, norm_type, error_if_nonfinite, foreach)
@@ -387,6 +387,11 @@ class MuonAdamW(torch.optim.Optimizer):
         self.last_grad_norm = total
         return total
 
+    def _split_over_ranks(self) -> bool:
+        """True when some Muon matrix is split into shards over ranks (FSDP)."""
+        return any(pl.kind not in ("local", "replicated", "empty")
+                   for g in self.param_groups if g.get("use_muon", False) for pl in self._get_muon_shard_plans(g))
+
     @torch.no_grad()
     def step(self, closure=None):
         loss = None
@@ -394,6 +399,10 @@ class MuonAdamW(torch.optim.Optimizer):
             with torch.enable_grad():
                 loss = closure()
         if self.max_grad_norm is not None and self._pending_clip is None:
+            if self._split_over_ranks():
+                raise RuntimeError("max_grad_norm needs parameters replicated on every rank; with FSDP shards "
+                                   "clip with FSDP's clip_grad_norm_ (the trainer's max_grad_norm), which "
+                                   "reduces the norm across ranks.")
             self.clip_grad_norm_(self.max_grad_norm)
         pending, self._pending_clip = self._pending_clip, None
         engine = self._engine if pending is not None else None

@@ -114,6 +114,7 @@ def _worker(rank, port, scenario, muon, adam, steps, outdir, world=WORLD):
         opt = MuonAdamW(model, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, _engine=engine,
                         state_sharding=(scenario in ("state_sharding", "waves", "adam_sharded", "flat_adam")),
                         adamw_sharding=(scenario in ("adam_sharded", "flat_adam")),
+                        max_grad_norm=1.0 if scenario == "flat_clip" else None,
                         allgather_waves=3 if scenario in ("waves", "adam_sharded") else None,
                         fsdp_owner_ns=(scenario != "flat_ref"))
         plist = list(model.parameters())
@@ -263,6 +264,14 @@ def test_adamw_sharding_refuses_fsdp_shards(tmp_path):
     res = _run("flat_adam", SMALL_MUON, SMALL_ADAM, 1, tmp_path)
     for r in res:
         assert "adamw_sharding needs replicated parameters" in r.get("error", ""), r
+
+
+def test_max_grad_norm_refuses_fsdp_shards(tmp_path):
+    """max_grad_norm with Muon matrices in FSDP-style flat shards: a local
+    norm would clip by the wrong total, so step() raises on every rank."""
+    res = _run("flat_clip", SMALL_MUON, SMALL_ADAM, 1, tmp_path)
+    for r in res:
+        assert "max_grad_norm needs parameters replicated" in r.get("error", ""), r
 
 
 def test_flat_shards_partial_and_owner_only(tmp_path):
