@@ -33,6 +33,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _native as N
+from . import trace
 
 _DTYPE_CODE = {torch.bfloat16: N.MUON_BF16, torch.float32: N.MUON_F32}
 PRECISIONS = {"tf32": N.MUON_TF32, "fp16": N.MUON_F16, "bf16": N.MUON_BF16}
@@ -198,6 +199,9 @@ class CudaMuonEngine:
         self.profile_events: list | None = None
 
     def _event_pair(self, name: str):
+        """Start a phase: an NVTX range always, and a pair of CUDA events when
+        ``profile_events`` collects them. Every call is closed by _event_end."""
+        trace.push(name)
         if self.profile_events is None:
             return None
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -205,6 +209,7 @@ class CudaMuonEngine:
         return name, start, end
 
     def _event_end(self, pair) -> None:
+        trace.pop()
         if pair is not None:
             pair[2].record()
             self.profile_events.append(pair)

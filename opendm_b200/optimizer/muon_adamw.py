@@ -79,6 +79,7 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
+from .. import trace
 from ..engine import AdamItem, CudaMuonEngine, MatrixItem, effective_lr
 from ..sharding import FlatAdamShards, FlatParamBuckets, assign_owners, assign_waves
 
@@ -409,7 +410,8 @@ class MuonAdamW(torch.optim.Optimizer):
         if engine is not None:
             engine.grad_scale = pending[1:2]
         try:
-            self._step_groups()
+            with trace.nvtx("step"):
+                self._step_groups()
         finally:
             if engine is not None:
                 engine.grad_scale = None
@@ -452,7 +454,9 @@ class MuonAdamW(torch.optim.Optimizer):
         pending, self._adam_pending = self._adam_pending, []
         for shards in pending:
             device = shards.buffers[0][0].device
-            self._adam_handles += shards.sync(async_op=device.type == "cuda", group=self._allgather_group(device))
+            with trace.nvtx("adamw_allgather"):
+                self._adam_handles += shards.sync(async_op=device.type == "cuda",
+                                                  group=self._allgather_group(device))
 
     def _host_step(self, param, state) -> float:
         hs = self._host_steps.get(param)
@@ -703,9 +707,10 @@ class MuonAdamW(torch.optim.Optimizer):
                 # copy engines: every SM stays with the Newton-Schulz
                 buckets.begin()
                 for w in range(n_waves):
-                    engine.muon_matrices(owned[w], momentum=momentum, nesterov=nesterov,
-                                         weight_decay_factor=wd_factor, ns_steps=ns_steps)
-                    buckets.wave_done(w)
+                    with trace.nvtx(f"wave{w}"):
+                        engine.muon_matrices(owned[w], momentum=momentum, nesterov=nesterov,
+                                             weight_decay_factor=wd_factor, ns_steps=ns_steps)
+                        buckets.wave_done(w)
                     if w == 0:
                         self._flush_adam_sync()
             else:
@@ -716,9 +721,10 @@ class MuonAdamW(torch.optim.Optimizer):
                     for w in range(n_waves):
                         if overlap:
                             engine.sm_limit = max(total_sms - self.comm_sms, 2) if w > 0 else 0
-                        engine.muon_matrices(owned[w], momentum=momentum, nesterov=nesterov,
-                                             weight_decay_factor=wd_factor, ns_steps=ns_steps)
-                        handles += buckets.sync(wave=w, async_op=device.type == "cuda", group=ag_group)
+                        with trace.nvtx(f"wave{w}"):
+                            engine.muon_matrices(owned[w], momentum=momentum, nesterov=nesterov,
+                                                 weight_decay_factor=wd_factor, ns_steps=ns_steps)
+                            handles += buckets.sync(wave=w, async_op=device.type == "cuda", group=ag_group)
                         if w == 0:
                             self._flush_adam_sync()
                 finally:

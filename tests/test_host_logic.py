@@ -470,3 +470,33 @@ def test_shard_plan_errors_single_process():
         MuonAdamW._gather_matrix(torch.zeros(8), plan)
     with pytest.raises(RuntimeError, match="Unknown Muon shard plan kind"):
         MuonAdamW._gather_matrix(torch.zeros(16), Plan("striped", 16, 16, (16,), (0,), 0))
+
+
+def test_nvtx_ranges_balanced(monkeypatch):
+    """The optimizer's NVTX ranges ("opendm/step", waves, all-gathers) close
+    on every path, exceptions included."""
+    from opendm_b200 import trace
+
+    depth, names = [0], []
+
+    def push(name):
+        depth[0] += 1
+        names.append(name)
+
+    def pop():
+        depth[0] -= 1
+
+    monkeypatch.setattr(trace, "ENABLED", True)
+    monkeypatch.setattr(torch.cuda.nvtx, "range_push", push)
+    monkeypatch.setattr(torch.cuda.nvtx, "range_pop", pop)
+    m = Tiny()
+    mark_muon_parameters(m)
+    opt = MuonAdamW(m, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0, _engine=OracleEngine())
+    for p in m.parameters():
+        p.grad = torch.zeros_like(p)
+    opt.step()
+    assert depth[0] == 0 and "opendm/step" in names
+    with pytest.raises(ZeroDivisionError):
+        with trace.nvtx("boom"):
+            1 / 0
+    assert depth[0] == 0
