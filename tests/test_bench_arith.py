@@ -11,7 +11,8 @@
 * that model is the one the library decides with: over a sweep of shapes and
   step counts, muon_ns_choose_algo (C ABI, host-only) picks the gram form
   exactly where the model's gram count is below 0.9x the standard count
-  (with at least one 3-iteration segment).
+  (with at least one 3-iteration segment);
+* the clock record (nvidia-smi parsing) that decides whether a run counts.
 """
 
 import itertools
@@ -63,3 +64,31 @@ def test_library_choice_follows_the_executed_flop_model():
             std = bench.ns_executed_flops((r, c), steps, "standard")
             want = "gram" if steps >= bench.GRAM_SEGMENT and gram < 0.9 * std else "standard"
             assert _lib_algo(lib, N, (r, c), steps) == want, (r, c, steps)
+
+
+def test_clock_sampler_parses_nvidia_smi_lines():
+    """bench.ClockSampler on canned `nvidia-smi --format=csv,noheader,nounits`
+    output: only the sampled GPUs count, the median SM clock and the max clock
+    are taken, a reason counts when any sample shows it "Active" ("Not Active"
+    does not), and malformed lines are skipped."""
+
+    class FakeProc:
+        def terminate(self):
+            pass
+
+        def communicate(self, timeout=None):
+            return ("0, 1900, 1965, 900.1, 0x4, Not Active, Not Active, Not Active, Active\n"
+                    "0, 1800, 1965, 950.0, 0x4, Not Active, Not Active, Not Active, Active\n"
+                    "1, 1000, 1965, 400.0, 0x0, Active, Not Active, Not Active, Not Active\n"
+                    "0, [N/A], 1965, 1.0, 0x0, Not Active, Not Active, Not Active, Not Active\n"
+                    "garbage\n"
+                    "0, 1700, 1965, 990.0, 0x0, Not Active, Not Active, Not Active, Not Active\n", "")
+
+    s = bench.ClockSampler([0])
+    s.proc = FakeProc()
+    got = s.stop()
+    assert got == {"sm_mhz": 1800.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"], "samples": 3}
+    s2 = bench.ClockSampler([0, 1])
+    s2.proc = FakeProc()
+    assert s2.stop()["reasons"] == ["hw_slowdown", "sw_power_cap"]
+    assert bench.ClockSampler([0]).stop() is None  # never started
