@@ -500,3 +500,22 @@ def test_nvtx_ranges_balanced(monkeypatch):
         with trace.nvtx("boom"):
             1 / 0
     assert depth[0] == 0
+
+
+def test_default_wave_counts():
+    """allgather_waves=None: 4 waves at >= 8 ranks with >= 16 dense TFLOP of
+    Newton-Schulz per rank (config 4), else 3 with >= 6 matrices per rank
+    (config 2 at 2-8 ranks), 1 with fewer matrices or off CUDA."""
+    import bench
+
+    m = Tiny()
+    mark_muon_parameters(m)
+    opt = MuonAdamW(m, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0, _engine=OracleEngine())
+    cuda = torch.device("cuda")
+    shapes = {c: [s for n, s in bench.config_params(c) if bench.is_muon(n, s)] for c in ("c2", "c4")}
+    assert opt._n_waves(shapes["c4"], 8, cuda, 5) == 4
+    assert opt._n_waves(shapes["c4"], 4, cuda, 5) == 3
+    for world in (2, 4, 8):
+        assert opt._n_waves(shapes["c2"], world, cuda, 5) == 3
+    assert opt._n_waves(shapes["c2"][:40], 8, cuda, 5) == 1  # 5 matrices per rank
+    assert opt._n_waves(shapes["c2"], 8, torch.device("cpu"), 5) == 1
