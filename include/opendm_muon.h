@@ -118,7 +118,9 @@ int muon_momentum(const muon_momentum_seg* segs_dev, int n_segs, int64_t total_c
  * exits. Limit: rows * cols <= MUON_NOALLOC_MAX_ELEMENTS; larger matrices are
  * rejected with MUON_ERR_ARG. The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress), so make that first call
- * before any stream capture. All calls on one device share its copy of the
+ * before any stream capture; the address is kept for the life of the
+ * process, so do not call this entry point on a device after a
+ * cudaDeviceReset of it. All calls on one device share its copy of the
  * array, which keeps the last call's contents: calls that overlap on that GPU
  * (for example on two streams) race with each other. Each call writes every
  * scratch value it reads, so nothing needs clearing between calls. Results

@@ -2,7 +2,7 @@
 iteration (gram, poly, apply) through the C ABI, against torch.matmul
 (cuBLAS) GEMMs of the same sizes on the same GPU.
 
-    python -m opendm_b200.nsbench [--reps 10]
+    python nsbench.py [--reps 10]
 
 For each shape class it prints the time of one ``muon_ns_plan_run`` with
 ``steps=1`` (standard form, fp16 operands), its executed FLOP rate (256x256
@@ -17,8 +17,8 @@ import ctypes
 
 import torch
 
-from . import _native as N
-from .engine import _ClassState
+from opendm_b200 import _native as N
+from opendm_b200.engine import _ClassState
 
 SHAPES = [(8192, 8192, 1), (2048, 8192, 8), (8192, 2048, 8), (2048, 2048, 32)]
 

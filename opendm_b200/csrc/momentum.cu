@@ -492,7 +492,11 @@ __global__ void momentum_single_scale_kernel(const float* __restrict__ partials,
 }
 
 // Device address of g_noalloc_partials, resolved once per device (with that
-// device current) on the first call made on it.
+// device current) on the first call made on it. The address belongs to the
+// device's context as it was at that call: after cudaDeviceReset (or anything
+// else that destroys the primary context) the library's module is loaded
+// again and the cached address is stale, so the entry point must not be used
+// in a process that resets a device it has already called it on.
 static std::mutex g_noalloc_mutex;
 static float* g_noalloc_ptr[kMaxNoAllocDevices] = {};
 
@@ -520,14 +524,20 @@ int launch_momentum_single_noalloc(const void* grad, float* exp_avg, void* direc
     return set_error(MUON_ERR_ARG, "grad_dtype must be MUON_BF16 or MUON_F32");
   if (dir_dtype != MUON_BF16 && dir_dtype != MUON_TF32 && dir_dtype != MUON_F32)
     return set_error(MUON_ERR_ARG, "dir_dtype must be MUON_BF16, MUON_TF32 or MUON_F32");
-  const int64_t chunks = momentum_chunks(rows, cols);
-  if (chunks > kNoAllocMaxChunks) {
-    char msg[160];
+  // The limit is checked on the factors, before any product is formed, so a
+  // shape whose rows * cols (or rows * ld) would overflow int64 is rejected too.
+  constexpr int64_t kMaxElements = kNoAllocMaxChunks * MOM_CHUNK;
+  static_assert(kMaxElements == MUON_NOALLOC_MAX_ELEMENTS, "limit and header disagree");
+  if (rows > 0 && (cols > kMaxElements / rows || ld > kMaxElements / rows)) {
+    char msg[200];
     snprintf(msg, sizeof(msg),
-             "matrix of %lld elements exceeds the allocation-free limit of %lld elements; use muon_momentum",
-             static_cast<long long>(rows * cols), static_cast<long long>(kNoAllocMaxChunks * MOM_CHUNK));
+             "matrix of %lld x %lld (leading dimension %lld) exceeds the allocation-free limit of %lld elements; "
+             "use muon_momentum",
+             static_cast<long long>(rows), static_cast<long long>(cols), static_cast<long long>(ld),
+             static_cast<long long>(kMaxElements));
     return set_error(MUON_ERR_ARG, msg);
   }
+  const int64_t chunks = momentum_chunks(rows, cols);
   float* partials = nullptr;
   const int rc = noalloc_scratch(&partials);
   if (rc != MUON_OK) return rc;

@@ -436,8 +436,33 @@ class CudaMuonEngine:
             self.kernel_launches += st.ns_launches
             self._record_error_check()
             self._apply_updates(st, items, weight_decay_factor)
+            self._last_state = (st, [it.param.data_ptr() for it in items])
         else:
+            self._last_state = None
             self._zero_step_update(st, items, weight_decay_factor)
+
+    def stored_updates(self) -> dict[int, torch.Tensor]:
+        """U of every matrix of the last ``muon_matrices`` call (ns_steps >=
+        1), keyed by the parameter's data_ptr(): [rows, cols] views, in the
+        parameter dtype, of the buffers the update kernel read. They stay
+        valid until the next step with the same matrix set overwrites them;
+        for checks of the update before it is added to the parameters."""
+        last = getattr(self, "_last_state", None)
+        if last is None:
+            return {}
+        st, ptrs = last
+        out: dict[int, torch.Tensor] = {}
+        for ptr, (ci, slot) in zip(ptrs, st.order):
+            cs = st.classes[ci]
+            dt = cs.param_dtype
+            if cs.u_buf is not None:
+                out[ptr] = cs.u_buf[slot, :, :cs.cols]
+                continue
+            es = torch.empty((), dtype=dt).element_size()
+            off = cs.u_base + slot * cs.u_stride - cs.workspace.data_ptr()
+            out[ptr] = torch.empty(0, dtype=dt, device=self.device).set_(
+                cs.workspace.untyped_storage(), off // es, (cs.rows, cs.cols), (int(cs.cls.ld_u), 1))
+        return out
 
     def _apply_updates(self, st: _PlanState, items: list[MatrixItem], wd_factor: float) -> None:
         """Weight decay + p -= eff * U for every matrix (muon_apply_update)."""

@@ -105,6 +105,29 @@ def test_argument_validation_reports_errors(lib):
         N.check(N.MUON_ERR_ARG, "probe")
 
 
+def test_noalloc_size_limit_rejected_on_host(lib):
+    """muon_momentum_single_noalloc refuses shapes beyond its fixed scratch
+    before touching the device: the pointers here are never dereferenced
+    (there is no GPU), and a regression of the check would surface as a CUDA
+    error status, not as a launch."""
+
+    def call(rows, cols, ld):
+        p = ctypes.c_void_p(4096)
+        return lib.muon_momentum_single_noalloc(None, p, p, rows, cols, ld, N.MUON_F32, N.MUON_F32,
+                                                ctypes.c_float(0.95), 1, ctypes.c_float(1e-7), p, None)
+
+    limit = 16384 * 16384
+    for rows, cols, ld in [(1, limit + 1, limit + 1),           # one element too many
+                           (16385, 16384, 16384),                # rows x cols just above
+                           (16384, 16384, 16392),                # padded rows push rows x ld above
+                           (1 << 40, 1 << 40, 1 << 40),          # rows x cols overflows int64
+                           ((1 << 62) + 1, 4, 4)]:
+        assert call(rows, cols, ld) == N.MUON_ERR_ARG, (rows, cols, ld)
+        assert "allocation-free limit" in N.last_error()
+    assert call(-1, 4, 4) == N.MUON_ERR_ARG  # negative shape
+    assert call(4, 8, 4) == N.MUON_ERR_ARG  # ld < cols
+
+
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(N, "_LIB", None)
     monkeypatch.setenv("OPENDM_MUON_LIB", str(tmp_path / "absent.so"))

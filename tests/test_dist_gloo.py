@@ -352,3 +352,93 @@ def test_unreconstructable_shard_sizes_raise(tmp_path):
     for r in range(2):
         res = torch.load(os.path.join(tmp_path, f"rank{r}.pt"), weights_only=False)
         assert "cannot be reconstructed from local shard sizes (6, 6)" in res.get("error", ""), res
+
+
+def _checkpoint_worker(rank, port, outdir, world=WORLD):
+    """Save after one step the way the HF Trainer does (rank 0 writes
+    optimizer.state_dict() with torch.save, after consolidate_state_dict() on
+    every rank), resume a fresh optimizer on every rank from that file
+    (torch.load, weights_only), and continue: bit-identical to the run that
+    never stopped."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.set_num_threads(2)
+    from datetime import timedelta
+
+    from opendm_b200.optimizer import MuonAdamW
+    from tests.oracle_engine import OracleEngine
+
+    result = {"rank": rank}
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
+        muon, adam, steps = SMALL_MUON, SMALL_ADAM, 3
+        params, grads = _data(muon, adam, steps)
+
+        def build(values):
+            model = torch.nn.Module()
+            for i, p in enumerate(values):
+                t = torch.nn.Parameter(torch.from_numpy(np.array(p, np.float32, copy=True)))
+                if i < len(muon):
+                    t._opendm_muon_shape = tuple(muon[i])
+                    t._opendm_muon_name = f"m{i}"
+                model.register_parameter(f"p{i}", t)
+            opt = MuonAdamW(model, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, _engine=OracleEngine(),
+                            state_sharding=True, adamw_sharding=True)
+            return model, opt
+
+        def step(model, opt, s):
+            for i, p in enumerate(model.parameters()):
+                p.grad = torch.from_numpy(grads[s][i].copy())
+            opt.step()
+
+        ma, oa = build(params)
+        step(ma, oa, 0)
+        oa.consolidate_state_dict()  # every rank, before rank 0 saves
+        path = os.path.join(outdir, "optimizer.pt")
+        if rank == 0:
+            torch.save(oa.state_dict(), path)
+        dist.barrier()
+        mb, ob = build([p.detach().numpy() for p in ma.parameters()])
+        ob.load_state_dict(torch.load(path, map_location="cpu", weights_only=True))
+        for s in range(1, steps):
+            step(ma, oa, s)
+            step(mb, ob, s)
+        oa.consolidate_state_dict()
+        ob.consolidate_state_dict()
+        result["same_params"] = all(torch.equal(a, b) for a, b in zip(ma.parameters(), mb.parameters()))
+        sa, sb = oa.state_dict()["state"], ob.state_dict()["state"]
+        result["same_state"] = sa.keys() == sb.keys() and all(
+            torch.equal(sa[k][f], sb[k][f]) for k in sa for f in ("exp_avg", "exp_avg_sq", "step"))
+        result["params"] = [p.detach().numpy().copy() for p in mb.parameters()]
+        result["exp_avg"] = [ob.state[p]["exp_avg"].numpy().copy() for p in list(mb.parameters())[:len(muon)]]
+        result["slices"] = None
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as exc:  # reported to the parent
+        result["error"] = f"{type(exc).__name__}: {exc}"
+        result["trace"] = traceback.format_exc()
+    torch.save(result, os.path.join(outdir, f"rank{rank}.pt"))
+
+
+def test_checkpoint_save_resume_continues_bit_identically(tmp_path):
+    """State sharding (owner-only momentum) with AdamW sharding, saved as the
+    HF Trainer saves an optimizer (torch.save of rank 0's state_dict() after
+    consolidate_state_dict()) and resumed on every rank (torch.load with
+    weights_only=True, load_state_dict): the two continuations agree bit for
+    bit and equal the single-process oracle (reference muon_adamw.py:240-317
+    for the state layout; trainer save/resume, opendm/exp/dm05_exp.py:1625)."""
+    ctx = mp.get_context("spawn")
+    port = _port()
+    procs = [ctx.Process(target=_checkpoint_worker, args=(r, port, str(tmp_path))) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("rank did not finish")
+    res = [torch.load(os.path.join(tmp_path, f"rank{r}.pt"), weights_only=False) for r in range(WORLD)]
+    for r in res:
+        assert "error" not in r, r.get("trace")
+        assert r["same_params"] and r["same_state"], r["rank"]
+    _check(res, SMALL_MUON, SMALL_ADAM, 3)

@@ -37,15 +37,32 @@ UPDATE_TOL = 5e-3
 BF16_PARAM_TOL = 2e-3
 
 
-def _check_params(got, want, before_got, before_want, wd_factor, dtype, what, max_beyond=None, step=0):
+def precast_error(before, u_got, u_want, wd_factor, eff):
+    """Relative error of the parameter value before its final bf16 rounding,
+    bf16(p * (1 - lr*wd)) - eff * bf16(U), with the GPU's U against the
+    oracle's, both from this side's parameters ``before`` (the update does not
+    depend on the parameters, so the check holds at every step)."""
+    base = O.cast_to(np.asarray(before, np.float32) * np.float32(wd_factor), "bfloat16").astype(np.float64)
+    got = base - eff * np.asarray(u_got, np.float64)
+    want = base - eff * O.cast_to(u_want, "bfloat16").astype(np.float64)
+    return O.rel_frobenius(got, want)
+
+
+def _check_params(got, want, before_got, before_want, wd_factor, dtype, what, max_beyond=None, step=0,
+                  precast=None):
     """Parity of updated parameters (see the module docstring for bf16).
     ``before_*`` are each side's parameters before this step; ``step`` is the
     0-based step index (bf16 rounding flips accumulate like a random walk, so
-    the bf16 bound grows as sqrt(step + 1))."""
+    the bf16 bound grows as sqrt(step + 1)). ``precast`` = (GPU U in bf16,
+    oracle U, eff) adds the check of the value before the final cast against
+    the 1e-3 bar itself."""
     err = O.rel_frobenius(got, want)
     if dtype != torch.bfloat16:
         assert err < PARAM_TOL, (what, err)
         return
+    if precast is not None:
+        pe = precast_error(before_got, precast[0], precast[1], wd_factor, precast[2])
+        assert pe < PARAM_TOL, (what, "before the final cast", pe)
     # Rounding flips are one ulp at the operand scale; an element whose update
     # dominates the parameter can differ by more (its own update error), so
     # only a small fraction of elements may exceed one ulp.
@@ -140,6 +157,8 @@ def _run_config(shapes_muon, shapes_adam, dtype, steps, seed=0, precision="fp16"
         before_want = [mp_[str(i)].copy() for i in range(n)]
         before_got = [params[i].detach().float().cpu().numpy() for i in range(n)]
         opt.step()
+        stored = opt._engine.stored_updates()
+        u_got = [stored[params[i].data_ptr()].float().cpu().numpy() for i in range(n)]
         updates = {}
         ref.step(mp_, {str(i): grads[s][i] for i in range(n)}, ap_,
                  {str(i): grads[s][i] for i in range(n, len(host))}, param_dtype=name, updates_out=updates,
@@ -152,9 +171,11 @@ def _run_config(shapes_muon, shapes_adam, dtype, steps, seed=0, precision="fp16"
         got = p.detach().float().cpu().numpy()
         worst = max(worst, O.rel_frobenius(got, want))
         if i < n:
+            eff = O.effective_lr(0.02, 1.0, 0.2, shapes_muon[i])
             # element-level flips compound over steps; checked for one-step runs only
             _check_params(got, want, before_got[i], before_want[i], 1.0 - 0.02 * 0.01, dtype, i,
-                          max_beyond=2e-2 if steps == 1 else None, step=steps - 1)
+                          max_beyond=2e-2 if steps == 1 else None, step=steps - 1,
+                          precast=(u_got[i], updates[str(i)], eff))
         else:
             assert O.rel_frobenius(got, want) < (BF16_PARAM_TOL if dtype == torch.bfloat16 else 1e-5), i
     for i in range(n):
@@ -259,6 +280,36 @@ def test_bounded_wait_reports_error_and_context_survives():
     st = lib.muon_read_error(ctypes.c_void_p(err.data_ptr()), ctypes.byref(code), stream)
     assert st == N.MUON_ERR_KERNEL and code.value == 0x1FF
     assert int(err.item()) == 0  # cleared by muon_read_error
+    x = torch.ones(1024, device=dev)
+    assert float((x * 2).sum()) == 2048.0
+
+
+def test_flag_wait_expires_with_status_and_context_survives():
+    """The copy-engine all-gather's cross-GPU flag wait (muon_flags_wait), on
+    one GPU: a flag in local device memory that nothing raises makes the wait
+    run out after 20 ms and record 0x106 in the error word; the stream goes
+    on and the context keeps working. A flag that was raised passes at once."""
+    from opendm_b200 import _native as N
+
+    dev = _dev()
+    lib = N.lib()
+    flags = torch.zeros(4, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    fl = N.FlagList()
+    fl.n = 2
+    fl.ptr[0], fl.ptr[1] = flags.data_ptr(), flags.data_ptr() + 8
+    N.check(lib.muon_flags_wait(ctypes.byref(fl), 1, 20000, ctypes.c_void_p(err.data_ptr()), stream), "flags_wait")
+    code = ctypes.c_int(0)
+    st = lib.muon_read_error(ctypes.c_void_p(err.data_ptr()), ctypes.byref(code), stream)
+    assert st == N.MUON_ERR_KERNEL and code.value == 0x106
+    assert int(err.item()) == 0
+    # raised flags: set on the stream, then the same wait completes with no error
+    N.check(lib.muon_flags_set(ctypes.byref(fl), 1, stream), "flags_set")
+    N.check(lib.muon_flags_wait(ctypes.byref(fl), 1, 20000, ctypes.c_void_p(err.data_ptr()), stream), "flags_wait")
+    st = lib.muon_read_error(ctypes.c_void_p(err.data_ptr()), ctypes.byref(code), stream)
+    assert st == N.MUON_OK and code.value == 0
+    assert flags.tolist() == [1, 0, 1, 0]
     x = torch.ones(1024, device=dev)
     assert float((x * 2).sum()) == 2048.0
 

@@ -77,7 +77,7 @@ def test_noalloc_matches_muon_momentum_two_calls(rows, cols, ld, gdt_name, ddt_n
         assert torch.equal(s_new, s_ref) and float(s_new) > 0
 
 
-def test_noalloc_zero_gradient_and_size_limit():
+def test_noalloc_zero_gradient():
     from opendm_b200 import _native as N
 
     dev = _dev()
@@ -92,10 +92,6 @@ def test_noalloc_zero_gradient_and_size_limit():
             "muon_momentum_single_noalloc")
     torch.cuda.synchronize()
     assert not d.any() and float(s) == 0.0
-    # beyond the fixed scratch: rejected before any launch, with a clear message
-    too_big = 16384 * 16384 + 1
-    st = lib.muon_momentum_single_noalloc(None, ctypes.c_void_p(m.data_ptr()), ctypes.c_void_p(d.data_ptr()),
-                                          1, too_big, too_big, N.MUON_F32, N.MUON_F32, ctypes.c_float(0.95), 1,
-                                          ctypes.c_float(1e-7), ctypes.c_void_p(s.data_ptr()), _stream())
-    assert st == N.MUON_ERR_ARG
-    assert "allocation-free limit" in N.last_error()
+    # Shapes beyond the fixed scratch are rejected on the host before any
+    # launch; that check runs without a GPU in tests/test_capi.py, so no
+    # out-of-bounds shape is ever passed here with real buffers.
