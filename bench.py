@@ -454,9 +454,11 @@ def run_ours(args):
         a1.record()
         sync_all()
         ag_ms = max_over_ranks(a0.elapsed_time(a1))
-    # grad (bf16) + exp_avg read/write + direction write; fp16: momentum pass
-    # (grad, exp_avg r/w) + the operand pass (grad, exp_avg, fp16 write)
-    mom_bytes = my_elems * {"tf32": 2 + 4 + 4 + 4, "bf16": 2 + 4 + 4 + 2, "fp16": 2 + 8 + 2 + 4 + 2}[args.precision]
+    # one pass per element: grad (bf16) read + exp_avg read and write + the
+    # Newton-Schulz operand write (tf32 4 B, bf16 and fp16 2 B); the fix-up of
+    # the fp16 path rewrites only matrices whose stored scale no longer fits
+    mom_bytes_per_el = {"tf32": 2 + 4 + 4 + 4, "bf16": 2 + 4 + 4 + 2, "fp16": 2 + 4 + 4 + 2}[args.precision]
+    mom_bytes = my_elems * mom_bytes_per_el
     mom_gbs = mom_bytes / (mom_ms * 1e-3) / 1e9 if mom_ms > 0 else 0.0
     adam_elems = sum(math.prod(s) for n, s in spec if not is_muon(n, s))
     adam_shards = opt._adam_shards.get(id(opt.param_groups[0]))
@@ -574,6 +576,8 @@ def run_ours(args):
                          "traffic_unit": "bytes per ns_gemm launch (ncu, c2s capture scaled by element count)",
                          "ns_ms": round(ns_ms, 3)},
             "elementwise": {"momentum_ms": round(mom_ms, 3), "momentum_gbs": round(mom_gbs, 1),
+                            "momentum_bytes_per_element": mom_bytes_per_el,
+                            "momentum_frac_of_hbm": round(mom_gbs / peaks["hbm_gbs"], 4),
                             "update_ms": round(upd_ms, 3),
                             "update_gbs": round(my_elems * 6 / (upd_ms * 1e-3) / 1e9, 1) if upd_ms > 0 else 0.0,
                             "adamw_ms": round(adam_ms, 3), "adamw_gbs": round(adam_gbs, 1),

@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define MUON_ABI_VERSION 2
+#define MUON_ABI_VERSION 3
 
 enum muon_status {
   MUON_OK = 0,
@@ -178,6 +178,39 @@ int muon_direction_f16(const muon_direction_f16_seg* segs_dev, int n_segs, int64
                        float momentum, int nesterov, const float* scales_dev, const float* grad_scale_dev,
                        void* stream);
 
+/* fp16 operands in the momentum pass itself. Replaces muon_adamw.py:381-394
+ * (momentum + Nesterov) and the normalisation of :118-121, like muon_momentum,
+ * but also writes the fp16 Newton-Schulz input, so each element is read and
+ * written once (12 bytes per element for bf16 gradients, against 18 for
+ * muon_momentum followed by muon_direction_f16):
+ *   x0 = fp16(d * p),  p = pscale[scale_index], a power of two
+ * chosen from the previous step's norm of the same matrix, and
+ *   scales[scale_index] = (1 / max(||d||, eps)) * mul / p
+ * (mul = muon_ns_operand_scale(rows, cols, 0, MUON_F16)), the factor that
+ * turns the stored x0 into the normalised input times mul. A Newton-Schulz
+ * class with the MUON_NS_INPUT_SCALED flag applies it in its first
+ * iteration. A matrix whose p is 0 (first step) or out of the safe range for
+ * this step's norm is rewritten by a fix-up pass with a new p (redo[i] = 1);
+ * pscale is updated for the next step either way. A zero or non-finite norm
+ * gives scales = 0 (a zero update). pscale: [n] device floats kept by the
+ * caller between steps, zero before the first; scales and redo: [n] outputs;
+ * partials: [total_chunks] scratch (chunks from muon_momentum_chunks). */
+typedef struct muon_momentum_f16_seg {
+  const void* grad;    /* [rows*cols] of grad_dtype, or NULL */
+  float* exp_avg;      /* [rows*cols] fp32, updated in place */
+  void* dst;           /* [rows][ld] fp16 (a class's x0 slot) */
+  int64_t rows;
+  int64_t cols;
+  int64_t ld;
+  int64_t chunk_begin;
+  float mul;           /* muon_ns_operand_scale(rows, cols, 0, MUON_F16) */
+  int32_t scale_index;
+} muon_momentum_f16_seg;
+
+int muon_momentum_f16(const muon_momentum_f16_seg* segs_dev, int n_segs, int64_t total_chunks, int grad_dtype,
+                      float momentum, int nesterov, float eps, float* partials_dev, float* pscale_dev,
+                      float* scales_dev, int* redo_dev, const float* grad_scale_dev, void* stream);
+
 /* Power-of-two scale of the stored operand X at Newton-Schulz iteration
  * `iteration` for op_dtype MUON_F16 (1.0 for the other types). */
 float muon_ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dtype);
@@ -229,6 +262,15 @@ float muon_ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dt
  * the reference adds to a bf16 parameter (muon_adamw.py:414 casts the update
  * to the parameter's dtype first). muon_apply_update then applies it.
  */
+/* muon_ns_class.flags: with MUON_F16 operands, x0 holds the direction times
+ * an arbitrary per-matrix factor and scales[i] turns it into the normalised
+ * input times muon_ns_operand_scale(rows, cols, 0, MUON_F16) (what
+ * muon_momentum_f16 writes). Without it, fp16 x0 holds that scaled,
+ * normalised input itself (muon_convert_f16, muon_direction_f16) and scales
+ * is not read. tf32 and bf16 classes always apply scales (x0 holds the raw
+ * direction). */
+#define MUON_NS_INPUT_SCALED 1
+
 typedef struct muon_ns_class {
   int32_t rows;
   int32_t cols;
@@ -245,7 +287,7 @@ typedef struct muon_ns_class {
   void* u_out;         /* [count][rows][ld_u] of u_dtype */
   int64_t ld_u;
   int32_t algo;        /* MUON_NS_STANDARD or MUON_NS_GRAM */
-  int32_t reserved;
+  int32_t flags;       /* MUON_NS_INPUT_SCALED or 0 */
   void* aa;            /* MUON_NS_GRAM: A, P A and the two Q buffers */
   void* pa;
   void* qa;

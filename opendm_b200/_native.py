@@ -27,8 +27,9 @@ MUON_TF32 = 2
 MUON_F16 = 3
 MUON_NS_STANDARD = 0
 MUON_NS_GRAM = 1
+MUON_NS_INPUT_SCALED = 1  # muon_ns_class.flags
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 
 class MomentumSeg(Structure):
@@ -74,7 +75,7 @@ class NsClass(Structure):
         ("u_out", c_void_p),
         ("ld_u", c_int64),
         ("algo", c_int32),
-        ("reserved", c_int32),
+        ("flags", c_int32),
         ("aa", c_void_p),
         ("pa", c_void_p),
         ("qa", c_void_p),
@@ -92,6 +93,11 @@ class FlagList(Structure):
 class DirectionF16Seg(Structure):
     _fields_ = [("grad", c_void_p), ("exp_avg", c_void_p), ("dst", c_void_p), ("rows", c_int64), ("cols", c_int64),
                 ("ld_dst", c_int64), ("chunk_begin", c_int64), ("mul", c_float), ("scale_index", c_int32)]
+
+
+class MomentumF16Seg(Structure):
+    _fields_ = [("grad", c_void_p), ("exp_avg", c_void_p), ("dst", c_void_p), ("rows", c_int64), ("cols", c_int64),
+                ("ld", c_int64), ("chunk_begin", c_int64), ("mul", c_float), ("scale_index", c_int32)]
 
 
 class NormSeg(Structure):
@@ -150,6 +156,8 @@ SIGNATURES = {
     "muon_flags_set": (c_int, [POINTER(FlagList), c_uint32, c_void_p]),
     "muon_norm_chunks": (c_int64, [c_int64]),
     "muon_direction_f16": (c_int, [c_void_p, c_int, c_int64, c_int, c_float, c_int, c_void_p, c_void_p, c_void_p]),
+    "muon_momentum_f16": (c_int, [c_void_p, c_int, c_int64, c_int, c_float, c_int, c_float, c_void_p, c_void_p,
+                                  c_void_p, c_void_p, c_void_p, c_void_p]),
     "muon_clip_grad_norm": (c_int, [c_void_p, c_int, c_int64, c_float, c_void_p, c_void_p, c_void_p]),
     "muon_momentum_scaled": (c_int, [c_void_p, c_int, c_int64, c_int, c_int, c_float, c_int, c_float, c_void_p,
                                      c_void_p, c_void_p, c_void_p]),

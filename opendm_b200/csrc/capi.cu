@@ -185,6 +185,14 @@ int muon_direction_f16(const muon_direction_f16_seg* segs_dev, int n_segs, int64
                                     grad_scale_dev, static_cast<cudaStream_t>(stream));
 }
 
+int muon_momentum_f16(const muon_momentum_f16_seg* segs_dev, int n_segs, int64_t total_chunks, int grad_dtype,
+                      float momentum, int nesterov, float eps, float* partials_dev, float* pscale_dev,
+                      float* scales_dev, int* redo_dev, const float* grad_scale_dev, void* stream) {
+  return muon::launch_momentum_f16(segs_dev, n_segs, total_chunks, grad_dtype, momentum, nesterov, eps, partials_dev,
+                                   pscale_dev, scales_dev, redo_dev, grad_scale_dev,
+                                   static_cast<cudaStream_t>(stream));
+}
+
 int muon_clip_grad_norm(const muon_norm_seg* segs_dev, int n_segs, int64_t total_chunks, float max_norm,
                         float* partials_dev, float* out_dev, void* stream) {
   return muon::launch_clip_grad_norm(segs_dev, n_segs, total_chunks, max_norm, partials_dev, out_dev,

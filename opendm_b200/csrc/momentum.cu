@@ -381,6 +381,238 @@ int launch_direction_f16(const muon_direction_f16_seg* segs_dev, int n_segs, int
   return check_cuda(cudaGetLastError(), "direction_f16 launch");
 }
 
+// ===========================================================================
+// fp16 Newton-Schulz input in the momentum pass itself (muon_momentum_f16).
+//
+// The normalisation 1/||d|| is only known once every chunk of a matrix has
+// been read, so the fp16 operand is written scaled by a power of two p that
+// the previous step's norm of the same matrix chose (entries of typical
+// magnitude 1/16: far from fp16's overflow and subnormal ranges while the norm
+// moves smoothly from step to step). The exact factor r = (1/||d||) * S0 / p,
+// which turns the stored x0 = d * p into the normalised input times the
+// operand scale S0, goes to the Newton-Schulz launches as the per-matrix input
+// scale (muon_ns_class flag MUON_NS_INPUT_SCALED). One pass reads the
+// gradient and the momentum and writes the momentum and the operand: 12 bytes
+// per element for bf16 gradients.
+//
+// A matrix whose p is missing (first step) or no longer safe (the norm moved
+// by more than the headroom allows) is rewritten by a fix-up pass with the
+// new p; every other chunk of that pass returns at once.
+constexpr float kF16Headroom = 1.0f / 16.0f;   // stored entries ~1/16 instead of ~1
+constexpr float kF16MaxNormTimesP = 32768.0f;  // ||d|| * p below this: no entry can overflow fp16
+constexpr float kF16MinRatio = 1.0f / 256.0f;  // p at least this fraction of the ideal one
+
+__device__ __forceinline__ int find_f16_segment(const muon_momentum_f16_seg* segs, int n_segs, int64_t chunk) {
+  int lo = 0, hi = n_segs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (segs[mid].chunk_begin <= chunk)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  return lo;
+}
+
+// Power of two nearest to x > 0 (in the log domain), 0 for x <= 0 or not finite.
+__device__ __forceinline__ float pow2_near(float x) {
+  if (!(x > 0.f) || !isfinite(x)) return 0.f;
+  int e = 0;
+  const float m = frexpf(x, &e);  // x = m * 2^e, m in [0.5, 1)
+  return ldexpf(1.0f, m >= 0.70710678f ? e : e - 1);
+}
+
+template <int kGradDt>
+__global__ void __launch_bounds__(MOM_THREADS) momentum_f16_kernel(const muon_momentum_f16_seg* __restrict__ segs,
+                                                                   int n_segs, float mu, int nesterov,
+                                                                   float* __restrict__ partials,
+                                                                   const float* __restrict__ pscale,
+                                                                   const float* __restrict__ grad_scale) {
+  __shared__ float red[MOM_THREADS / 32];
+  const int64_t chunk = blockIdx.x;
+  const muon_momentum_f16_seg sg = segs[find_f16_segment(segs, n_segs, chunk)];
+  const int64_t numel = sg.rows * sg.cols;
+  const int64_t e0 = (chunk - sg.chunk_begin) * MOM_CHUNK;
+  const int64_t e1 = min(e0 + MOM_CHUNK, numel);
+  const bool nest = nesterov != 0;
+  const float p = pscale[sg.scale_index];
+  const bool write = p > 0.f;  // else the fix-up pass writes this matrix
+  const bool clip = grad_scale != nullptr && sg.grad != nullptr;
+  const float coef = clip ? *grad_scale : 1.f;
+  __half* dst = reinterpret_cast<__half*>(sg.dst);
+  const bool vec_ok = sg.ld == sg.cols && (numel % 8) == 0 &&
+                      ((reinterpret_cast<uintptr_t>(sg.grad) | reinterpret_cast<uintptr_t>(sg.exp_avg) |
+                        reinterpret_cast<uintptr_t>(sg.dst)) & 15u) == 0;
+  float acc = 0.f;
+  if (vec_ok) {
+#pragma unroll 2
+    for (int it = 0; it < MOM_ITERS; ++it) {
+      const int64_t e = e0 + (int64_t(it) * MOM_THREADS + threadIdx.x) * MOM_VEC;
+      if (e >= e1) break;
+      float g[8];
+      load_grad8<kGradDt, MUON_F16>(sg.grad, e, g);
+      if (clip) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) g[i] = clip_grad<kGradDt>(g[i], coef);
+      }
+      float4* mp = reinterpret_cast<float4*>(sg.exp_avg + e);
+      const float4 m0 = mp[0], m1 = mp[1];
+      const float mo[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+      float mn[8], x[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const MomOut o = mom_op(g[i], mo[i], mu, nest);
+        mn[i] = o.m;
+        x[i] = o.d * p;  // exact: p is a power of two
+        acc = fmaf(o.d, o.d, acc);
+      }
+      mp[0] = make_float4(mn[0], mn[1], mn[2], mn[3]);
+      mp[1] = make_float4(mn[4], mn[5], mn[6], mn[7]);
+      if (write) {
+        uint4 raw;
+        __half2* h = reinterpret_cast<__half2*>(&raw);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+        *reinterpret_cast<uint4*>(dst + e) = raw;
+      }
+    }
+  } else {
+    for (int64_t e = e0 + threadIdx.x; e < e1; e += MOM_THREADS) {
+      float g = 0.f;
+      if (sg.grad) {
+        if constexpr (kGradDt == MUON_BF16)
+          g = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sg.grad)[e]);
+        else
+          g = reinterpret_cast<const float*>(sg.grad)[e];
+        if (clip) g = clip_grad<kGradDt>(g, coef);
+      }
+      const MomOut o = mom_op(g, sg.exp_avg[e], mu, nest);
+      sg.exp_avg[e] = o.m;
+      acc = fmaf(o.d, o.d, acc);
+      if (write) {
+        const int64_t r = e / sg.cols, c = e - r * sg.cols;
+        dst[r * sg.ld + c] = __float2half_rn(o.d * p);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < MOM_THREADS / 32 ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if (threadIdx.x == 0) partials[chunk] = v;
+  }
+}
+
+// One warp per segment: the fixed-order norm reduction of momentum_scale_kernel,
+// then the Newton-Schulz input factor r, the fix-up decision and the next p.
+__global__ void momentum_f16_scale_kernel(const muon_momentum_f16_seg* __restrict__ segs, int n_segs,
+                                          int64_t total_chunks, const float* __restrict__ partials, float eps,
+                                          float* __restrict__ pscale, float* __restrict__ scales,
+                                          int* __restrict__ redo) {
+  const int s = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (s >= n_segs) return;
+  const int64_t b = segs[s].chunk_begin;
+  const int64_t e = (s + 1 < n_segs) ? segs[s + 1].chunk_begin : total_chunks;
+  float acc = 0.f;
+  for (int64_t c = b + lane; c < e; c += 32) acc += partials[c];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    const int idx = segs[s].scale_index;
+    const float norm = sqrtf(acc);
+    const float sc = (isfinite(norm) && norm > 0.f) ? 1.0f / fmaxf(norm, eps) : 0.f;
+    const float s0 = segs[s].mul;  // operand scale S0 of the first iteration
+    const float p_old = pscale[idx];
+    if (sc == 0.f) {  // zero or non-finite: the Newton-Schulz result is zero
+      scales[idx] = 0.f;
+      redo[idx] = 0;
+      return;
+    }
+    const float p_ideal = pow2_near(s0 * sc * kF16Headroom);
+    const bool keep = p_old > 0.f && norm * p_old < kF16MaxNormTimesP && p_old >= p_ideal * kF16MinRatio;
+    const float p_used = keep ? p_old : p_ideal;
+    scales[idx] = sc * s0 / p_used;
+    redo[idx] = keep ? 0 : 1;
+    if (p_ideal > 0.f) pscale[idx] = p_ideal;  // the next step's p (and the fix-up's)
+  }
+}
+
+// Fix-up: the operand of the matrices flagged by momentum_f16_scale_kernel,
+// rebuilt from the gradient and the advanced momentum with the same
+// operations and written as fp16(d * p) with the new p.
+template <int kGradDt>
+__global__ void __launch_bounds__(MOM_THREADS) momentum_f16_fixup_kernel(const muon_momentum_f16_seg* __restrict__ segs,
+                                                                         int n_segs, float mu, int nesterov,
+                                                                         const float* __restrict__ pscale,
+                                                                         const int* __restrict__ redo,
+                                                                         const float* __restrict__ grad_scale) {
+  const int64_t chunk = blockIdx.x;
+  const muon_momentum_f16_seg sg = segs[find_f16_segment(segs, n_segs, chunk)];
+  if (redo[sg.scale_index] == 0) return;
+  const int64_t numel = sg.rows * sg.cols;
+  const int64_t e0 = (chunk - sg.chunk_begin) * MOM_CHUNK;
+  const int64_t e1 = min(e0 + MOM_CHUNK, numel);
+  const float p = pscale[sg.scale_index];
+  const bool nest = nesterov != 0;
+  const bool clip = grad_scale != nullptr && sg.grad != nullptr;
+  const float coef = clip ? *grad_scale : 1.f;
+  __half* dst = reinterpret_cast<__half*>(sg.dst);
+  for (int64_t e = e0 + threadIdx.x; e < e1; e += MOM_THREADS) {
+    float g = 0.f;
+    if (sg.grad) {
+      if constexpr (kGradDt == MUON_BF16)
+        g = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sg.grad)[e]);
+      else
+        g = reinterpret_cast<const float*>(sg.grad)[e];
+      if (clip) g = clip_grad<kGradDt>(g, coef);
+    }
+    const float m = sg.exp_avg[e];
+    const float d = nest ? __fmaf_rn(mu, m, g) : m;
+    const int64_t r = e / sg.cols, c = e - r * sg.cols;
+    dst[r * sg.ld + c] = __float2half_rn(d * p);
+  }
+}
+
+int launch_momentum_f16(const muon_momentum_f16_seg* segs_dev, int n_segs, int64_t total_chunks, int grad_dtype,
+                        float momentum, int nesterov, float eps, float* partials_dev, float* pscale_dev,
+                        float* scales_dev, int* redo_dev, const float* grad_scale, cudaStream_t stream) {
+  if (n_segs <= 0) return MUON_OK;
+  if (!segs_dev || !partials_dev || !pscale_dev || !scales_dev || !redo_dev)
+    return set_error(MUON_ERR_ARG, "null momentum_f16 buffer");
+  if (grad_dtype != MUON_BF16 && grad_dtype != MUON_F32)
+    return set_error(MUON_ERR_ARG, "grad_dtype must be MUON_BF16 or MUON_F32");
+  if (total_chunks > 0x7fffffffLL) return set_error(MUON_ERR_ARG, "too many momentum chunks");
+  const dim3 grid(static_cast<unsigned>(total_chunks > 0 ? total_chunks : 1));
+  if (total_chunks > 0) {
+    if (grad_dtype == MUON_BF16)
+      momentum_f16_kernel<MUON_BF16><<<grid, MOM_THREADS, 0, stream>>>(segs_dev, n_segs, momentum, nesterov,
+                                                                      partials_dev, pscale_dev, grad_scale);
+    else
+      momentum_f16_kernel<MUON_F32><<<grid, MOM_THREADS, 0, stream>>>(segs_dev, n_segs, momentum, nesterov,
+                                                                     partials_dev, pscale_dev, grad_scale);
+    if (check_cuda(cudaGetLastError(), "momentum_f16 launch")) return MUON_ERR_CUDA;
+  }
+  const int warps_per_block = 8;
+  momentum_f16_scale_kernel<<<(n_segs + warps_per_block - 1) / warps_per_block, warps_per_block * 32, 0, stream>>>(
+      segs_dev, n_segs, total_chunks, partials_dev, eps, pscale_dev, scales_dev, redo_dev);
+  if (check_cuda(cudaGetLastError(), "momentum_f16 scale launch")) return MUON_ERR_CUDA;
+  if (total_chunks > 0) {
+    if (grad_dtype == MUON_BF16)
+      momentum_f16_fixup_kernel<MUON_BF16><<<grid, MOM_THREADS, 0, stream>>>(segs_dev, n_segs, momentum, nesterov,
+                                                                            pscale_dev, redo_dev, grad_scale);
+    else
+      momentum_f16_fixup_kernel<MUON_F32><<<grid, MOM_THREADS, 0, stream>>>(segs_dev, n_segs, momentum, nesterov,
+                                                                           pscale_dev, redo_dev, grad_scale);
+    if (check_cuda(cudaGetLastError(), "momentum_f16 fix-up launch")) return MUON_ERR_CUDA;
+  }
+  return MUON_OK;
+}
+
 int launch_convert(const muon_convert_seg* segs_dev, int n_segs, int64_t total_chunks, const float* scales_dev,
                    cudaStream_t stream) {
   if (n_segs <= 0 || total_chunks <= 0) return MUON_OK;

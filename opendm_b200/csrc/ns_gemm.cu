@@ -947,6 +947,7 @@ int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, in
     } else if (k.algo != MUON_NS_STANDARD) {
       return set_error(MUON_ERR_ARG, "algo must be MUON_NS_STANDARD or MUON_NS_GRAM");
     }
+    if ((k.flags & ~MUON_NS_INPUT_SCALED) != 0) return set_error(MUON_ERR_ARG, "unknown muon_ns_class flags");
   }
   int dev = 0, sms = 0;
   if (check_cuda(cudaGetDevice(&dev), "cudaGetDevice")) return MUON_ERR_CUDA;
@@ -970,6 +971,9 @@ int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, in
     const muon_ns_class& k = classes[c];
     ClassGeom G{&k, op_dtype, es, std::min(k.rows, k.cols), std::max(k.rows, k.cols), k.rows <= k.cols,
                 static_cast<long long>(k.rows) * k.ld_x, static_cast<long long>(std::min(k.rows, k.cols)) * k.ld_m};
+    // The first iteration applies the per-matrix input scale unless x0 already
+    // holds the normalised fp16 input (fp16 without MUON_NS_INPUT_SCALED).
+    const bool scaled_in = !f16 || (k.flags & MUON_NS_INPUT_SCALED) != 0;
     auto xscale = [&](int it) { return ns_operand_scale(k.rows, k.cols, it, op_dtype); };
     if (k.algo == MUON_NS_STANDARD) {
       for (int it = 0; it < steps; ++it) {
@@ -978,11 +982,11 @@ int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, in
         const bool last = it == steps - 1;
         // fp16: X is stored pre-normalised and scaled by S_it, so A = acc / S_it^2.
         const float S = xscale(it);
-        slots[slot_of[3 * it]].push_back(G.gram_x(xin, !f16 && it == 0, 1.0f / (S * S), nullptr, 1.0f));
+        slots[slot_of[3 * it]].push_back(G.gram_x(xin, scaled_in && it == 0, 1.0f / (S * S), nullptr, 1.0f));
         slots[slot_of[3 * it + 1]].push_back(G.sym(k.ap, k.bp, EPI_POLY, 1.0f, k.mm));
         // acc = M (S_it X): rescale to S_{it+1} X' for the next iteration, or to X' itself.
         const float Sn = last ? 1.0f : xscale(it + 1);
-        slots[slot_of[3 * it + 2]].push_back(G.apply(k.mm, xin, !f16 && it == 0, Sn / S, last ? nullptr : xout));
+        slots[slot_of[3 * it + 2]].push_back(G.apply(k.mm, xin, scaled_in && it == 0, Sn / S, last ? nullptr : xout));
       }
       continue;
     }
@@ -997,7 +1001,7 @@ int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, in
       for (int it = s0; it < s1; ++it) {
         // phase 0: A' and B' of A_it, and A_it * SA
         if (it == s0)
-          slots[slot_of[3 * it]].push_back(G.gram_x(xseg, !f16 && it == 0, 1.0f / (S * S), k.aa, SA));
+          slots[slot_of[3 * it]].push_back(G.gram_x(xseg, scaled_in && it == 0, 1.0f / (S * S), k.aa, SA));
         else  // A_it = P_{it-1} (P_{it-1} A_{it-1}), operands stored times SA
           slots[slot_of[3 * it]].push_back([&] {
             Pending p = G.sym(k.mm, k.pa, EPI_GRAM, 1.0f / (SA * SA), k.ap);
@@ -1030,7 +1034,7 @@ int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, in
       // segment end: X_{s1} = Q X_{s0} (or U)
       const bool last = s1 == steps;
       const float Sn = last ? 1.0f : xscale(s1);
-      slots[ex_slot[s1 - 1]].push_back(G.apply(qbuf(s1 - 1), xseg, !f16 && s0 == 0, Sn / (SQ * S),
+      slots[ex_slot[s1 - 1]].push_back(G.apply(qbuf(s1 - 1), xseg, scaled_in && s0 == 0, Sn / (SQ * S),
                                                last ? nullptr : xnext));
     }
   }

@@ -14,7 +14,8 @@ whole matrices it must update and the AdamW-group tensors. The engine
   (the AdamW table's per-step step size and bias correction are written on
   the device), so a steady-state step at a constant learning rate copies
   nothing host to device (a new rate re-uploads the small update tables);
-* launches (a) momentum + Frobenius scale (+ the fp16 operand conversion),
+* launches (a) momentum + Frobenius scale (in fp16 mode with the operand
+  written in the same pass, scaled by a power of two carried between steps),
   (b) the grouped tcgen05 Newton-Schulz launches (3 per iteration, plus one
   per gram segment) whose last epilogue writes U in the parameter dtype,
   (c) weight decay + the scaled update, and the fused AdamW kernel, all on
@@ -128,7 +129,9 @@ class _ClassState:
         self.op_dtype = op_dtype
         self.es = 4 if op_dtype == N.MUON_TF32 else 2
         self.x_stride = rows * int(self.cls.ld_x) * self.es  # bytes per matrix in x0
-        # fp16 stores X0 normalised and scaled by this power of two.
+        # fp16 operand scale S0 of the first iteration: the Newton-Schulz input is
+        # X0 * S0 (stored so by the orthogonalize paths; muon_momentum_f16 stores
+        # d * p and hands the plan the factor to X0 * S0).
         self.x0_scale = float(lib.muon_ns_operand_scale(rows, cols, 0, op_dtype))
 
     def last_x_read(self, steps: int) -> int:
@@ -156,6 +159,10 @@ class _PlanState:
         self.order: list[tuple[int, int]] = []  # item index -> (class index, slot)
         self.seg_order: list[int] = []
         self.scales = None
+        # fp16: the per-matrix power of two of the stored operand, kept between
+        # steps (0 until the first step), and the fix-up flags (muon_momentum_f16)
+        self.pscale = None
+        self.redo = None
         self.ns_launches = 0
         self.sm_limit = 0
 
@@ -298,10 +305,15 @@ class CudaMuonEngine:
             cs.cls.ld_u = ld_u
             st.classes.append(cs)
         st.scales = torch.zeros(max(len(items), 1), dtype=torch.float32, device=self.device)
+        if self.op_dtype == N.MUON_F16:
+            st.pscale = torch.zeros_like(st.scales)
+            st.redo = torch.zeros(st.scales.numel(), dtype=torch.int32, device=self.device)
         first = 0
         for cs in st.classes:
             cs.first_seg = first
             cs.cls.scales = c_void_p(st.scales.data_ptr() + 4 * first)
+            if self.op_dtype == N.MUON_F16:
+                cs.cls.flags = N.MUON_NS_INPUT_SCALED  # x0 = d * p, scales = the factor to the normalised input
             first += cs.count
         if ns_steps >= 1:
             st.plans = self._create_plans([cs.cls for cs in st.classes], ns_steps)
@@ -353,6 +365,26 @@ class CudaMuonEngine:
                 "muon_momentum_scaled")
         self.kernel_launches += 2 if total > 0 else 1
 
+    def _momentum_f16(self, st: _PlanState, segs: list, grad_dtype: int, momentum: float, nesterov: bool,
+                      eps: float = 1e-7) -> None:
+        """One muon_momentum_f16 call: momentum, norm, the fp16 operand and
+        each matrix's Newton-Schulz input factor (plus the fix-up of matrices
+        whose carried power of two does not fit this step)."""
+        total = 0
+        for sg in segs:
+            sg.chunk_begin = total
+            total += int(self.lib.muon_momentum_chunks(sg.rows, sg.cols))
+        table = self._tables.get(N.struct_bytes(segs))
+        partials = torch.empty(max(total, 1), dtype=torch.float32, device=self.device)
+        gs = self.grad_scale
+        N.check(self.lib.muon_momentum_f16(c_void_p(table.data_ptr()), len(segs), total, grad_dtype, c_float(momentum),
+                                           int(bool(nesterov)), c_float(eps), c_void_p(partials.data_ptr()),
+                                           c_void_p(st.pscale.data_ptr()), c_void_p(st.scales.data_ptr()),
+                                           c_void_p(st.redo.data_ptr()),
+                                           c_void_p(gs.data_ptr() if gs is not None else None), _stream_handle()),
+                "muon_momentum_f16")
+        self.kernel_launches += 3 if total > 0 else 1
+
     def muon_matrices(self, items: list[MatrixItem], *, momentum: float, nesterov: bool, weight_decay_factor: float,
                       ns_steps: int) -> None:
         """Full Muon update of whole matrices: momentum, Newton-Schulz and the
@@ -374,36 +406,33 @@ class CudaMuonEngine:
             it = items[i]
             ci, slot = st.order[i]
             cs = st.classes[ci]
-            seg = N.MomentumSeg()
             g = it.grad
             if g is not None and not g.is_contiguous():
                 g = g.contiguous()
                 keep.append(g)  # the copy must outlive the launches that read it
+            if f16:
+                # one pass: momentum, norm and the fp16 operand d * p (muon_momentum_f16)
+                seg = N.MomentumF16Seg()
+                seg.dst = cs.cls.x0 + slot * cs.x_stride
+                seg.mul, seg.scale_index = cs.x0_scale, cs.first_seg + slot
+            else:
+                seg = N.MomentumSeg()
+                seg.direction = cs.cls.x0 + slot * cs.x_stride
             seg.grad = g.data_ptr() if g is not None else None
             seg.exp_avg = it.exp_avg.data_ptr()
-            if f16:
-                # momentum and norm only; the fp16 operand is rebuilt below from
-                # the gradient and the advanced exp_avg (muon_direction_f16)
-                seg.direction = None
-                seg.rows, seg.cols, seg.ld = cs.rows, cs.cols, cs.cols
-                dseg = N.DirectionF16Seg()
-                dseg.grad, dseg.exp_avg = seg.grad, seg.exp_avg
-                dseg.dst = cs.cls.x0 + slot * cs.x_stride
-                dseg.rows, dseg.cols, dseg.ld_dst = cs.rows, cs.cols, int(cs.cls.ld_x)
-                dseg.mul, dseg.scale_index = cs.x0_scale, cs.first_seg + slot
-            else:
-                seg.direction = cs.cls.x0 + slot * cs.x_stride
-                seg.rows, seg.cols, seg.ld = cs.rows, cs.cols, int(cs.cls.ld_x)
-                dseg = None
+            seg.rows, seg.cols, seg.ld = cs.rows, cs.cols, int(cs.cls.ld_x)
             code = _dtype_code(g) if g is not None else next(iter(gdt))
-            by_dtype.setdefault(code, []).append((cs.first_seg + slot, seg, dseg))
+            by_dtype.setdefault(code, []).append((cs.first_seg + slot, seg))
         ev = self._event_pair("momentum")
         for code, lst in by_dtype.items():
-            # Each launch writes scales for a contiguous run; split into runs.
             lst.sort(key=lambda x: x[0])
+            if f16:
+                self._momentum_f16(st, [seg for _, seg in lst], code, momentum, nesterov)
+                continue
+            # Each launch writes scales for a contiguous run; split into runs.
             run: list = []
             start = None
-            for idx, seg, _ in lst:
+            for idx, seg in lst:
                 if run and idx != start + len(run):
                     self._momentum(run, code, momentum, nesterov, st.scales.data_ptr() + 4 * start)
                     run = []
@@ -412,21 +441,6 @@ class CudaMuonEngine:
                 run.append(seg)
             if run:
                 self._momentum(run, code, momentum, nesterov, st.scales.data_ptr() + 4 * start)
-        if f16:
-            for code, lst in by_dtype.items():
-                dsegs, total = [], 0
-                for _, _, dseg in lst:
-                    dseg.chunk_begin = total
-                    total += int(self.lib.muon_momentum_chunks(dseg.rows, dseg.cols))
-                    dsegs.append(dseg)
-                table = self._tables.get(N.struct_bytes(dsegs))
-                gs = self.grad_scale
-                N.check(self.lib.muon_direction_f16(c_void_p(table.data_ptr()), len(dsegs), total, code,
-                                                    c_float(momentum), int(bool(nesterov)),
-                                                    c_void_p(st.scales.data_ptr()),
-                                                    c_void_p(gs.data_ptr() if gs is not None else None),
-                                                    _stream_handle()), "muon_direction_f16")
-                self.kernel_launches += 1
         self._event_end(ev)
         if ns_steps >= 1:
             ev = self._event_pair("ns")
@@ -490,8 +504,8 @@ class CudaMuonEngine:
     def _normalized_input(self, st: _PlanState, cs: _ClassState, slot: int) -> torch.Tensor:
         """The unit-norm Newton-Schulz input of one matrix, fp32 (ns_steps == 0 result)."""
         x = cs.x0_view(slot).float()
-        if self.op_dtype == N.MUON_F16:
-            return x / cs.x0_scale
+        if self.op_dtype == N.MUON_F16:  # x0 = d * p; scales = (1 / ||d||) * x0_scale / p
+            return x * st.scales[cs.first_seg + slot] / cs.x0_scale
         return x * st.scales[cs.first_seg + slot]
 
     def _zero_step_update(self, st: _PlanState, items: list[MatrixItem], wd_factor: float) -> None:
