@@ -1,7 +1,7 @@
 """Benchmark: one full MuonAdamW optimizer step (Muon + AdamW groups).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c2s|c4|c5]
-                    [--precision fp16|tf32|bf16] [--impl ours|reference]
+                    [--precision fp16|tf32|bf16|parity] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
 
 Workloads (synthetic, seeded; shapes of the configurations the reference's
@@ -431,7 +431,9 @@ def run_ours(args):
         owner_balance = {"dense": dense, "executed": executed}
     # the algorithm each shape class ran (the engine's classes, as planned)
     algo_of = {(cs.rows, cs.cols): ("gram" if int(cs.cls.algo) == 1 else "standard") for cs in engine.classes}
-    my_exec = sum(ns_executed_flops(s, algo=algo_of.get(tuple(s), "standard")) for s in mine)
+    # split operands ("parity") run every product three times (hi*hi, hi*lo, lo*hi)
+    my_exec = sum(ns_executed_flops(s, algo=algo_of.get(tuple(s), "standard")) for s in mine) * (
+        3 if args.precision == "parity" else 1)
     my_elems = sum(math.prod(s) for s in mine)
     my_ns_ms = per_step("ns")
     ns_tflops = my_flops / (my_ns_ms * 1e-3) / 1e12 if my_ns_ms > 0 else 0.0
@@ -457,7 +459,8 @@ def run_ours(args):
     # one pass per element: grad (bf16) read + exp_avg read and write + the
     # Newton-Schulz operand write (tf32 4 B, bf16 and fp16 2 B); the fix-up of
     # the fp16 path rewrites only matrices whose stored scale no longer fits
-    mom_bytes_per_el = {"tf32": 2 + 4 + 4 + 4, "bf16": 2 + 4 + 4 + 2, "fp16": 2 + 4 + 4 + 2}[args.precision]
+    mom_bytes_per_el = {"tf32": 2 + 4 + 4 + 4, "bf16": 2 + 4 + 4 + 2, "fp16": 2 + 4 + 4 + 2,
+                        "parity": 2 + 4 + 4 + 4}[args.precision]
     mom_bytes = my_elems * mom_bytes_per_el
     mom_gbs = mom_bytes / (mom_ms * 1e-3) / 1e9 if mom_ms > 0 else 0.0
     adam_elems = sum(math.prod(s) for n, s in spec if not is_muon(n, s))
@@ -611,7 +614,7 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default="c2", choices=["c2", "c2s", "c4", "c5"])
-    ap.add_argument("--precision", default="fp16", choices=["fp16", "tf32", "bf16"])
+    ap.add_argument("--precision", default="fp16", choices=["fp16", "tf32", "bf16", "parity"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--allgather", default="nccl", choices=["nccl", "p2p"],

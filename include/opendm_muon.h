@@ -47,7 +47,9 @@ enum muon_dtype {
   MUON_BF16 = 0, /* bfloat16 storage */
   MUON_F32 = 1,  /* float32 storage */
   MUON_TF32 = 2, /* float32 storage holding values rounded to tf32 (NS operands) */
-  MUON_F16 = 3   /* float16 storage (NS operands, scaled by powers of two) */
+  MUON_F16 = 3,  /* float16 storage (NS operands, scaled by powers of two) */
+  MUON_F16X3 = 4 /* NS operands as float16 pairs hi + lo (hi = fp16(x), lo = fp16(x - hi)), each
+                    product as hi*hi + hi*lo + lo*hi: ~22-bit operands for 3x the MMA work */
 };
 
 enum muon_ns_algo {
@@ -203,6 +205,8 @@ typedef struct muon_momentum_f16_seg {
   int64_t cols;
   int64_t ld;
   int64_t chunk_begin;
+  int64_t lo_offset;   /* MUON_F16X3 classes: elements from dst to the lo half (its x0 batch slot
+                          2g + 1); lo = fp16(x - fp16(x)) is written there. 0: no lo half */
   float mul;           /* muon_ns_operand_scale(rows, cols, 0, MUON_F16) */
   int32_t scale_index;
 } muon_momentum_f16_seg;
@@ -262,7 +266,7 @@ float muon_ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dt
  * the reference adds to a bf16 parameter (muon_adamw.py:414 casts the update
  * to the parameter's dtype first). muon_apply_update then applies it.
  */
-/* muon_ns_class.flags: with MUON_F16 operands, x0 holds the direction times
+/* muon_ns_class.flags: with MUON_F16 (or MUON_F16X3) operands, x0 holds the direction times
  * an arbitrary per-matrix factor and scales[i] turns it into the normalised
  * input times muon_ns_operand_scale(rows, cols, 0, MUON_F16) (what
  * muon_momentum_f16 writes). Without it, fp16 x0 holds that scaled,

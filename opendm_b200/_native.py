@@ -25,6 +25,7 @@ MUON_BF16 = 0
 MUON_F32 = 1
 MUON_TF32 = 2
 MUON_F16 = 3
+MUON_F16X3 = 4  # Newton-Schulz operands as fp16 hi/lo pairs
 MUON_NS_STANDARD = 0
 MUON_NS_GRAM = 1
 MUON_NS_INPUT_SCALED = 1  # muon_ns_class.flags
@@ -97,7 +98,8 @@ class DirectionF16Seg(Structure):
 
 class MomentumF16Seg(Structure):
     _fields_ = [("grad", c_void_p), ("exp_avg", c_void_p), ("dst", c_void_p), ("rows", c_int64), ("cols", c_int64),
-                ("ld", c_int64), ("chunk_begin", c_int64), ("mul", c_float), ("scale_index", c_int32)]
+                ("ld", c_int64), ("chunk_begin", c_int64), ("lo_offset", c_int64), ("mul", c_float),
+                ("scale_index", c_int32)]
 
 
 class NormSeg(Structure):

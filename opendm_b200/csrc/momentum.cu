@@ -422,6 +422,28 @@ __device__ __forceinline__ float pow2_near(float x) {
   return ldexpf(1.0f, m >= 0.70710678f ? e : e - 1);
 }
 
+// fp16 operand stores; with lo_offset != 0 (split operands) also the low half
+// fp16(x - fp16(x)), lo_offset elements further on.
+__device__ __forceinline__ void store_f16x8(__half* dst, int64_t lo_offset, int64_t e, const float (&x)[8]) {
+  uint4 hi, lo;
+  __half2* h = reinterpret_cast<__half2*>(&hi);
+  __half2* l = reinterpret_cast<__half2*>(&lo);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    h[i] = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+    const float2 hf = __half22float2(h[i]);
+    l[i] = __floats2half2_rn(x[2 * i] - hf.x, x[2 * i + 1] - hf.y);
+  }
+  *reinterpret_cast<uint4*>(dst + e) = hi;
+  if (lo_offset != 0) *reinterpret_cast<uint4*>(dst + lo_offset + e) = lo;
+}
+
+__device__ __forceinline__ void store_f16(__half* dst, int64_t lo_offset, int64_t idx, float x) {
+  const __half h = __float2half_rn(x);
+  dst[idx] = h;
+  if (lo_offset != 0) dst[lo_offset + idx] = __float2half_rn(x - __half2float(h));
+}
+
 template <int kGradDt>
 __global__ void __launch_bounds__(MOM_THREADS) momentum_f16_kernel(const muon_momentum_f16_seg* __restrict__ segs,
                                                                    int n_segs, float mu, int nesterov,
@@ -440,7 +462,7 @@ __global__ void __launch_bounds__(MOM_THREADS) momentum_f16_kernel(const muon_mo
   const bool clip = grad_scale != nullptr && sg.grad != nullptr;
   const float coef = clip ? *grad_scale : 1.f;
   __half* dst = reinterpret_cast<__half*>(sg.dst);
-  const bool vec_ok = sg.ld == sg.cols && (numel % 8) == 0 &&
+  const bool vec_ok = sg.ld == sg.cols && (numel % 8) == 0 && (sg.lo_offset % 8) == 0 &&
                       ((reinterpret_cast<uintptr_t>(sg.grad) | reinterpret_cast<uintptr_t>(sg.exp_avg) |
                         reinterpret_cast<uintptr_t>(sg.dst)) & 15u) == 0;
   float acc = 0.f;
@@ -468,13 +490,7 @@ __global__ void __launch_bounds__(MOM_THREADS) momentum_f16_kernel(const muon_mo
       }
       mp[0] = make_float4(mn[0], mn[1], mn[2], mn[3]);
       mp[1] = make_float4(mn[4], mn[5], mn[6], mn[7]);
-      if (write) {
-        uint4 raw;
-        __half2* h = reinterpret_cast<__half2*>(&raw);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
-        *reinterpret_cast<uint4*>(dst + e) = raw;
-      }
+      if (write) store_f16x8(dst, sg.lo_offset, e, x);
     }
   } else {
     for (int64_t e = e0 + threadIdx.x; e < e1; e += MOM_THREADS) {
@@ -489,10 +505,7 @@ __global__ void __launch_bounds__(MOM_THREADS) momentum_f16_kernel(const muon_mo
       const MomOut o = mom_op(g, sg.exp_avg[e], mu, nest);
       sg.exp_avg[e] = o.m;
       acc = fmaf(o.d, o.d, acc);
-      if (write) {
-        const int64_t r = e / sg.cols, c = e - r * sg.cols;
-        dst[r * sg.ld + c] = __float2half_rn(o.d * p);
-      }
+      if (write) store_f16(dst, sg.lo_offset, (e / sg.cols) * sg.ld + e % sg.cols, o.d * p);
     }
   }
 #pragma unroll
@@ -562,6 +575,28 @@ __global__ void __launch_bounds__(MOM_THREADS) momentum_f16_fixup_kernel(const m
   const bool clip = grad_scale != nullptr && sg.grad != nullptr;
   const float coef = clip ? *grad_scale : 1.f;
   __half* dst = reinterpret_cast<__half*>(sg.dst);
+  const bool vec_ok = sg.ld == sg.cols && (numel % 8) == 0 && (sg.lo_offset % 8) == 0 &&
+                      ((reinterpret_cast<uintptr_t>(sg.grad) | reinterpret_cast<uintptr_t>(sg.exp_avg) |
+                        reinterpret_cast<uintptr_t>(sg.dst)) & 15u) == 0;
+  if (vec_ok) {
+    for (int it = 0; it < MOM_ITERS; ++it) {
+      const int64_t e = e0 + (int64_t(it) * MOM_THREADS + threadIdx.x) * MOM_VEC;
+      if (e >= e1) break;
+      float g[8];
+      load_grad8<kGradDt, MUON_F16>(sg.grad, e, g);
+      const float4* mp = reinterpret_cast<const float4*>(sg.exp_avg + e);
+      const float4 m0 = __ldg(mp), m1 = __ldg(mp + 1);
+      const float m[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+      float x[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float gi = clip ? clip_grad<kGradDt>(g[i], coef) : g[i];
+        x[i] = (nest ? __fmaf_rn(mu, m[i], gi) : m[i]) * p;
+      }
+      store_f16x8(dst, sg.lo_offset, e, x);
+    }
+    return;
+  }
   for (int64_t e = e0 + threadIdx.x; e < e1; e += MOM_THREADS) {
     float g = 0.f;
     if (sg.grad) {
@@ -573,8 +608,7 @@ __global__ void __launch_bounds__(MOM_THREADS) momentum_f16_fixup_kernel(const m
     }
     const float m = sg.exp_avg[e];
     const float d = nest ? __fmaf_rn(mu, m, g) : m;
-    const int64_t r = e / sg.cols, c = e - r * sg.cols;
-    dst[r * sg.ld + c] = __float2half_rn(d * p);
+    store_f16(dst, sg.lo_offset, (e / sg.cols) * sg.ld + e % sg.cols, d * p);
   }
 }
 

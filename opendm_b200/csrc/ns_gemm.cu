@@ -74,6 +74,7 @@ struct GemmProblem {
   int symmetric;   // compute upper-triangle tiles and mirror them
   int epi;
   int first;       // apply the per-matrix input scale
+  int split;       // operands stored as fp16 hi/lo pairs (batch slots 2g, 2g+1): K runs three times
   float mul;       // constant multiplier of the accumulator (power of two)
   float omul;      // poly: multiplier of the stored M / P (power of two)
   float omul3;     // gram: of the stored A; poly: of the stored Q (power of two)
@@ -279,6 +280,25 @@ __device__ __forceinline__ void store_chunk(StoreRing& ring, const CUtensorMap* 
   }
 }
 
+// Store one chunk of a Newton-Schulz operand output (32 fp32 values of this
+// lane's row), rounded to the operand type. With split operands the value
+// goes out as a pair: hi = round(x) at batch slot 2g and lo = round(x - hi)
+// at 2g + 1 (x - hi is exact in fp32), so hi + lo carries ~22 bits.
+template <int kOp, int kWords>
+__device__ __forceinline__ void store_operand(StoreRing& ring, const CUtensorMap* map, int lane, const float (&x)[32],
+                                              int kind, int col0, int row0, int g, bool mirror, bool split) {
+  uint32_t w[kWords];
+  pack_row<kWords>(x, kind, w);
+  store_chunk<kWords>(ring, map, lane, w, col0, row0, split ? 2 * g : g, mirror);
+  if (split) {
+    float lo[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) lo[i] = x[i] - round_op<kOp>(x[i]);
+    pack_row<kWords>(lo, kind, w);
+    store_chunk<kWords>(ring, map, lane, w, col0, row0, 2 * g + 1, mirror);
+  }
+}
+
 template <int kOp>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     ns_gemm_kernel(const __grid_constant__ GemmParams P) {
@@ -350,9 +370,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         const TileCoord tc = decode_tile(P, t);
         const GemmProblem& pr = P.prob[tc.p];
         const int kb_count = (pr.K + BKE - 1) / BKE;
+        const int kb_total = pr.split ? 3 * kb_count : kb_count;
         const int m0 = tc.ti * PAIR_M + static_cast<int>(rank) * BM;
         const int n0 = tc.tj * BN + static_cast<int>(rank) * BN_CTA;
-        for (int kb = 0; kb < kb_count; ++kb) {
+        for (int kbi = 0; kbi < kb_total; ++kbi) {
+          // Split operands: K segment 0 = hi * hi, 1 = hi * lo, 2 = lo * hi.
+          const int seg = pr.split ? kbi / kb_count : 0;
+          const int kb = kbi - seg * kb_count;
+          const int za = pr.split ? 2 * tc.g + (seg == 2 ? 1 : 0) : tc.g;
+          const int zb = pr.split ? 2 * tc.g + (seg == 1 ? 1 : 0) : tc.g;
           if (!mbar_wait(&empty[stage], phase ^ 1u, P.err, kDevTimeoutEmpty)) {
             ok = false;
             break;
@@ -363,18 +389,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           uint8_t* sb = stage_b + stage * B_STAGE_BYTES;
           const int k0 = kb * BKE;
           if (!pr.a_mn) {
-            tma_load_3d_pair(sa, &P.map_a[tc.p], bar, k0, m0, tc.g);
+            tma_load_3d_pair(sa, &P.map_a[tc.p], bar, k0, m0, za);
           } else {
 #pragma unroll
             for (int j = 0; j < BM / BKE; ++j)
-              tma_load_3d_pair(sa + j * BKE * 128, &P.map_a[tc.p], bar, m0 + j * BKE, k0, tc.g);
+              tma_load_3d_pair(sa + j * BKE * 128, &P.map_a[tc.p], bar, m0 + j * BKE, k0, za);
           }
           if (!pr.b_mn) {
-            tma_load_3d_pair(sb, &P.map_b[tc.p], bar, k0, n0, tc.g);
+            tma_load_3d_pair(sb, &P.map_b[tc.p], bar, k0, n0, zb);
           } else {
 #pragma unroll
             for (int j = 0; j < BN_CTA / BKE; ++j)
-              tma_load_3d_pair(sb + j * BKE * 128, &P.map_b[tc.p], bar, n0 + j * BKE, k0, tc.g);
+              tma_load_3d_pair(sb + j * BKE * 128, &P.map_b[tc.p], bar, n0 + j * BKE, k0, zb);
           }
           issued[stage] = 1;
           issued_phase[stage] = phase;
@@ -399,7 +425,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       for (int t = cluster_id; ok && t < P.total_tiles; t += n_clusters, ++local_t) {
         const TileCoord tc = decode_tile(P, t);
         const GemmProblem& pr = P.prob[tc.p];
-        const int kb_count = (pr.K + BKE - 1) / BKE;
+        const int kb_count = (pr.K + BKE - 1) / BKE * (pr.split ? 3 : 1);
         const int acc = local_t & 1;
         const uint32_t acc_phase = (local_t >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, P.err, kDevTimeoutTmemEmpty)) {
@@ -489,50 +515,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         if (sym && col0 + 32 <= row0) continue;
         const bool mirror = sym && col0 >= row0 + 32;
         float x[32];
+        const bool split = pr.split != 0;
         if (pr.epi == EPI_GRAM) {
-          uint32_t w[kOpWords];
           if (has3) {  // A itself, scaled for storage
             const float m3 = pr.omul3;
 #pragma unroll
             for (int i = 0; i < 32; ++i) x[i] = zero ? 0.f : (v[i] * f) * m3;
-            pack_row<kOpWords>(x, kOpKind, w);
-            store_chunk<kOpWords>(ring, map3, lane, w, col0, row0, tc.g, mirror);
+            store_operand<kOp, kOpWords>(ring, map3, lane, x, kOpKind, col0, row0, tc.g, mirror, split);
           }
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const float a = zero ? 0.f : v[i] * f;
             x[i] = (myrow == col0 + i) ? a - 1.f : a;  // A'
           }
-          pack_row<kOpWords>(x, kOpKind, w);
-          store_chunk<kOpWords>(ring, map1, lane, w, col0, row0, tc.g, mirror);
+          store_operand<kOp, kOpWords>(ring, map1, lane, x, kOpKind, col0, row0, tc.g, mirror, split);
 #pragma unroll
           for (int i = 0; i < 32; ++i) x[i] = fmaf(P.gamma, x[i], (myrow == col0 + i) ? P.beta : 0.f);  // B'
-          pack_row<kOpWords>(x, kOpKind, w);
-          store_chunk<kOpWords>(ring, map2, lane, w, col0, row0, tc.g, mirror);
+          store_operand<kOp, kOpWords>(ring, map2, lane, x, kOpKind, col0, row0, tc.g, mirror, split);
         } else if (pr.epi == EPI_POLY) {
           const float pm = pr.mul, om = pr.omul;
 #pragma unroll
           for (int i = 0; i < 32; ++i) x[i] = (myrow == col0 + i) ? fmaf(v[i], pm, P.alpha) : v[i] * pm;
-          uint32_t w[kOpWords];
           if (has3) {  // the same polynomial, stored a second time at another scale
             float y[32];
             const float m3 = pr.omul3;
 #pragma unroll
             for (int i = 0; i < 32; ++i) y[i] = x[i] * m3;
-            pack_row<kOpWords>(y, kOpKind, w);
-            store_chunk<kOpWords>(ring, map3, lane, w, col0, row0, tc.g, mirror);
+            store_operand<kOp, kOpWords>(ring, map3, lane, y, kOpKind, col0, row0, tc.g, mirror, split);
           }
 #pragma unroll
           for (int i = 0; i < 32; ++i) x[i] *= om;
-          pack_row<kOpWords>(x, kOpKind, w);
-          store_chunk<kOpWords>(ring, map1, lane, w, col0, row0, tc.g, mirror);
+          store_operand<kOp, kOpWords>(ring, map1, lane, x, kOpKind, col0, row0, tc.g, mirror, split);
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) x[i] = zero ? 0.f : v[i] * fa;
           if (pr.epi == EPI_APPLY) {
-            uint32_t w[kOpWords];
-            pack_row<kOpWords>(x, kOpKind, w);
-            store_chunk<kOpWords>(ring, map1, lane, w, col0, row0, tc.g, mirror);
+            store_operand<kOp, kOpWords>(ring, map1, lane, x, kOpKind, col0, row0, tc.g, mirror, split);
           } else if (pr.epi == EPI_U_BF16) {
             uint32_t w[16];
             pack_row<16>(x, 3, w);
@@ -585,6 +603,9 @@ static EncodeTiledFn get_encode_fn() {
 // and bs (batch). `box_outer` rows are loaded per TMA request, 128 bytes of
 // the inner dimension each.
 static int op_bytes(int op) { return op == MUON_TF32 ? 4 : 2; }
+// Split operands (MUON_F16X3) take two batch slots per matrix: hi, then lo.
+static int op_halves(int op) { return op == MUON_F16X3 ? 2 : 1; }
+static bool op_is_f16(int op) { return op == MUON_F16 || op == MUON_F16X3; }
 
 static int encode_operand(CUtensorMap* map, const void* base, int op, long long inner,
                           long long outer, long long batch, long long ld, long long bs,
@@ -597,7 +618,7 @@ static int encode_operand(CUtensorMap* map, const void* base, int op, long long 
   if (((ld * es) & 15) != 0 || ((bs * es) & 15) != 0)
     return set_error(MUON_ERR_ARG, "NS operand leading dimension is not a multiple of 16 bytes");
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer),
-                        static_cast<cuuint64_t>(batch)};
+                        static_cast<cuuint64_t>(batch * op_halves(op))};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld * es), static_cast<cuuint64_t>(bs * es)};
   cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / es), static_cast<cuuint32_t>(box_outer), 1};
   cuuint32_t estr[3] = {1, 1, 1};
@@ -637,7 +658,7 @@ namespace muon {
 // have singular values ~1 (entries ~ 1/sqrt(max(rows, cols))). Powers of two
 // keep every rescaling exact. Other modes store X unscaled (1.0).
 float ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dtype) {
-  if (op_dtype != MUON_F16 || rows <= 0 || cols <= 0) return 1.0f;
+  if (!op_is_f16(op_dtype) || rows <= 0 || cols <= 0) return 1.0f;
   const double target = iteration == 0 ? std::sqrt(double(rows) * double(cols))
                                         : std::sqrt(double(std::max(rows, cols)));
   return std::ldexp(1.0f, static_cast<int>(std::lround(std::log2(target))));
@@ -659,6 +680,7 @@ static int encode_output(CUtensorMap* map, const void* base, int dtype, long lon
   EncodeTiledFn fn = get_encode_fn();
   if (!fn) return set_error(MUON_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   const int es = (dtype == MUON_F32 || dtype == MUON_TF32) ? 4 : 2;
+  batch *= op_halves(dtype);  // split operand outputs: hi and lo slots
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
     return set_error(MUON_ERR_ARG, "NS output buffer is not 16-byte aligned");
   if (((ld * es) & 15) != 0 || ((bs * es) & 15) != 0)
@@ -669,7 +691,7 @@ static int encode_output(CUtensorMap* map, const void* base, int dtype, long lon
   cuuint32_t box[3] = {32, 32, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   const CUtensorMapDataType dt = es == 4             ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
-                                 : dtype == MUON_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                 : op_is_f16(dtype) ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                      : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   es == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
@@ -705,8 +727,8 @@ static double p2_near(double x) { return std::ldexp(1.0, static_cast<int>(std::l
 // fp16 storage scales of the gram-form m x m matrices (1 for tf32): A, P, PA
 // have eigenvalues below 3.5 and are stored times m/4; Q (a product of up to
 // three P) below 41, stored times m/64.
-static float gram_scale_a(int m, int op) { return op == MUON_F16 ? float(p2_near(m / 4.0)) : 1.0f; }
-static float gram_scale_q(int m, int op) { return op == MUON_F16 ? float(p2_near(m / 64.0)) : 1.0f; }
+static float gram_scale_a(int m, int op) { return op_is_f16(op) ? float(p2_near(m / 4.0)) : 1.0f; }
+static float gram_scale_q(int m, int op) { return op_is_f16(op) ? float(p2_near(m / 64.0)) : 1.0f; }
 
 static double exec_flops(int rows, int cols, int steps, int algo) {
   const double m = std::min(rows, cols), n = std::max(rows, cols);
@@ -726,7 +748,7 @@ static double exec_flops(int rows, int cols, int steps, int algo) {
 }
 
 int ns_choose_algo(int32_t rows, int32_t cols, int op_dtype, int steps) {
-  if (op_dtype != MUON_F16 && op_dtype != MUON_TF32) return MUON_NS_STANDARD;
+  if (!op_is_f16(op_dtype) && op_dtype != MUON_TF32) return MUON_NS_STANDARD;
   if (rows <= 0 || cols <= 0 || steps < kGramSegment) return MUON_NS_STANDARD;
   if (std::min(rows, cols) > kGramMaxM) return MUON_NS_STANDARD;
   return exec_flops(rows, cols, steps, MUON_NS_GRAM) < 0.9 * exec_flops(rows, cols, steps, MUON_NS_STANDARD)
@@ -736,7 +758,7 @@ int ns_choose_algo(int32_t rows, int32_t cols, int op_dtype, int steps) {
 
 int64_t ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype, int algo) {
   if (rows <= 0 || cols <= 0 || count <= 0) return 0;
-  if (op_dtype != MUON_TF32 && op_dtype != MUON_BF16 && op_dtype != MUON_F16) return 0;
+  if (op_dtype != MUON_TF32 && op_dtype != MUON_BF16 && !op_is_f16(op_dtype)) return 0;
   if (algo != MUON_NS_STANDARD && algo != MUON_NS_GRAM) return 0;
   const int es = op_bytes(op_dtype);
   const int align_el = 16 / es;
@@ -745,15 +767,16 @@ int64_t ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int 
   const int64_t ld_m = (m + align_el - 1) / align_el * align_el;
   auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
   const int n_mm = algo == MUON_NS_GRAM ? 7 : 3;
-  return 2 * up(int64_t(count) * rows * ld_x * es) + n_mm * up(int64_t(count) * m * ld_m * es);
+  const int64_t h = op_halves(op_dtype);
+  return 2 * up(h * count * rows * ld_x * es) + n_mm * up(h * count * m * ld_m * es);
 }
 
 int ns_class_layout(muon_ns_class* cls, void* base, int op_dtype) {
   if (!cls || !base) return set_error(MUON_ERR_ARG, "null class or workspace");
   if ((reinterpret_cast<uintptr_t>(base) & 255u) != 0)
     return set_error(MUON_ERR_ARG, "NS workspace must be 256-byte aligned");
-  if (op_dtype != MUON_TF32 && op_dtype != MUON_BF16 && op_dtype != MUON_F16)
-    return set_error(MUON_ERR_ARG, "op_dtype must be MUON_TF32, MUON_BF16 or MUON_F16");
+  if (op_dtype != MUON_TF32 && op_dtype != MUON_BF16 && !op_is_f16(op_dtype))
+    return set_error(MUON_ERR_ARG, "op_dtype must be MUON_TF32, MUON_BF16, MUON_F16 or MUON_F16X3");
   if (cls->algo != MUON_NS_STANDARD && cls->algo != MUON_NS_GRAM)
     return set_error(MUON_ERR_ARG, "algo must be MUON_NS_STANDARD or MUON_NS_GRAM");
   const int es = op_bytes(op_dtype);
@@ -763,8 +786,9 @@ int ns_class_layout(muon_ns_class* cls, void* base, int op_dtype) {
   cls->ld_x = (cols + align_el - 1) / align_el * align_el;
   cls->ld_m = (m + align_el - 1) / align_el * align_el;
   auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
-  const int64_t xb = up(count * rows * cls->ld_x * es);
-  const int64_t mb = up(count * m * cls->ld_m * es);
+  const int64_t h = op_halves(op_dtype);
+  const int64_t xb = up(h * count * rows * cls->ld_x * es);
+  const int64_t mb = up(h * count * m * cls->ld_m * es);
   uint8_t* p = reinterpret_cast<uint8_t*>(base);
   cls->x0 = p;
   cls->x1 = p + xb;
@@ -831,7 +855,8 @@ struct ClassGeom {
     p.pr.omul = 1.0f;
     p.pr.omul3 = 1.0f;
     p.pr.scale = k->scales;
-    p.work = double(M) * N * K * k->count;
+    p.pr.split = op == MUON_F16X3 ? 1 : 0;
+    p.work = double(M) * N * K * k->count * (p.pr.split ? 3 : 1);
     return p;
   }
 
@@ -922,8 +947,8 @@ int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, in
                    muon_ns_plan** plan_out) {
   if (!plan_out) return set_error(MUON_ERR_ARG, "plan_out is null");
   *plan_out = nullptr;
-  if (op_dtype != MUON_TF32 && op_dtype != MUON_BF16 && op_dtype != MUON_F16)
-    return set_error(MUON_ERR_ARG, "op_dtype must be MUON_TF32, MUON_BF16 or MUON_F16");
+  if (op_dtype != MUON_TF32 && op_dtype != MUON_BF16 && !op_is_f16(op_dtype))
+    return set_error(MUON_ERR_ARG, "op_dtype must be MUON_TF32, MUON_BF16, MUON_F16 or MUON_F16X3");
   if (steps < 1) return set_error(MUON_ERR_UNSUPPORTED, "Newton-Schulz plans need steps >= 1");
   if (n_classes < 1 || n_classes > kMaxProblems / 2)
     return set_error(MUON_ERR_ARG, "n_classes must be in [1, 16]");
@@ -940,7 +965,8 @@ int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, in
     if (k.ld_x < k.cols || k.ld_m < m) return set_error(MUON_ERR_ARG, "leading dimension too small");
     if (k.ld_u < k.cols) return set_error(MUON_ERR_ARG, "ld_u too small");
     if (k.algo == MUON_NS_GRAM) {
-      if (op_dtype == MUON_BF16) return set_error(MUON_ERR_UNSUPPORTED, "MUON_NS_GRAM needs MUON_F16 or MUON_TF32");
+      if (op_dtype == MUON_BF16)
+        return set_error(MUON_ERR_UNSUPPORTED, "MUON_NS_GRAM needs MUON_F16, MUON_F16X3 or MUON_TF32");
       if (m > kGramMaxM) return set_error(MUON_ERR_UNSUPPORTED, "MUON_NS_GRAM supports min(rows, cols) <= 32768");
       if (!k.aa || !k.pa || !k.qa || !k.qb) return set_error(MUON_ERR_ARG, "gram class buffer pointer is null");
       any_gram = true;
@@ -954,7 +980,7 @@ int ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, in
   if (check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "SM count"))
     return MUON_ERR_CUDA;
 
-  const bool f16 = op_dtype == MUON_F16;
+  const bool f16 = op_is_f16(op_dtype);
   const int es = op_bytes(op_dtype);
 
   // Launch slots: three phases per iteration, plus one apply slot at the end
@@ -1092,8 +1118,9 @@ int ns_plan_run(const muon_ns_plan* plan, int* err_dev, cudaStream_t stream) {
   if (!err_dev) return set_error(MUON_ERR_ARG, "err_dev is null");
   constexpr int kMaxDevices = 64;
   static std::mutex attr_mu;
-  static int max_clusters[kMaxDevices][4] = {};  // 0: not set up on that device yet
+  static int max_clusters[kMaxDevices][3] = {};  // per kernel (tf32, bf16, f16); 0: not set up yet
   const int op = plan->op_dtype;
+  const int kern = op == MUON_TF32 ? 0 : op == MUON_BF16 ? 1 : 2;  // fp16 and split fp16 share a kernel
   const void* fn = op == MUON_TF32   ? reinterpret_cast<const void*>(&ns_gemm_kernel<kOpTf32>)
                    : op == MUON_BF16 ? reinterpret_cast<const void*>(&ns_gemm_kernel<kOpBf16>)
                                      : reinterpret_cast<const void*>(&ns_gemm_kernel<kOpF16>);
@@ -1103,7 +1130,7 @@ int ns_plan_run(const muon_ns_plan* plan, int* err_dev, cudaStream_t stream) {
   int clusters = 0;
   {
   std::lock_guard<std::mutex> lock(attr_mu);
-  if (max_clusters[dev][op] == 0) {
+  if (max_clusters[dev][kern] == 0) {
     if (check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
                    "cudaFuncSetAttribute(ns_gemm)"))
       return MUON_ERR_CUDA;
@@ -1123,9 +1150,9 @@ int ns_plan_run(const muon_ns_plan* plan, int* err_dev, cudaStream_t stream) {
     int resident = 0;
     if (check_cuda(cudaOccupancyMaxActiveClusters(&resident, fn, &cfg), "cudaOccupancyMaxActiveClusters"))
       return MUON_ERR_CUDA;
-    max_clusters[dev][op] = std::max(1, std::min(resident, plan->num_sms / 2));
+    max_clusters[dev][kern] = std::max(1, std::min(resident, plan->num_sms / 2));
   }
-  clusters = max_clusters[dev][op];
+  clusters = max_clusters[dev][kern];
   }
   if (plan->sm_limit > 0) clusters = std::max(1, std::min(clusters, plan->sm_limit / 2));
   const int n = static_cast<int>(plan->launches.size());

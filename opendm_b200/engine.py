@@ -37,11 +37,13 @@ from . import _native as N
 from . import trace
 
 _DTYPE_CODE = {torch.bfloat16: N.MUON_BF16, torch.float32: N.MUON_F32}
-PRECISIONS = {"tf32": N.MUON_TF32, "fp16": N.MUON_F16, "bf16": N.MUON_BF16}
+PRECISIONS = {"tf32": N.MUON_TF32, "fp16": N.MUON_F16, "bf16": N.MUON_BF16, "parity": N.MUON_F16X3}
+_F16_OPS = (N.MUON_F16, N.MUON_F16X3)  # fp16 storage: power-of-two scaled operands
 # Newton-Schulz algorithm per shape class: "auto" (the library's choice by
 # executed FLOPs), "standard" (iterate on X) or "gram" (iterate on X X^T).
 NS_ALGOS = ("auto", "standard", "gram")
-_OP_TORCH = {N.MUON_TF32: torch.float32, N.MUON_F16: torch.float16, N.MUON_BF16: torch.bfloat16}
+_OP_TORCH = {N.MUON_TF32: torch.float32, N.MUON_F16: torch.float16, N.MUON_BF16: torch.bfloat16,
+             N.MUON_F16X3: torch.float16}
 
 
 @dataclass
@@ -128,7 +130,11 @@ class _ClassState:
                 "muon_ns_class_layout")
         self.op_dtype = op_dtype
         self.es = 4 if op_dtype == N.MUON_TF32 else 2
-        self.x_stride = rows * int(self.cls.ld_x) * self.es  # bytes per matrix in x0
+        # split operands (MUON_F16X3) keep each matrix as a hi half and, lo_offset
+        # elements further on, a lo half
+        halves = 2 if op_dtype == N.MUON_F16X3 else 1
+        self.lo_offset = rows * int(self.cls.ld_x) if halves == 2 else 0
+        self.x_stride = halves * rows * int(self.cls.ld_x) * self.es  # bytes per matrix in x0
         # fp16 operand scale S0 of the first iteration: the Newton-Schulz input is
         # X0 * S0 (stored so by the orthogonalize paths; muon_momentum_f16 stores
         # d * p and hands the plan the factor to X0 * S0).
@@ -141,12 +147,19 @@ class _ClassState:
             return ((steps - 1) // 3) % 2  # segments of 3 iterations alternate x0, x1
         return (steps - 1) % 2
 
-    def x0_view(self, slot: int) -> torch.Tensor:
-        """The stored Newton-Schulz input of matrix `slot` as a [rows, cols] tensor."""
+    def x0_view(self, slot: int, lo: bool = False) -> torch.Tensor:
+        """The stored Newton-Schulz input of matrix `slot` as a [rows, cols]
+        tensor (its lo half with ``lo`` for split operands)."""
         ld = int(self.cls.ld_x)
-        off = (int(self.cls.x0) - self.workspace.data_ptr()) // self.es + slot * self.rows * ld
+        off = ((int(self.cls.x0) - self.workspace.data_ptr() + slot * self.x_stride) // self.es
+               + (self.lo_offset if lo else 0))
         return torch.empty(0, dtype=_OP_TORCH[self.op_dtype], device=self.workspace.device).set_(
             self.workspace.untyped_storage(), off, (self.rows, self.cols), (ld, 1))
+
+    def x0_value(self, slot: int) -> torch.Tensor:
+        """The stored input's value in fp32 (hi + lo for split operands)."""
+        x = self.x0_view(slot).float()
+        return x + self.x0_view(slot, lo=True).float() if self.lo_offset else x
 
 
 class _PlanState:
@@ -165,6 +178,16 @@ class _PlanState:
         self.redo = None
         self.ns_launches = 0
         self.sm_limit = 0
+
+
+class _F16Inputs:
+    """pscale / scales / redo of a one-off muon_momentum_f16 call (no carried
+    power of two: every matrix is written by the fix-up pass)."""
+
+    def __init__(self, n: int, scales: torch.Tensor, device: torch.device):
+        self.scales = scales
+        self.pscale = torch.zeros(max(n, 1), dtype=torch.float32, device=device)
+        self.redo = torch.zeros(max(n, 1), dtype=torch.int32, device=device)
 
 
 class CudaMuonEngine:
@@ -305,14 +328,14 @@ class CudaMuonEngine:
             cs.cls.ld_u = ld_u
             st.classes.append(cs)
         st.scales = torch.zeros(max(len(items), 1), dtype=torch.float32, device=self.device)
-        if self.op_dtype == N.MUON_F16:
+        if self.op_dtype in _F16_OPS:
             st.pscale = torch.zeros_like(st.scales)
             st.redo = torch.zeros(st.scales.numel(), dtype=torch.int32, device=self.device)
         first = 0
         for cs in st.classes:
             cs.first_seg = first
             cs.cls.scales = c_void_p(st.scales.data_ptr() + 4 * first)
-            if self.op_dtype == N.MUON_F16:
+            if self.op_dtype in _F16_OPS:
                 cs.cls.flags = N.MUON_NS_INPUT_SCALED  # x0 = d * p, scales = the factor to the normalised input
             first += cs.count
         if ns_steps >= 1:
@@ -356,7 +379,7 @@ class CudaMuonEngine:
         table = self._tables.get(N.struct_bytes(segs))
         partials = torch.empty(max(total, 1), dtype=torch.float32, device=self.device)
         if dir_dtype is None:
-            dir_dtype = N.MUON_F32 if self.op_dtype == N.MUON_F16 else self.op_dtype
+            dir_dtype = N.MUON_F32 if self.op_dtype in _F16_OPS else self.op_dtype
         gs = self.grad_scale if gradients else None
         N.check(self.lib.muon_momentum_scaled(c_void_p(table.data_ptr()), len(segs), total, grad_dtype, dir_dtype,
                                               c_float(momentum), int(bool(nesterov)), c_float(eps),
@@ -365,8 +388,8 @@ class CudaMuonEngine:
                 "muon_momentum_scaled")
         self.kernel_launches += 2 if total > 0 else 1
 
-    def _momentum_f16(self, st: _PlanState, segs: list, grad_dtype: int, momentum: float, nesterov: bool,
-                      eps: float = 1e-7) -> None:
+    def _momentum_f16(self, st, segs: list, grad_dtype: int, momentum: float, nesterov: bool,
+                      eps: float = 1e-7, gradients: bool = True) -> None:
         """One muon_momentum_f16 call: momentum, norm, the fp16 operand and
         each matrix's Newton-Schulz input factor (plus the fix-up of matrices
         whose carried power of two does not fit this step)."""
@@ -376,7 +399,7 @@ class CudaMuonEngine:
             total += int(self.lib.muon_momentum_chunks(sg.rows, sg.cols))
         table = self._tables.get(N.struct_bytes(segs))
         partials = torch.empty(max(total, 1), dtype=torch.float32, device=self.device)
-        gs = self.grad_scale
+        gs = self.grad_scale if gradients else None
         N.check(self.lib.muon_momentum_f16(c_void_p(table.data_ptr()), len(segs), total, grad_dtype, c_float(momentum),
                                            int(bool(nesterov)), c_float(eps), c_void_p(partials.data_ptr()),
                                            c_void_p(st.pscale.data_ptr()), c_void_p(st.scales.data_ptr()),
@@ -399,7 +422,7 @@ class CudaMuonEngine:
         grads = [it.grad for it in items]
         gdt = {_dtype_code(g) for g in grads if g is not None} or {N.MUON_F32}
         # Segments in class order: segment index == scale index.
-        f16 = self.op_dtype == N.MUON_F16
+        f16 = self.op_dtype in _F16_OPS
         keep: list[torch.Tensor] = []  # contiguous copies of strided gradients
         by_dtype: dict[int, list] = {}
         for i in st.seg_order:
@@ -414,7 +437,7 @@ class CudaMuonEngine:
                 # one pass: momentum, norm and the fp16 operand d * p (muon_momentum_f16)
                 seg = N.MomentumF16Seg()
                 seg.dst = cs.cls.x0 + slot * cs.x_stride
-                seg.mul, seg.scale_index = cs.x0_scale, cs.first_seg + slot
+                seg.mul, seg.scale_index, seg.lo_offset = cs.x0_scale, cs.first_seg + slot, cs.lo_offset
             else:
                 seg = N.MomentumSeg()
                 seg.direction = cs.cls.x0 + slot * cs.x_stride
@@ -503,8 +526,8 @@ class CudaMuonEngine:
 
     def _normalized_input(self, st: _PlanState, cs: _ClassState, slot: int) -> torch.Tensor:
         """The unit-norm Newton-Schulz input of one matrix, fp32 (ns_steps == 0 result)."""
-        x = cs.x0_view(slot).float()
-        if self.op_dtype == N.MUON_F16:  # x0 = d * p; scales = (1 / ||d||) * x0_scale / p
+        x = cs.x0_value(slot)
+        if self.op_dtype in _F16_OPS:  # x0 = d * p; scales = (1 / ||d||) * x0_scale / p
             return x * st.scales[cs.first_seg + slot] / cs.x0_scale
         return x * st.scales[cs.first_seg + slot]
 
@@ -595,47 +618,41 @@ class CudaMuonEngine:
             if m.ndim != 2 or m.dtype != torch.float32 or not m.is_contiguous() or m.device != self.device:
                 raise RuntimeError("orthogonalize_many takes contiguous fp32 matrices on the engine's device")
             groups.setdefault((int(m.shape[0]), int(m.shape[1]), dt), []).append(i)
-        f16 = self.op_dtype == N.MUON_F16
-        classes, segs, convs, outs = [], [], [], [None] * len(mats)
+        f16 = self.op_dtype in _F16_OPS
+        classes, segs, outs = [], [], [None] * len(mats)
         scales = torch.zeros(len(mats), dtype=torch.float32, device=self.device)
-        staging = torch.empty(sum(m.numel() for m in mats), dtype=torch.float32, device=self.device) if f16 else None
         keep = []
-        first, soff, chunks = 0, 0, 0
+        first = 0
         for (rows, cols, dt), idxs in groups.items():
             cs = _ClassState(rows, cols, dt, len(idxs), self.op_dtype, self.device, int(steps), self._class_algo())
             ld_u = _pad16(cols, dt)
             u_buf = torch.empty((len(idxs), rows, ld_u), dtype=dt, device=self.device)
             cs.cls.u_dtype, cs.cls.u_out, cs.cls.ld_u = _dtype_code(u_buf), c_void_p(u_buf.data_ptr()), ld_u
             cs.cls.scales = c_void_p(scales.data_ptr() + 4 * first)
+            if f16:
+                cs.cls.flags = N.MUON_NS_INPUT_SCALED
             for slot, i in enumerate(idxs):
                 # momentum 0 with exp_avg aliasing the input: exp_avg = d = input,
                 # i.e. a copy into the operand buffer plus the Frobenius norm
-                seg = N.MomentumSeg()
+                seg = N.MomentumF16Seg() if f16 else N.MomentumSeg()
                 seg.grad, seg.exp_avg = mats[i].data_ptr(), mats[i].data_ptr()
-                seg.rows, seg.cols = rows, cols
+                seg.rows, seg.cols, seg.ld = rows, cols, int(cs.cls.ld_x)
                 if f16:
-                    seg.direction, seg.ld = staging.data_ptr() + 4 * soff, cols
-                    cv = N.ConvertSeg()
-                    cv.src, cv.dst = seg.direction, cs.cls.x0 + slot * cs.x_stride
-                    cv.rows, cv.cols, cv.ld_src, cv.ld_dst = rows, cols, cols, int(cs.cls.ld_x)
-                    cv.chunk_begin, cv.mul, cv.scale_index = chunks, cs.x0_scale, first + slot
-                    convs.append(cv)
-                    chunks += int(self.lib.muon_momentum_chunks(rows, cols))
-                    soff += rows * cols
+                    seg.dst = cs.cls.x0 + slot * cs.x_stride
+                    seg.mul, seg.scale_index, seg.lo_offset = cs.x0_scale, first + slot, cs.lo_offset
                 else:
-                    seg.direction, seg.ld = cs.cls.x0 + slot * cs.x_stride, int(cs.cls.ld_x)
+                    seg.direction = cs.cls.x0 + slot * cs.x_stride
                 segs.append(seg)
                 outs[i] = u_buf[slot, :, :cols]
             classes.append(cs)
             keep += [cs.workspace, u_buf]
             first += len(idxs)
-        self._momentum(segs, N.MUON_F32, 0.0, False, scales.data_ptr(), eps=eps, gradients=False)
         if f16:
-            table = _upload(N.struct_bytes(convs), self.device)
-            N.check(self.lib.muon_convert_f16(c_void_p(table.data_ptr()), len(convs), chunks,
-                                              c_void_p(scales.data_ptr()), _stream_handle()), "muon_convert_f16")
-            self.kernel_launches += 1
-            keep += [table, staging]
+            tmp = _F16Inputs(len(mats), scales, self.device)  # no carried scale: every matrix takes the fix-up
+            self._momentum_f16(tmp, segs, N.MUON_F32, 0.0, False, eps=eps, gradients=False)
+            keep += [tmp.pscale, tmp.redo]
+        else:
+            self._momentum(segs, N.MUON_F32, 0.0, False, scales.data_ptr(), eps=eps, gradients=False)
         plans = self._create_plans([cs.cls for cs in classes], steps)
         try:
             self._run_plans(plans)
@@ -687,30 +704,23 @@ class CudaMuonEngine:
         cs = _ClassState(rows, cols, torch.float32, 1, self.op_dtype, self.device, int(steps), self._class_algo())
         scales = torch.zeros(1, dtype=torch.float32, device=self.device)
         exp_avg = torch.zeros((rows, cols), dtype=torch.float32, device=self.device)
-        seg = N.MomentumSeg()
+        f16 = self.op_dtype in _F16_OPS
+        seg = N.MomentumF16Seg() if f16 else N.MomentumSeg()
         seg.grad = src.data_ptr()
         seg.exp_avg = exp_avg.data_ptr()
-        seg.rows, seg.cols = rows, cols
-        f16 = self.op_dtype == N.MUON_F16
-        staging = torch.empty((rows, cols), dtype=torch.float32, device=self.device) if f16 else None
-        if f16:
-            seg.direction, seg.ld = staging.data_ptr(), cols
-        else:
-            seg.direction, seg.ld = cs.cls.x0, int(cs.cls.ld_x)
+        seg.rows, seg.cols, seg.ld = rows, cols, int(cs.cls.ld_x)
         # momentum 0, no Nesterov: exp_avg = g and d = g, i.e. a copy plus the norm.
-        self._momentum([seg], _dtype_code(src), 0.0, False, scales.data_ptr(), eps=eps, gradients=False)
         if f16:
-            cv = N.ConvertSeg()
-            cv.src, cv.dst = staging.data_ptr(), cs.cls.x0
-            cv.rows, cv.cols, cv.ld_src, cv.ld_dst = rows, cols, cols, int(cs.cls.ld_x)
-            cv.chunk_begin, cv.mul, cv.scale_index = 0, cs.x0_scale, 0
-            table = _upload(N.struct_bytes([cv]), self.device)
-            N.check(self.lib.muon_convert_f16(c_void_p(table.data_ptr()), 1,
-                                              int(self.lib.muon_momentum_chunks(rows, cols)),
-                                              c_void_p(scales.data_ptr()), _stream_handle()), "muon_convert_f16")
-        if steps < 1:
+            seg.dst, seg.mul, seg.scale_index, seg.lo_offset = cs.cls.x0, cs.x0_scale, 0, cs.lo_offset
+            cs.cls.flags = N.MUON_NS_INPUT_SCALED
+            tmp = _F16Inputs(1, scales, self.device)
+            self._momentum_f16(tmp, [seg], _dtype_code(src), 0.0, False, eps=eps, gradients=False)
+        else:
+            seg.direction = cs.cls.x0
+            self._momentum([seg], _dtype_code(src), 0.0, False, scales.data_ptr(), eps=eps, gradients=False)
+        if steps < 1:  # the normalised input itself
             if f16:
-                return staging * scales[0]
+                return cs.x0_value(0) * scales[0] / cs.x0_scale
             return cs.x0_view(0).float() * scales[0]
         cs.cls.scales = c_void_p(scales.data_ptr())
         cs.cls.u_out = c_void_p(out_buf.data_ptr())

@@ -19,6 +19,10 @@ The arithmetic runs in the sm_100a kernels of ``libopendm_muon.so`` through
   of two to stay in fp16's range; the same 11-bit significand as tf32 at
   twice the tensor-core rate. "tf32": operands rounded to tf32, the same
   accuracy at half the rate. "bf16": ~1e-2 relative update error (opt-in).
+  "parity": each fp16 operand split into a hi and a lo half and every
+  product taken as hi*hi + hi*lo + lo*hi (~22-bit operands, 3x the tensor
+  work): within ~1e-5 of the fp32 reference even on rank-deficient inputs,
+  where the 11-bit types amplify rounding in the null space past the bar.
 * ``ns_algo``: "auto" (default: per shape, the form with fewer executed
   FLOPs), "standard" (the reference's iteration on X) or "gram" (the
   iteration on the m x m gram matrix X X^T, applied to X every three
@@ -225,8 +229,8 @@ class MuonAdamW(torch.optim.Optimizer):
             raise RuntimeError("MuonAdamW metadata is missing; mark parameters before FSDP wrapping.")
         if sharding not in ("auto", "off"):
             raise ValueError(f"sharding must be 'auto' or 'off', got {sharding!r}")
-        if precision not in ("tf32", "fp16", "bf16"):
-            raise ValueError(f"precision must be 'tf32', 'fp16' or 'bf16', got {precision!r}")
+        if precision not in ("tf32", "fp16", "bf16", "parity"):
+            raise ValueError(f"precision must be 'tf32', 'fp16', 'bf16' or 'parity', got {precision!r}")
         if ns_algo not in ("auto", "standard", "gram"):
             raise ValueError(f"ns_algo must be 'auto', 'standard' or 'gram', got {ns_algo!r}")
         effective_lr(1.0, 1.0, 1.0, (1, 1), scale_mode)  # validates scale_mode

@@ -500,3 +500,53 @@ def test_momentum_f16_one_pass_operand_and_fixup():
             assert O.rel_frobenius(got.cpu().numpy(), want.cpu().numpy()) < 1e-3, (step, i)
             # the stored entries stay far inside fp16's range
             assert float(x0[i][:, :c].abs().max()) < 2048.0
+
+
+# ---------------------------------------------------- split operands ("parity")
+PARITY_TOL = 2e-4  # Gaussian inputs; the emulation predicts ~3e-6 plus fp32 accumulation
+
+
+@pytest.mark.parametrize("shape", [(1, 16), (33, 70), (70, 33), (130, 300), (300, 130), (512, 2048), (2048, 512),
+                                   (1000, 1000)])
+@pytest.mark.parametrize("algo", ["standard", "gram"])
+def test_orthogonalize_parity_precision(algo, shape):
+    """Split fp16 operands (hi + lo halves, three MMAs per product) against the
+    fp32 reference: far inside the bar on Gaussian inputs, both forms."""
+    eng = _engine_for("parity", algo)
+    x = _rand(shape, sum(shape)) * 1.95
+    got = eng.orthogonalize(x.to(eng.device)).cpu().numpy()
+    eng.check_errors(block=True)
+    err = O.rel_frobenius(got, O.zeropower_via_newtonschulz5(x.numpy()))
+    print(f"parity-mode {algo} {shape} {err:.2e}")
+    assert err < PARITY_TOL, err
+
+
+def _rank_deficient(shape, kind, seed):
+    rng = np.random.default_rng(seed)
+    m, n = shape
+    if kind == "rank1":
+        return np.outer(rng.standard_normal(m), rng.standard_normal(n)).astype(np.float32) * 1e-3
+    k = min(shape)  # singular values decaying by e^-20 across the rank
+    u, _ = np.linalg.qr(rng.standard_normal((m, k)))
+    v, _ = np.linalg.qr(rng.standard_normal((n, k)))
+    return ((u * np.exp(-20.0 * np.arange(k) / k)) @ v.T).astype(np.float32) * 1e-3
+
+
+@pytest.mark.parametrize("kind", ["rank1", "expdecay20"])
+@pytest.mark.parametrize("shape", [(512, 2048), (2048, 512), (1024, 1024)])
+def test_rank_deficient_inputs_parity_vs_fp16(kind, shape):
+    """Inputs with a large null space, where any 11-bit operand type exceeds the
+    1e-2 bar (rounding noise in the null directions is amplified ~a^5 by the
+    quintic): the parity precision stays within it in both forms. The fp16
+    result is measured alongside and must indeed exceed the parity one."""
+    x = _rank_deficient(shape, kind, 5)
+    ref = O.zeropower_via_newtonschulz5(x)
+    errs = {}
+    for prec, algo in (("parity", "standard"), ("parity", "gram"), ("fp16", "auto")):
+        eng = _engine_for(prec, algo)
+        got = eng.orthogonalize(torch.from_numpy(x).to(eng.device)).cpu().numpy()
+        eng.check_errors(block=True)
+        errs[(prec, algo)] = O.rel_frobenius(got, ref)
+    print(f"rank-deficient {kind} {shape} " + " ".join(f"{k[0]}/{k[1]} {v:.2e}" for k, v in errs.items()))
+    assert errs[("parity", "standard")] < 2e-3 and errs[("parity", "gram")] < 2e-3, errs
+    assert errs[("fp16", "auto")] > errs[("parity", "standard")], errs
