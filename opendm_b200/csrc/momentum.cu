@@ -401,6 +401,7 @@ int launch_direction_f16(const muon_direction_f16_seg* segs_dev, int n_segs, int
 constexpr float kF16Headroom = 1.0f / 16.0f;   // stored entries ~1/16 instead of ~1
 constexpr float kF16MaxNormTimesP = 32768.0f;  // ||d|| * p below this: no entry can overflow fp16
 constexpr float kF16MinRatio = 1.0f / 256.0f;  // p at least this fraction of the ideal one
+constexpr int64_t kFixupCtas = 1184;           // fix-up grid (8 CTAs on each of 148 SMs), grid-stride
 
 __device__ __forceinline__ int find_f16_segment(const muon_momentum_f16_seg* segs, int n_segs, int64_t chunk) {
   int lo = 0, hi = n_segs - 1;
@@ -557,21 +558,40 @@ __global__ void momentum_f16_scale_kernel(const muon_momentum_f16_seg* __restric
 
 // Fix-up: the operand of the matrices flagged by momentum_f16_scale_kernel,
 // rebuilt from the gradient and the advanced momentum with the same
-// operations and written as fp16(d * p) with the new p.
+// operations and written as fp16(d * p) with the new p. A grid-stride loop
+// over the chunks that jumps over whole segments nobody flagged, so a step
+// without fix-ups costs one pass over the segment table per CTA.
+template <int kGradDt>
+__device__ __forceinline__ void fixup_chunk(const muon_momentum_f16_seg& sg, int64_t chunk, float p, float mu,
+                                            bool nest, const float* __restrict__ grad_scale);
+
 template <int kGradDt>
 __global__ void __launch_bounds__(MOM_THREADS) momentum_f16_fixup_kernel(const muon_momentum_f16_seg* __restrict__ segs,
-                                                                         int n_segs, float mu, int nesterov,
+                                                                         int n_segs, int64_t total_chunks, float mu,
+                                                                         int nesterov,
                                                                          const float* __restrict__ pscale,
                                                                          const int* __restrict__ redo,
                                                                          const float* __restrict__ grad_scale) {
-  const int64_t chunk = blockIdx.x;
-  const muon_momentum_f16_seg sg = segs[find_f16_segment(segs, n_segs, chunk)];
-  if (redo[sg.scale_index] == 0) return;
+  const int64_t stride = gridDim.x;
+  for (int64_t chunk = blockIdx.x; chunk < total_chunks;) {
+    const int s = find_f16_segment(segs, n_segs, chunk);
+    const muon_momentum_f16_seg sg = segs[s];
+    if (redo[sg.scale_index] == 0) {  // next chunk of this CTA at or after the next segment
+      const int64_t next = s + 1 < n_segs ? segs[s + 1].chunk_begin : total_chunks;
+      chunk += (next - chunk + stride - 1) / stride * stride;
+      continue;
+    }
+    fixup_chunk<kGradDt>(sg, chunk, pscale[sg.scale_index], mu, nesterov != 0, grad_scale);
+    chunk += stride;
+  }
+}
+
+template <int kGradDt>
+__device__ __forceinline__ void fixup_chunk(const muon_momentum_f16_seg& sg, int64_t chunk, float p, float mu,
+                                            bool nest, const float* __restrict__ grad_scale) {
   const int64_t numel = sg.rows * sg.cols;
   const int64_t e0 = (chunk - sg.chunk_begin) * MOM_CHUNK;
   const int64_t e1 = min(e0 + MOM_CHUNK, numel);
-  const float p = pscale[sg.scale_index];
-  const bool nest = nesterov != 0;
   const bool clip = grad_scale != nullptr && sg.grad != nullptr;
   const float coef = clip ? *grad_scale : 1.f;
   __half* dst = reinterpret_cast<__half*>(sg.dst);
@@ -636,12 +656,13 @@ int launch_momentum_f16(const muon_momentum_f16_seg* segs_dev, int n_segs, int64
       segs_dev, n_segs, total_chunks, partials_dev, eps, pscale_dev, scales_dev, redo_dev);
   if (check_cuda(cudaGetLastError(), "momentum_f16 scale launch")) return MUON_ERR_CUDA;
   if (total_chunks > 0) {
+    const dim3 fix_grid(static_cast<unsigned>(total_chunks < kFixupCtas ? total_chunks : kFixupCtas));
     if (grad_dtype == MUON_BF16)
-      momentum_f16_fixup_kernel<MUON_BF16><<<grid, MOM_THREADS, 0, stream>>>(segs_dev, n_segs, momentum, nesterov,
-                                                                            pscale_dev, redo_dev, grad_scale);
+      momentum_f16_fixup_kernel<MUON_BF16><<<fix_grid, MOM_THREADS, 0, stream>>>(
+          segs_dev, n_segs, total_chunks, momentum, nesterov, pscale_dev, redo_dev, grad_scale);
     else
-      momentum_f16_fixup_kernel<MUON_F32><<<grid, MOM_THREADS, 0, stream>>>(segs_dev, n_segs, momentum, nesterov,
-                                                                           pscale_dev, redo_dev, grad_scale);
+      momentum_f16_fixup_kernel<MUON_F32><<<fix_grid, MOM_THREADS, 0, stream>>>(
+          segs_dev, n_segs, total_chunks, momentum, nesterov, pscale_dev, redo_dev, grad_scale);
     if (check_cuda(cudaGetLastError(), "momentum_f16 fix-up launch")) return MUON_ERR_CUDA;
   }
   return MUON_OK;
