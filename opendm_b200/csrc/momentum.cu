@@ -558,9 +558,10 @@ __global__ void momentum_f16_scale_kernel(const muon_momentum_f16_seg* __restric
 
 // Fix-up: the operand of the matrices flagged by momentum_f16_scale_kernel,
 // rebuilt from the gradient and the advanced momentum with the same
-// operations and written as fp16(d * p) with the new p. A grid-stride loop
-// over the chunks that jumps over whole segments nobody flagged, so a step
-// without fix-ups costs one pass over the segment table per CTA.
+// operations and written as fp16(d * p) with the new p. Every CTA reads the
+// flags of 256 segments at a time in one parallel pass and then takes its
+// share (grid stride) of the chunks of the flagged ones, so a step without
+// fix-ups costs each CTA one or two dependent loads per 256 segments.
 template <int kGradDt>
 __device__ __forceinline__ void fixup_chunk(const muon_momentum_f16_seg& sg, int64_t chunk, float p, float mu,
                                             bool nest, const float* __restrict__ grad_scale);
@@ -572,17 +573,24 @@ __global__ void __launch_bounds__(MOM_THREADS) momentum_f16_fixup_kernel(const m
                                                                          const float* __restrict__ pscale,
                                                                          const int* __restrict__ redo,
                                                                          const float* __restrict__ grad_scale) {
-  const int64_t stride = gridDim.x;
-  for (int64_t chunk = blockIdx.x; chunk < total_chunks;) {
-    const int s = find_f16_segment(segs, n_segs, chunk);
-    const muon_momentum_f16_seg sg = segs[s];
-    if (redo[sg.scale_index] == 0) {  // next chunk of this CTA at or after the next segment
-      const int64_t next = s + 1 < n_segs ? segs[s + 1].chunk_begin : total_chunks;
-      chunk += (next - chunk + stride - 1) / stride * stride;
-      continue;
+  __shared__ int flagged[MOM_THREADS];
+  __shared__ int n_flagged;
+  for (int base = 0; base < n_segs; base += MOM_THREADS) {
+    if (threadIdx.x == 0) n_flagged = 0;
+    __syncthreads();
+    const int s = base + static_cast<int>(threadIdx.x);
+    if (s < n_segs && redo[segs[s].scale_index] != 0) flagged[atomicAdd(&n_flagged, 1)] = s;
+    __syncthreads();
+    const int nf = n_flagged;
+    for (int f = 0; f < nf; ++f) {
+      const int si = flagged[f];
+      const muon_momentum_f16_seg sg = segs[si];
+      const int64_t end = si + 1 < n_segs ? segs[si + 1].chunk_begin : total_chunks;
+      const float p = pscale[sg.scale_index];
+      for (int64_t chunk = sg.chunk_begin + blockIdx.x; chunk < end; chunk += gridDim.x)
+        fixup_chunk<kGradDt>(sg, chunk, p, mu, nesterov != 0, grad_scale);
     }
-    fixup_chunk<kGradDt>(sg, chunk, pscale[sg.scale_index], mu, nesterov != 0, grad_scale);
-    chunk += stride;
+    __syncthreads();  // every thread is done with flagged[] before the next batch
   }
 }
 
