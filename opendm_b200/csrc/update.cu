@@ -34,22 +34,20 @@ __device__ __forceinline__ float upd_elem(float p, float u, float neg_eff, float
   return fmaf(neg_eff, u, p);
 }
 
-// The segment's fields arrive by value (a reference to a local copy of the
-// segment would place it in local memory).
 template <bool kBf16>
-__device__ __forceinline__ void update_chunk(void* param, const void* update, int64_t cols, int64_t ld, int64_t numel,
-                                             float eff, int64_t e0, int64_t e1, float wd_factor) {
-  const float neg_eff = -eff;
-  const bool vec_ok = ld == cols && (numel % 8) == 0 &&
-                      ((reinterpret_cast<uintptr_t>(param) | reinterpret_cast<uintptr_t>(update)) & 15u) == 0;
+__device__ __forceinline__ void update_chunk(const muon_update_seg& sg, int64_t e0, int64_t e1, float wd_factor) {
+  const float neg_eff = -sg.eff;
+  const int64_t numel = sg.rows * sg.cols;
+  const bool vec_ok = sg.ld == sg.cols && (numel % 8) == 0 &&
+                      ((reinterpret_cast<uintptr_t>(sg.param) | reinterpret_cast<uintptr_t>(sg.update)) & 15u) == 0;
   if (vec_ok) {
     for (int it = 0; it < UPD_ITERS; ++it) {
       const int64_t e = e0 + (int64_t(it) * UPD_THREADS + threadIdx.x) * UPD_VEC;
       if (e >= e1) break;
       if constexpr (kBf16) {
-        uint4* pp = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(param) + e);
+        uint4* pp = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(sg.param) + e);
         const uint4 praw = *pp;
-        const uint4 uraw = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(update) + e));
+        const uint4 uraw = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(sg.update) + e));
         const __nv_bfloat162* ph = reinterpret_cast<const __nv_bfloat162*>(&praw);
         const __nv_bfloat162* uh = reinterpret_cast<const __nv_bfloat162*>(&uraw);
         uint4 out;
@@ -63,8 +61,8 @@ __device__ __forceinline__ void update_chunk(void* param, const void* update, in
         }
         *pp = out;
       } else {
-        float4* pp = reinterpret_cast<float4*>(reinterpret_cast<float*>(param) + e);
-        const float4* up = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(update) + e);
+        float4* pp = reinterpret_cast<float4*>(reinterpret_cast<float*>(sg.param) + e);
+        const float4* up = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(sg.update) + e);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           float4 p = pp[h];
@@ -79,33 +77,30 @@ __device__ __forceinline__ void update_chunk(void* param, const void* update, in
     }
   } else {
     for (int64_t e = e0 + threadIdx.x; e < e1; e += UPD_THREADS) {
-      const int64_t r = e / cols, c = e - r * cols;
-      const int64_t ui = r * ld + c;
+      const int64_t r = e / sg.cols, c = e - r * sg.cols;
+      const int64_t ui = r * sg.ld + c;
       if constexpr (kBf16) {
-        __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(param) + e;
-        const float u = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(update)[ui]);
+        __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(sg.param) + e;
+        const float u = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sg.update)[ui]);
         *p = __float2bfloat16_rn(upd_elem<true>(__bfloat162float(*p), u, neg_eff, wd_factor));
       } else {
-        float* p = reinterpret_cast<float*>(param) + e;
-        *p = upd_elem<false>(*p, reinterpret_cast<const float*>(update)[ui], neg_eff, wd_factor);
+        float* p = reinterpret_cast<float*>(sg.param) + e;
+        *p = upd_elem<false>(*p, reinterpret_cast<const float*>(sg.update)[ui], neg_eff, wd_factor);
       }
     }
   }
 }
 
-// (256, 4): lets ptxas use up to 64 registers; with the bound on threads
-// alone it settled on 32 and spilled.
-__global__ void __launch_bounds__(UPD_THREADS, 4) apply_update_kernel(const muon_update_seg* __restrict__ segs,
+__global__ void __launch_bounds__(UPD_THREADS) apply_update_kernel(const muon_update_seg* __restrict__ segs,
                                                                    int n_segs, float wd_factor) {
   const int64_t chunk = blockIdx.x;
   const muon_update_seg sg = segs[find_update_segment(segs, n_segs, chunk)];
   const int64_t e0 = (chunk - sg.chunk_begin) * UPD_CHUNK;
-  const int64_t numel = sg.rows * sg.cols;
-  const int64_t e1 = min(e0 + UPD_CHUNK, numel);
+  const int64_t e1 = min(e0 + UPD_CHUNK, sg.rows * sg.cols);
   if (sg.param_dtype == MUON_BF16)
-    update_chunk<true>(sg.param, sg.update, sg.cols, sg.ld, numel, sg.eff, e0, e1, wd_factor);
+    update_chunk<true>(sg, e0, e1, wd_factor);
   else
-    update_chunk<false>(sg.param, sg.update, sg.cols, sg.ld, numel, sg.eff, e0, e1, wd_factor);
+    update_chunk<false>(sg, e0, e1, wd_factor);
 }
 
 int launch_apply_update(const muon_update_seg* segs_dev, int n_segs, int64_t total_chunks, float wd_factor,
