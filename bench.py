@@ -369,6 +369,7 @@ def run_ours(args):
     opt = MuonAdamW(model, lr=LR, betas=BETAS, eps=EPS, weight_decay=WD, muon_momentum=MOMENTUM,
                     muon_ns_steps=NS_STEPS, precision=args.precision, state_sharding=world > 1,
                     allgather=args.allgather, comm_sms=args.comm_sms,
+                    allgather_waves=args.waves, allgather_wave_ratio=args.wave_ratio,
                     adamw_sharding=args.adamw_sharding and world > 1)
     params = list(model.parameters())
     ggen = torch.Generator(device=device).manual_seed(1)
@@ -636,6 +637,7 @@ def run_ours(args):
                             "waves": bucket.n_waves if bucket is not None else 1,
                             "transport": opt.allgather,
                             "comm_sms": opt.comm_sms if opt.allgather == "nccl" else 0,
+                            "wave_ratio": opt.allgather_wave_ratio,
                             "exposed_wait_ms": round(ag_wait_ms, 3),
                             "adamw_allgather_bytes_received": (adam_shards.nbytes_received()
                                                                if adam_shards is not None else 0),
@@ -662,6 +664,10 @@ def main(argv=None):
     ap.add_argument("--allgather", default="nccl", choices=["nccl", "p2p"],
                     help="parameter all-gather of the sharded step (N > 1)")
     ap.add_argument("--comm-sms", type=int, default=32, help="SMs left to an overlapping NCCL all-gather")
+    ap.add_argument("--waves", type=int, default=None,
+                    help="N > 1: all-gather waves per step (default: the optimizer's choice)")
+    ap.add_argument("--wave-ratio", type=float, default=0.7,
+                    help="N > 1: each wave's FLOP share relative to the wave before (default 0.7)")
     ap.add_argument("--adamw-sharding", action=argparse.BooleanOptionalAction, default=True,
                     help="N > 1: each rank updates an equal range of the AdamW parameters, then all-gather "
                          "(default on; --no-adamw-sharding runs the whole AdamW group on every rank)")

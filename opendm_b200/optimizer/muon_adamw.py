@@ -43,6 +43,9 @@ The arithmetic runs in the sm_100a kernels of ``libopendm_muon.so`` through
   Newton-Schulz of the next (default on CUDA with at least 6 matrices per
   rank: 4 at 8 or more ranks carrying >= 16 dense TFLOP each, else 3;
   1 otherwise).
+* ``allgather_wave_ratio``: each wave's share of a rank's Newton-Schulz
+  FLOPs relative to the wave before (default 0.7: decreasing waves; 1.0:
+  equal waves).
 * ``comm_sms``: SMs the Newton-Schulz launches leave free while an NCCL
   all-gather overlaps them, and the CTA limit of the optimizer's own NCCL
   group for that all-gather (default 32).
@@ -211,7 +214,8 @@ class MuonAdamW(torch.optim.Optimizer):
                  muon_ns_steps: int = 5, muon_lr_scale: float = 1.0, muon_moonlight_coefficient: float = 0.2,
                  precision: str = "fp16", scale_mode: str = "reference", sharding: str = "auto",
                  state_sharding: bool = False, process_group=None, ns_algo: str = "auto",
-                 allgather_waves: int | None = None, comm_sms: int = 32, allgather: str = "nccl",
+                 allgather_waves: int | None = None, allgather_wave_ratio: float = 0.7, comm_sms: int = 32,
+                 allgather: str = "nccl",
                  fsdp_owner_ns: bool = True, max_grad_norm: float | None = None, adamw_sharding: bool = False,
                  _engine=None) -> None:
         adamw_params, muon_params, muon_shapes, muon_names = [], [], [], []
@@ -261,6 +265,8 @@ class MuonAdamW(torch.optim.Optimizer):
         self._ag_group = None  # NCCL group of the parameter all-gather (CTA-limited)
         if allgather_waves is not None and int(allgather_waves) < 1:
             raise ValueError("allgather_waves must be >= 1")
+        if not float(allgather_wave_ratio) > 0:
+            raise ValueError("allgather_wave_ratio must be > 0")
         if allgather not in ("nccl", "p2p"):
             raise ValueError(f"allgather must be 'nccl' or 'p2p', got {allgather!r}")
         self.allgather = allgather
@@ -276,6 +282,7 @@ class MuonAdamW(torch.optim.Optimizer):
         self._pending_clip: torch.Tensor | None = None  # [total, coefficient] for the next step
         self.last_grad_norm: torch.Tensor | None = None
         self.allgather_waves = allgather_waves
+        self.allgather_wave_ratio = float(allgather_wave_ratio)
         self.comm_sms = max(int(comm_sms), 0)
 
     # ---------------------------------------------------------------- groups
@@ -606,7 +613,7 @@ class MuonAdamW(torch.optim.Optimizer):
             shapes, steps = group["muon_shapes"], int(group["muon_ns_steps"])
             owners = assign_owners(shapes, world, steps)
             n_waves = self._n_waves(shapes, world, self._device_for_params(group["params"]), steps)
-            waves = assign_waves(shapes, owners, world, n_waves, steps)
+            waves = assign_waves(shapes, owners, world, n_waves, steps, self.allgather_wave_ratio)
             self._owners[key] = owners
             self._waves[key] = waves
             device = self._device_for_params(group["params"])

@@ -62,17 +62,17 @@ def _bytes_per_flop(shape: tuple[int, int], steps: int) -> float:
 
 
 def assign_waves(shapes: list[tuple[int, int]], owners: list[int], world_size: int, n_waves: int,
-                 steps: int = 5) -> list[int]:
+                 steps: int = 5, ratio: float = 0.7) -> list[int]:
     """Wave index of each matrix: every rank orders its own matrices by
     decreasing bytes per FLOP and cuts them at the cumulative FLOP shares of
-    ``wave_fractions``. Deterministic, so every rank computes every rank's
-    waves."""
+    ``wave_fractions(n_waves, ratio)``. Deterministic, so every rank computes
+    every rank's waves."""
     waves = [0] * len(shapes)
     if n_waves <= 1:
         return waves
     bounds = []
     acc = 0.0
-    for f in wave_fractions(n_waves)[:-1]:
+    for f in wave_fractions(n_waves, ratio)[:-1]:
         acc += f
         bounds.append(acc)
     for r in range(world_size):

@@ -519,3 +519,26 @@ def test_default_wave_counts():
         assert opt._n_waves(shapes["c2"], world, cuda, 5) == 3
     assert opt._n_waves(shapes["c2"][:40], 8, cuda, 5) == 1  # 5 matrices per rank
     assert opt._n_waves(shapes["c2"], 8, torch.device("cpu"), 5) == 1
+
+
+def test_wave_ratio_shapes_the_waves():
+    """allgather_wave_ratio: 1.0 cuts a rank's matrices into waves of equal FLOP
+    shares, a ratio below 1 front-loads them; every rank gets the same count."""
+    from opendm_b200.sharding import assign_owners, assign_waves, ns_cost, wave_fractions
+
+    assert wave_fractions(4, 1.0) == [0.25] * 4
+    f = wave_fractions(3, 0.5)
+    assert abs(sum(f) - 1.0) < 1e-12 and f[0] > f[1] > f[2]
+    shapes = [(512, 512)] * 48
+    owners = assign_owners(shapes, 2)
+    for ratio in (0.5, 1.0, 1.5):
+        waves = assign_waves(shapes, owners, 2, 4, ratio=ratio)
+        for r in range(2):
+            mine = [w for w, o in zip(waves, owners) if o == r]
+            counts = [mine.count(w) for w in range(4)]
+            assert sum(counts) == len(mine) and all(c > 0 for c in counts), (ratio, counts)
+            if ratio == 1.0:
+                assert max(counts) - min(counts) <= 1, counts
+            if ratio == 0.5:
+                assert counts[0] > counts[-1], counts
+    assert ns_cost((512, 512)) > 0
