@@ -182,6 +182,9 @@ def _flat_worker(rank, port, outdir):
             kinds = [p.kind for p in opt._get_muon_shard_plans(opt.param_groups[1])]
             runs[name] = {"params": [p.detach().reshape(-1).cpu() for p in model.parameters()], "kinds": kinds}
         result.update(runs=runs, slices=slices)
+        if rank == 0:  # the inputs, for the oracle run in the parent
+            result["host"] = {"full": [t.float().cpu() for t in full],
+                              "grads": [[t.float().cpu() for t in gs] for gs in grads]}
         dist.barrier()
         dist.destroy_process_group()
     except Exception as exc:  # reported to the parent
@@ -213,3 +216,20 @@ def test_two_gpu_flat_shards_owner_ns_equals_unsharded(tmp_path):
             for i, (got, want) in enumerate(zip(r["runs"][name]["params"], r["runs"]["full"]["params"])):
                 a, b = r["slices"][i]
                 assert torch.equal(got, want[a:b]), (r["rank"], name, i)
+    # and the unsharded run (which both shard schedules equal bit for bit) is
+    # the reference's step: the CPU oracle on the same inputs, bf16 parameters
+    # within the bf16 floor over two steps (tests/test_gpu_optimizer.py)
+    import numpy as np
+
+    from oracle import muon_oracle as O
+
+    host = res[0]["host"]
+    ref = O.OracleMuonAdamW(lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01)
+    want = {str(i): host["full"][i].numpy().copy() for i in range(len(MUON))}
+    for s in range(STEPS):
+        ref.step(want, {str(i): host["grads"][s][i].numpy() for i in range(len(MUON))}, {}, {},
+                 param_dtype="bfloat16", device_semantics="cuda")
+    for i, shape in enumerate(MUON):
+        got = res[0]["runs"]["full"]["params"][i].float().numpy().reshape(shape)
+        err = O.rel_frobenius(got, want[str(i)])
+        assert err < 2e-3 * np.sqrt(STEPS), (i, shape, err)
