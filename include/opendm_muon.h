@@ -89,8 +89,8 @@ int muon_selftest_bounded_wait(int* err_dev, int timeout_us, void* stream);
  *   scale = 1 / max(norm, eps)      otherwise.
  * d is written rounded to `dir_dtype` into `direction` with row stride `ld`
  * (the matrix keeps the parameter's layout): MUON_BF16 / MUON_TF32 write the
- * Newton-Schulz operand directly; MUON_F32 writes d unrounded, for
- * muon_convert_f16 to normalise and round afterwards.
+ * Newton-Schulz operand directly; MUON_F32 writes d unrounded (fp32
+ * directions of FSDP shards, exchanged before the owner orthogonalises).
  */
 typedef struct muon_momentum_seg {
   const void* grad;    /* [rows*cols] of grad_dtype, or NULL for an absent grad */
@@ -133,58 +133,11 @@ int muon_momentum_single_noalloc(const void* grad, float* exp_avg, void* directi
                                  float eps, float* scale_out, void* stream);
 
 /* ------------------------------------------- fp16 operand preparation
- * fp16 has tf32's 11-bit significand but a narrow exponent range, so the
- * fp16 Newton-Schulz input is written after normalisation:
- *   dst = 0                                  if scales[scale_index] == 0
- *   dst = fp16(src * (scales[scale_index] * mul))   otherwise,
- * with mul = muon_ns_operand_scale(rows, cols, 0, MUON_F16), a power of two
- * that brings the entries of the unit-norm matrix to magnitude ~1.
- */
-typedef struct muon_convert_seg {
-  const float* src;    /* [rows][ld_src] fp32 direction (muon_momentum, MUON_F32) */
-  void* dst;           /* [rows][ld_dst] fp16 (a class's x0 slot) */
-  int64_t rows;
-  int64_t cols;
-  int64_t ld_src;
-  int64_t ld_dst;
-  int64_t chunk_begin; /* prefix sum of muon_momentum_chunks() */
-  float mul;
-  int32_t scale_index;
-} muon_convert_seg;
-
-int muon_convert_f16(const muon_convert_seg* segs_dev, int n_segs, int64_t total_chunks,
-                     const float* scales_dev, void* stream);
-
-/* fp16 operands without the fp32 direction: after muon_momentum ran with
- * direction NULL (momentum and norm only), rebuild each direction from the
- * gradient and the advanced exp_avg with the same operations (d = g +
- * momentum * exp_avg when nesterov, else exp_avg; the gradient multiplied by
- * *grad_scale_dev when it is not NULL, as muon_momentum_scaled does),
- * normalise it with scales[scale_index] and scale it by `mul` into fp16, as
- * muon_convert_f16 does. Bit-identical to muon_momentum (MUON_F32 direction)
- * followed by muon_convert_f16, without the fp32 copy (4 bytes per element of
- * memory and 8 of traffic fewer, 2 more read back from the gradient). */
-typedef struct muon_direction_f16_seg {
-  const void* grad;     /* [rows * cols] of the launch's grad dtype, or NULL */
-  const float* exp_avg; /* [rows * cols], already advanced this step */
-  void* dst;            /* [rows][ld_dst] fp16 */
-  int64_t rows;
-  int64_t cols;
-  int64_t ld_dst;
-  int64_t chunk_begin;  /* prefix sum of muon_momentum_chunks() */
-  float mul;
-  int32_t scale_index;
-} muon_direction_f16_seg;
-
-int muon_direction_f16(const muon_direction_f16_seg* segs_dev, int n_segs, int64_t total_chunks, int grad_dtype,
-                       float momentum, int nesterov, const float* scales_dev, const float* grad_scale_dev,
-                       void* stream);
-
-/* fp16 operands in the momentum pass itself. Replaces muon_adamw.py:381-394
+ * fp16 operands in the momentum pass itself. Replaces muon_adamw.py:381-394
  * (momentum + Nesterov) and the normalisation of :118-121, like muon_momentum,
  * but also writes the fp16 Newton-Schulz input, so each element is read and
- * written once (12 bytes per element for bf16 gradients, against 18 for
- * muon_momentum followed by muon_direction_f16):
+ * written once (12 bytes per element for bf16 gradients; a momentum pass
+ * followed by a second pass writing the operand would take 18):
  *   x0 = fp16(d * p),  p = pscale[scale_index], a power of two
  * chosen from the previous step's norm of the same matrix, and
  *   scales[scale_index] = (1 / max(||d||, eps)) * mul / p
@@ -251,8 +204,8 @@ float muon_ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dt
  * Each class owns caller-provided buffers of op dtype (MUON_BF16 and
  * MUON_F16: 2 bytes, MUON_TF32: 4 bytes per element):
  *   x0, x1:     [count][rows][ld_x]  (x0 holds the direction written by
- *               muon_momentum, or by muon_convert_f16 for MUON_F16, which
- *               stores it normalised; x1 is the ping-pong partner)
+ *               muon_momentum, or by muon_momentum_f16 for the fp16
+ *               types; x1 is the ping-pong partner)
  *   ap, bp, mm: [count][m][ld_m]     m = min(rows, cols)
  *   aa, pa, qa, qb: [count][m][ld_m] (MUON_NS_GRAM only; NULL otherwise)
  * ld_x and ld_m must make rows 16-byte aligned (multiple of 8 for 2-byte,
@@ -269,9 +222,8 @@ float muon_ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dt
 /* muon_ns_class.flags: with MUON_F16 (or MUON_F16X3) operands, x0 holds the direction times
  * an arbitrary per-matrix factor and scales[i] turns it into the normalised
  * input times muon_ns_operand_scale(rows, cols, 0, MUON_F16) (what
- * muon_momentum_f16 writes). Without it, fp16 x0 holds that scaled,
- * normalised input itself (muon_convert_f16, muon_direction_f16) and scales
- * is not read. tf32 and bf16 classes always apply scales (x0 holds the raw
+ * muon_momentum_f16 writes). Without it, fp16 x0 must hold that scaled,
+ * normalised input itself and scales is not read. tf32 and bf16 classes always apply scales (x0 holds the raw
  * direction). */
 #define MUON_NS_INPUT_SCALED 1
 

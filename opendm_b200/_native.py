@@ -45,20 +45,6 @@ class MomentumSeg(Structure):
     ]
 
 
-class ConvertSeg(Structure):
-    _fields_ = [
-        ("src", c_void_p),
-        ("dst", c_void_p),
-        ("rows", c_int64),
-        ("cols", c_int64),
-        ("ld_src", c_int64),
-        ("ld_dst", c_int64),
-        ("chunk_begin", c_int64),
-        ("mul", c_float),
-        ("scale_index", c_int32),
-    ]
-
-
 class NsClass(Structure):
     _fields_ = [
         ("rows", c_int32),
@@ -89,11 +75,6 @@ MUON_MAX_FLAGS = 32
 
 class FlagList(Structure):
     _fields_ = [("ptr", c_void_p * MUON_MAX_FLAGS), ("n", c_int32)]
-
-
-class DirectionF16Seg(Structure):
-    _fields_ = [("grad", c_void_p), ("exp_avg", c_void_p), ("dst", c_void_p), ("rows", c_int64), ("cols", c_int64),
-                ("ld_dst", c_int64), ("chunk_begin", c_int64), ("mul", c_float), ("scale_index", c_int32)]
 
 
 class MomentumF16Seg(Structure):
@@ -147,7 +128,6 @@ SIGNATURES = {
                               c_void_p, c_void_p]),
     "muon_momentum_single_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_int,
                                              c_float, c_int, c_float, c_void_p, c_void_p]),
-    "muon_convert_f16": (c_int, [c_void_p, c_int, c_int64, c_void_p, c_void_p]),
     "muon_ns_operand_scale": (c_float, [c_int32, c_int32, c_int, c_int]),
     "muon_ns_plan_create": (c_int, [POINTER(NsClass), c_int, c_int, c_int, POINTER(c_void_p)]),
     "muon_ns_plan_run": (c_int, [c_void_p, c_void_p, c_void_p]),
@@ -157,7 +137,6 @@ SIGNATURES = {
     "muon_ns_plan_set_sm_limit": (c_int, [c_void_p, c_int]),
     "muon_flags_set": (c_int, [POINTER(FlagList), c_uint32, c_void_p]),
     "muon_norm_chunks": (c_int64, [c_int64]),
-    "muon_direction_f16": (c_int, [c_void_p, c_int, c_int64, c_int, c_float, c_int, c_void_p, c_void_p, c_void_p]),
     "muon_momentum_f16": (c_int, [c_void_p, c_int, c_int64, c_int, c_float, c_int, c_float, c_void_p, c_void_p,
                                   c_void_p, c_void_p, c_void_p, c_void_p]),
     "muon_clip_grad_norm": (c_int, [c_void_p, c_int, c_int64, c_float, c_void_p, c_void_p, c_void_p]),

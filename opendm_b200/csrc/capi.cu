@@ -112,11 +112,6 @@ int muon_momentum_single_noalloc(const void* grad, float* exp_avg, void* directi
                                               momentum, nesterov, eps, scale_out, static_cast<cudaStream_t>(stream));
 }
 
-int muon_convert_f16(const muon_convert_seg* segs_dev, int n_segs, int64_t total_chunks, const float* scales_dev,
-                     void* stream) {
-  return muon::launch_convert(segs_dev, n_segs, total_chunks, scales_dev, static_cast<cudaStream_t>(stream));
-}
-
 float muon_ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dtype) {
   return muon::ns_operand_scale(rows, cols, iteration, op_dtype);
 }
@@ -177,13 +172,6 @@ int muon_adamw_scaled(const muon_adamw_seg* segs_dev, int n_segs, int64_t total_
 }
 
 int64_t muon_norm_chunks(int64_t numel) { return muon::norm_chunks(numel); }
-
-int muon_direction_f16(const muon_direction_f16_seg* segs_dev, int n_segs, int64_t total_chunks, int grad_dtype,
-                       float momentum, int nesterov, const float* scales_dev, const float* grad_scale_dev,
-                       void* stream) {
-  return muon::launch_direction_f16(segs_dev, n_segs, total_chunks, grad_dtype, momentum, nesterov, scales_dev,
-                                    grad_scale_dev, static_cast<cudaStream_t>(stream));
-}
 
 int muon_momentum_f16(const muon_momentum_f16_seg* segs_dev, int n_segs, int64_t total_chunks, int grad_dtype,
                       float momentum, int nesterov, float eps, float* partials_dev, float* pscale_dev,

@@ -46,13 +46,7 @@ int launch_flags_set(const muon_flag_list* list, uint32_t value, cudaStream_t st
 int launch_flags_wait(const muon_flag_list* list, uint32_t value, int64_t timeout_us, int* err_dev,
                       cudaStream_t stream);
 
-int launch_direction_f16(const muon_direction_f16_seg* segs_dev, int n_segs, int64_t total_chunks, int grad_dtype,
-                         float momentum, int nesterov, const float* scales_dev, const float* grad_scale,
-                         cudaStream_t stream);
 int launch_momentum_f16(const muon_momentum_f16_seg* segs_dev, int n_segs, int64_t total_chunks, int grad_dtype,
                         float momentum, int nesterov, float eps, float* partials_dev, float* pscale_dev,
                         float* scales_dev, int* redo_dev, const float* grad_scale, cudaStream_t stream);
-int launch_convert(const muon_convert_seg* segs_dev, int n_segs, int64_t total_chunks,
-                   const float* scales_dev, cudaStream_t stream);
-
 }  // namespace muon

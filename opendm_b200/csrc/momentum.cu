@@ -237,150 +237,6 @@ int launch_momentum(const muon_momentum_seg* segs_dev, int n_segs, int64_t total
   return MUON_OK;
 }
 
-// fp16 Newton-Schulz input: normalise, scale by a power of two, round.
-__device__ __forceinline__ int find_convert_segment(const muon_convert_seg* segs, int n_segs, int64_t chunk) {
-  int lo = 0, hi = n_segs - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (segs[mid].chunk_begin <= chunk)
-      lo = mid;
-    else
-      hi = mid - 1;
-  }
-  return lo;
-}
-
-__global__ void __launch_bounds__(MOM_THREADS) convert_f16_kernel(const muon_convert_seg* __restrict__ segs,
-                                                                  int n_segs, const float* __restrict__ scales) {
-  const int64_t chunk = blockIdx.x;
-  const muon_convert_seg sg = segs[find_convert_segment(segs, n_segs, chunk)];
-  const int64_t numel = sg.rows * sg.cols;
-  const int64_t e0 = (chunk - sg.chunk_begin) * MOM_CHUNK;
-  const int64_t e1 = min(e0 + MOM_CHUNK, numel);
-  const float s = scales[sg.scale_index];
-  const bool zero = !(s != 0.f);
-  const float f = s * sg.mul;
-  __half* dst = reinterpret_cast<__half*>(sg.dst);
-  const bool vec_ok = sg.ld_src == sg.cols && sg.ld_dst == sg.cols && (numel % 8) == 0 &&
-                      ((reinterpret_cast<uintptr_t>(sg.src) | reinterpret_cast<uintptr_t>(sg.dst)) & 15u) == 0;
-  if (vec_ok) {
-    for (int it = 0; it < MOM_ITERS; ++it) {
-      const int64_t e = e0 + (int64_t(it) * MOM_THREADS + threadIdx.x) * MOM_VEC;
-      if (e >= e1) break;
-      const float4* sp = reinterpret_cast<const float4*>(sg.src + e);
-      const float4 a = __ldg(sp), b = __ldg(sp + 1);
-      uint4 raw;
-      __half2* h = reinterpret_cast<__half2*>(&raw);
-      if (zero) {
-        h[0] = h[1] = h[2] = h[3] = __floats2half2_rn(0.f, 0.f);
-      } else {
-        h[0] = __floats2half2_rn(a.x * f, a.y * f);
-        h[1] = __floats2half2_rn(a.z * f, a.w * f);
-        h[2] = __floats2half2_rn(b.x * f, b.y * f);
-        h[3] = __floats2half2_rn(b.z * f, b.w * f);
-      }
-      *reinterpret_cast<uint4*>(dst + e) = raw;
-    }
-  } else {
-    for (int64_t e = e0 + threadIdx.x; e < e1; e += MOM_THREADS) {
-      const int64_t r = e / sg.cols, c = e - r * sg.cols;
-      const float v = zero ? 0.f : sg.src[r * sg.ld_src + c] * f;
-      dst[r * sg.ld_dst + c] = __float2half_rn(v);
-    }
-  }
-}
-
-// fp16 Newton-Schulz input straight from the gradient and the momentum the
-// momentum pass has just advanced, with no fp32 staging copy of the direction:
-// d = g + mu * exp_avg (Nesterov) or exp_avg is recomputed exactly as that
-// pass computed it (same operations, same clip coefficient on the gradient),
-// then normalised and scaled by a power of two as convert_f16_kernel does.
-template <int kGradDt>
-__global__ void __launch_bounds__(MOM_THREADS) direction_f16_kernel(const muon_direction_f16_seg* __restrict__ segs,
-                                                                    int n_segs, float mu, int nesterov,
-                                                                    const float* __restrict__ scales,
-                                                                    const float* __restrict__ grad_scale) {
-  const int64_t chunk = blockIdx.x;
-  int lo = 0, hi = n_segs - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (segs[mid].chunk_begin <= chunk)
-      lo = mid;
-    else
-      hi = mid - 1;
-  }
-  const muon_direction_f16_seg sg = segs[lo];
-  const int64_t numel = sg.rows * sg.cols;
-  const int64_t e0 = (chunk - sg.chunk_begin) * MOM_CHUNK;
-  const int64_t e1 = min(e0 + MOM_CHUNK, numel);
-  const float s = scales[sg.scale_index];
-  const bool zero = !(s != 0.f);
-  const float f = s * sg.mul;
-  const bool nest = nesterov != 0;
-  const bool clip = grad_scale != nullptr && sg.grad != nullptr;
-  const float coef = clip ? *grad_scale : 1.f;
-  __half* dst = reinterpret_cast<__half*>(sg.dst);
-  const bool vec_ok = sg.ld_dst == sg.cols && (numel % 8) == 0 &&
-                      ((reinterpret_cast<uintptr_t>(sg.grad) | reinterpret_cast<uintptr_t>(sg.exp_avg) |
-                        reinterpret_cast<uintptr_t>(sg.dst)) & 15u) == 0;
-  if (vec_ok) {
-    for (int it = 0; it < MOM_ITERS; ++it) {
-      const int64_t e = e0 + (int64_t(it) * MOM_THREADS + threadIdx.x) * MOM_VEC;
-      if (e >= e1) break;
-      float g[8];
-      load_grad8<kGradDt, MUON_F16>(sg.grad, e, g);
-      const float4* mp = reinterpret_cast<const float4*>(sg.exp_avg + e);
-      const float4 m0 = __ldg(mp), m1 = __ldg(mp + 1);
-      const float m[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
-      float x[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float gi = clip ? clip_grad<kGradDt>(g[i], coef) : g[i];
-        const float d = nest ? __fmaf_rn(mu, m[i], gi) : m[i];
-        x[i] = zero ? 0.f : d * f;
-      }
-      uint4 raw;
-      __half2* h = reinterpret_cast<__half2*>(&raw);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
-      *reinterpret_cast<uint4*>(dst + e) = raw;
-    }
-  } else {
-    for (int64_t e = e0 + threadIdx.x; e < e1; e += MOM_THREADS) {
-      float g = 0.f;
-      if (sg.grad) {
-        if constexpr (kGradDt == MUON_BF16)
-          g = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sg.grad)[e]);
-        else
-          g = reinterpret_cast<const float*>(sg.grad)[e];
-        if (clip) g = clip_grad<kGradDt>(g, coef);
-      }
-      const float m = sg.exp_avg[e];
-      const float d = nest ? __fmaf_rn(mu, m, g) : m;
-      const int64_t r = e / sg.cols, c = e - r * sg.cols;
-      dst[r * sg.ld_dst + c] = __float2half_rn(zero ? 0.f : d * f);
-    }
-  }
-}
-
-int launch_direction_f16(const muon_direction_f16_seg* segs_dev, int n_segs, int64_t total_chunks, int grad_dtype,
-                         float momentum, int nesterov, const float* scales_dev, const float* grad_scale,
-                         cudaStream_t stream) {
-  if (n_segs <= 0 || total_chunks <= 0) return MUON_OK;
-  if (!segs_dev || !scales_dev) return set_error(MUON_ERR_ARG, "null direction segment table or scales");
-  if (grad_dtype != MUON_BF16 && grad_dtype != MUON_F32)
-    return set_error(MUON_ERR_ARG, "grad_dtype must be MUON_BF16 or MUON_F32");
-  if (total_chunks > 0x7fffffffLL) return set_error(MUON_ERR_ARG, "too many direction chunks");
-  const dim3 grid(static_cast<unsigned>(total_chunks));
-  if (grad_dtype == MUON_BF16)
-    direction_f16_kernel<MUON_BF16><<<grid, MOM_THREADS, 0, stream>>>(segs_dev, n_segs, momentum, nesterov,
-                                                                      scales_dev, grad_scale);
-  else
-    direction_f16_kernel<MUON_F32><<<grid, MOM_THREADS, 0, stream>>>(segs_dev, n_segs, momentum, nesterov,
-                                                                     scales_dev, grad_scale);
-  return check_cuda(cudaGetLastError(), "direction_f16 launch");
-}
-
 // ===========================================================================
 // fp16 Newton-Schulz input in the momentum pass itself (muon_momentum_f16).
 //
@@ -673,17 +529,6 @@ int launch_momentum_f16(const muon_momentum_f16_seg* segs_dev, int n_segs, int64
           segs_dev, n_segs, total_chunks, momentum, nesterov, pscale_dev, redo_dev, grad_scale);
     if (check_cuda(cudaGetLastError(), "momentum_f16 fix-up launch")) return MUON_ERR_CUDA;
   }
-  return MUON_OK;
-}
-
-int launch_convert(const muon_convert_seg* segs_dev, int n_segs, int64_t total_chunks, const float* scales_dev,
-                   cudaStream_t stream) {
-  if (n_segs <= 0 || total_chunks <= 0) return MUON_OK;
-  if (!segs_dev || !scales_dev) return set_error(MUON_ERR_ARG, "null convert buffer");
-  if (total_chunks > 0x7fffffffLL) return set_error(MUON_ERR_ARG, "too many convert chunks");
-  convert_f16_kernel<<<static_cast<unsigned>(total_chunks), MOM_THREADS, 0, stream>>>(segs_dev, n_segs,
-                                                                                       scales_dev);
-  if (check_cuda(cudaGetLastError(), "convert launch")) return MUON_ERR_CUDA;
   return MUON_OK;
 }
 

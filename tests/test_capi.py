@@ -84,7 +84,6 @@ def test_argument_validation_reports_errors(lib):
     assert lib.muon_ns_plan_create(ctypes.byref(cls), 1, N.MUON_F16, 5, ctypes.byref(plan)) == N.MUON_ERR_ARG
     assert lib.muon_momentum(None, 2, 4, N.MUON_BF16, N.MUON_TF32, 0.9, 1, 1e-7, None, None, None) == N.MUON_ERR_ARG
     assert lib.muon_apply_update(None, 2, 4, 1.0, None) == N.MUON_ERR_ARG
-    assert lib.muon_convert_f16(None, 2, 4, None, None) == N.MUON_ERR_ARG
     # cross-GPU flags: list size, null and misaligned pointers are rejected before any launch
     fl = N.FlagList()
     fl.n = N.MUON_MAX_FLAGS + 1
