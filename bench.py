@@ -127,10 +127,11 @@ def ns_flops(shape, steps=NS_STEPS):
 
 GRAM_SEGMENT = 3  # iterations between restarts of the gram-form Newton-Schulz
 
-# DRAM bytes (read + write) per ns_gemm launch, from one ncu capture
-# (dram__bytes_read.sum + dram__bytes_write.sum) of the c2s case, 0.668 GB per
-# launch, scaled by the Muon element count (c2 has 7x c2s's matrices, same classes).
-NS_TRAFFIC_PER_LAUNCH = {"c2": 7 * 0.668e9, "c2s": 0.668e9}
+# DRAM bytes (read + write) per ns_gemm launch: ncu's dram__bytes_read.sum +
+# dram__bytes_write.sum over the 17 ns_gemm launches of one captured step of
+# each configuration on one GPU (c2: 57.55 GB read + 34.43 GB written; c2s:
+# 7.05 GB + 4.34 GB), divided by 17.
+NS_TRAFFIC_PER_LAUNCH = {"c2": 91.98e9 / 17, "c2s": 11.39e9 / 17}
 
 
 def ns_executed_flops(shape, steps=NS_STEPS, algo="standard"):
@@ -617,9 +618,9 @@ def run_ours(args):
                          "frac_of_tf32_peak": round(ns_tflops / (peak / 2), 4) if args.precision == "tf32" else None,
                          "mma_kind": "kind::tf32" if args.precision == "tf32" else "kind::f16",
                          "traffic": (NS_TRAFFIC_PER_LAUNCH[cfg] if cfg in NS_TRAFFIC_PER_LAUNCH and world == 1
-                                     else None),
-                         "traffic_unit": "bytes per ns_gemm launch: modelled, the ncu DRAM bytes of a c2s capture "
-                                         "scaled by element count (not a counter read on this configuration)",
+                                     and args.precision == "fp16" else None),
+                         "traffic_unit": "bytes per ns_gemm launch: ncu dram__bytes_read.sum + dram__bytes_write.sum, "
+                                         "mean over the 17 launches of one captured step of this configuration",
                          "ns_ms": round(ns_ms, 3)},
             "elementwise": {"momentum_ms": round(mom_ms, 3), "momentum_gbs": round(mom_gbs, 1),
                             "momentum_bytes_per_element": mom_bytes_per_el,
