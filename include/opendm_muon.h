@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define MUON_ABI_VERSION 3
+#define MUON_ABI_VERSION 4
 
 enum muon_status {
   MUON_OK = 0,
@@ -193,12 +193,14 @@ float muon_ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dt
  *   MUON_NS_GRAM      the iteration on the m x m gram matrix A = X X^T: each
  *                     P_j = a + b A_j + c A_j^2 is a polynomial of A_j, so
  *                     A_{j+1} = P_j (P_j A_j) and X_k = (P_{k-1} ... P_s) X_s;
- *                     the product is applied to X once per 3 iterations, after
- *                     which A is recomputed from X (a restart that keeps the
- *                     rounding of the m x m products from growing). For
- *                     n >= ~1.5 m it executes about 1.7x fewer FLOPs; it needs
- *                     MUON_F16 or MUON_TF32 operands. muon_ns_choose_algo
- *                     returns the cheaper one for a shape.
+ *                     the product is applied to X once per segment of
+ *                     muon_ns_gram_segment() = 3 iterations, after which A is
+ *                     recomputed from X (a restart that keeps the rounding of
+ *                     the m x m products from growing; split fp16 operands
+ *                     need it too, since fp32 accumulation then dominates).
+ *                     For n >= ~1.5 m it executes about 1.7x fewer FLOPs; it
+ *                     needs MUON_F16, MUON_F16X3 or MUON_TF32 operands.
+ *                     muon_ns_choose_algo returns the cheaper one for a shape.
  * Both give the same result up to operand rounding.
  *
  * Each class owns caller-provided buffers of op dtype (MUON_BF16 and
@@ -282,6 +284,14 @@ int64_t muon_ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count,
 /* The algorithm with fewer executed FLOPs for a rows x cols class iterated
  * `steps` times (MUON_NS_STANDARD for MUON_BF16 operands or steps < 3). */
 int muon_ns_choose_algo(int32_t rows, int32_t cols, int op_dtype, int steps);
+
+/* Iterations per MUON_NS_GRAM segment of the reference's 5-step loop
+ * (muon_adamw.py:124-127; the product of the segment's P is applied to X,
+ * and A recomputed, at the end of each): 3 for MUON_F16, MUON_F16X3 and
+ * MUON_TF32; 0 for an op_dtype without the gram form. Segments alternate the
+ * x0 / x1 buffers, so a caller that reuses the X buffer the last apply does
+ * not read (as U's destination) needs it. */
+int muon_ns_gram_segment(int op_dtype);
 
 /* Fill the buffer pointers and ld_x/ld_m of `cls` (rows, cols, count and
  * algo set by the caller) from one workspace buffer `base` of

@@ -30,7 +30,7 @@ MUON_NS_STANDARD = 0
 MUON_NS_GRAM = 1
 MUON_NS_INPUT_SCALED = 1  # muon_ns_class.flags
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 
 class MomentumSeg(Structure):
@@ -147,6 +147,7 @@ SIGNATURES = {
     "muon_flags_wait": (c_int, [POINTER(FlagList), c_uint32, c_int64, c_void_p, c_void_p]),
     "muon_ns_class_workspace_bytes": (c_int64, [c_int32, c_int32, c_int32, c_int, c_int]),
     "muon_ns_choose_algo": (c_int, [c_int32, c_int32, c_int, c_int]),
+    "muon_ns_gram_segment": (c_int, [c_int]),
     "muon_ns_class_layout": (c_int, [POINTER(NsClass), c_void_p, c_int]),
     "muon_adamw_chunks": (c_int64, [c_int64]),
     "muon_adamw": (c_int, [c_void_p, c_int, c_int64, c_double, c_double, c_float, c_float, c_void_p]),

@@ -153,6 +153,8 @@ int muon_ns_choose_algo(int32_t rows, int32_t cols, int op_dtype, int steps) {
   return muon::ns_choose_algo(rows, cols, op_dtype, steps);
 }
 
+int muon_ns_gram_segment(int op_dtype) { return muon::ns_gram_segment(op_dtype); }
+
 int muon_ns_class_layout(muon_ns_class* cls, void* base, int op_dtype) {
   return muon::ns_class_layout(cls, base, op_dtype);
 }

@@ -39,6 +39,7 @@ int ns_plan_launches(const muon_ns_plan* plan);
 int ns_plan_set_sm_limit(muon_ns_plan* plan, int sms);
 int64_t ns_class_workspace_bytes(int32_t rows, int32_t cols, int32_t count, int op_dtype, int algo);
 int ns_choose_algo(int32_t rows, int32_t cols, int op_dtype, int steps);
+int ns_gram_segment(int op_dtype);
 int ns_class_layout(muon_ns_class* cls, void* base, int op_dtype);
 float ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dtype);
 

@@ -730,6 +730,8 @@ static double p2_near(double x) { return std::ldexp(1.0, static_cast<int>(std::l
 static float gram_scale_a(int m, int op) { return op_is_f16(op) ? float(p2_near(m / 4.0)) : 1.0f; }
 static float gram_scale_q(int m, int op) { return op_is_f16(op) ? float(p2_near(m / 64.0)) : 1.0f; }
 
+int ns_gram_segment(int op_dtype) { return op_is_f16(op_dtype) || op_dtype == MUON_TF32 ? kGramSegment : 0; }
+
 static double exec_flops(int rows, int cols, int steps, int algo) {
   const double m = std::min(rows, cols), n = std::max(rows, cols);
   auto kp = [](double k) { return std::ceil(k / 64.0) * 64.0; };

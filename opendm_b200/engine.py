@@ -144,7 +144,8 @@ class _ClassState:
         """0 or 1: the X buffer (x0, x1) the last Newton-Schulz apply reads;
         the other one is free when U is written."""
         if int(self.cls.algo) == N.MUON_NS_GRAM:
-            return ((steps - 1) // 3) % 2  # segments of 3 iterations alternate x0, x1
+            # gram segments alternate x0, x1
+            return ((steps - 1) // int(N.lib().muon_ns_gram_segment(self.op_dtype))) % 2
         return (steps - 1) % 2
 
     def x0_view(self, slot: int, lo: bool = False) -> torch.Tensor:

@@ -55,6 +55,10 @@ def test_host_only_entry_points(lib):
     assert lib.muon_ns_choose_algo(2048, 2048, N.MUON_F16, 5) == std
     assert lib.muon_ns_choose_algo(2048, 8192, N.MUON_BF16, 5) == std
     assert lib.muon_ns_choose_algo(2048, 8192, N.MUON_F16, 2) == std
+    # gram-form segment length (iterations between re-formings of X), per operand type
+    for op in (N.MUON_F16, N.MUON_F16X3, N.MUON_TF32):
+        assert lib.muon_ns_gram_segment(op) == 3
+    assert lib.muon_ns_gram_segment(N.MUON_BF16) == 0 and lib.muon_ns_gram_segment(N.MUON_F32) == 0
     # fp16 operand scales: powers of two bringing entries to magnitude ~1
     assert lib.muon_ns_operand_scale(2048, 8192, 0, N.MUON_F16) == 4096.0
     assert lib.muon_ns_operand_scale(2048, 8192, 1, N.MUON_F16) == 128.0
