@@ -22,7 +22,9 @@
 //   warp 1      TMEM allocation (both CTAs); single-thread MMA issuer (leader)
 //   warps 2..5  epilogue (both CTAs): tcgen05.ld -> registers -> swizzled
 //               shared-memory staging -> one TMA tensor store per 32 x 32
-//               chunk (+ a transposed mirror store for symmetric C)
+//               chunk; a symmetric C stores its upper 256 x 256 blocks only,
+//               and a later product reads a block below the diagonal as
+//               the MN-major transpose of the stored block
 // Accumulators: two 128 x 256 fp32 buffers per CTA in TMEM (all 512 columns),
 // so the epilogue of tile i overlaps the main loop of tile i+1. Each CTA
 // loads its own operand halves with plain (single-destination) TMA loads.
@@ -71,17 +73,15 @@ struct GemmProblem {
   int tiles_per_mat;
   int tile_begin;
   int a_mn, b_mn;  // operand majorness: 0 = K-major, 1 = MN-major
-  int symmetric;   // compute upper-triangle tiles and mirror them
+  int a_sym, b_sym;  // operand is a symmetric m x m matrix stored as its upper 256 x 256 blocks
+  int symmetric;   // output is symmetric: only its upper 256 x 256 blocks are computed and stored
   int epi;
   int first;       // apply the per-matrix input scale
   int split;       // operands stored as fp16 hi/lo pairs (batch slots 2g, 2g+1): K runs three times
   float mul;       // constant multiplier of the accumulator (power of two)
   float omul;      // poly: multiplier of the stored M / P (power of two)
   float omul3;     // gram: of the stored A; poly: of the stored Q (power of two)
-  void* out;
-  long long out_ld, out_bs;
-  void* out2;      // gram: B' (same geometry as out)
-  void* out3;      // optional (gram: A; poly: Q), same geometry as out
+  const void* out3;  // optional third output (gram: A; poly: Q); non-null when map_out3 is set
   const float* scale;
 };
 
@@ -91,6 +91,8 @@ struct GemmParams {
   CUtensorMap map_out[kMaxProblems];   // D (A', M, X or U): 32 x 32 store boxes
   CUtensorMap map_out2[kMaxProblems];  // gram: B'
   CUtensorMap map_out3[kMaxProblems];  // gram: A; poly: Q (only where out3 is set)
+  CUtensorMap map_at[kMaxProblems];    // a_sym: the A operand with MN-major boxes, for transposed blocks
+  CUtensorMap map_bt[kMaxProblems];    // b_sym: the same for the B operand
   GemmProblem prob[kMaxProblems];
   int n_problems;
   int total_tiles;
@@ -104,6 +106,13 @@ static_assert(sizeof(GemmParams) <= 32764, "GemmParams exceeds the kernel parame
 struct TileCoord {
   int p, g, ti, tj;
 };
+
+// Symmetric m x m operands keep only their 256 x 256 blocks on and above the
+// diagonal. The K range [k0, k0 + stage) of operand rows in block `block`
+// lies in a block below the diagonal when k0 / 256 < block; that stage reads
+// the transposed block (k0 / 256, block) instead. Both CTAs of a pair hold
+// rows of the same 256-row block, so they agree on every stage's layout.
+__device__ __forceinline__ bool below_diagonal(int sym, int block, int k0) { return sym && k0 / PAIR_M < block; }
 
 __device__ __forceinline__ TileCoord decode_tile(const GemmParams& P, int t) {
   TileCoord c;
@@ -191,24 +200,6 @@ __device__ __forceinline__ void stage_rows_32(uint8_t* buf, int lane, const uint
     st_shared_v4(base + ((k ^ sw) << 4), w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
 }
 
-// Transposed staging: element (row = lane, col = i) goes to row i, column lane.
-__device__ __forceinline__ void stage_cols_16(uint8_t* buf, int lane, const uint32_t (&w)[16]) {
-  const uint32_t base = smem_u32(buf) + (lane & 7) * 2;
-  const int unit = lane >> 3;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const uint16_t h = static_cast<uint16_t>((i & 1) ? (w[i >> 1] >> 16) : (w[i >> 1] & 0xffffu));
-    st_shared_b16(base + i * 64 + ((unit ^ ((i >> 1) & 3)) << 4), h);
-  }
-}
-
-__device__ __forceinline__ void stage_cols_32(uint8_t* buf, int lane, const uint32_t (&w)[32]) {
-  const uint32_t base = smem_u32(buf) + (lane & 3) * 4;
-  const int unit = lane >> 2;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) st_shared_b32(base + i * 128 + ((unit ^ (i & 7)) << 4), w[i]);
-}
-
 // Rounds 32 fp32 values of one row into output words.
 // kind: 0 = fp32 (raw), 1 = tf32 (rna), 2 = fp16, 3 = bf16.
 template <int kWords>
@@ -264,20 +255,14 @@ __device__ __forceinline__ void ring_store(StoreRing& ring, uint8_t* buf, const 
   ++ring.issued;
 }
 
-// Store one chunk (row-major words of this lane's row) at (x = col0, y = row0)
-// and, when `mirror`, its transpose at (x = row0, y = col0).
+// Store one chunk (row-major words of this lane's row) at (x = col0, y = row0).
 template <int kWords>
 __device__ __forceinline__ void store_chunk(StoreRing& ring, const CUtensorMap* map, int lane, const uint32_t (&w)[kWords],
-                                            int col0, int row0, int g, bool mirror) {
+                                            int col0, int row0, int g) {
   constexpr int kOutBytes = kWords == 32 ? 4 : 2;
   uint8_t* buf = ring_acquire<kOutBytes>(ring, lane);
   if constexpr (kWords == 32) stage_rows_32(buf, lane, w); else stage_rows_16(buf, lane, w);
   ring_store(ring, buf, map, lane, col0, row0, g);
-  if (mirror) {
-    buf = ring_acquire<kOutBytes>(ring, lane);
-    if constexpr (kWords == 32) stage_cols_32(buf, lane, w); else stage_cols_16(buf, lane, w);
-    ring_store(ring, buf, map, lane, row0, col0, g);
-  }
 }
 
 // Store one chunk of a Newton-Schulz operand output (32 fp32 values of this
@@ -286,16 +271,16 @@ __device__ __forceinline__ void store_chunk(StoreRing& ring, const CUtensorMap* 
 // at 2g + 1 (x - hi is exact in fp32), so hi + lo carries ~22 bits.
 template <int kOp, int kWords>
 __device__ __forceinline__ void store_operand(StoreRing& ring, const CUtensorMap* map, int lane, const float (&x)[32],
-                                              int kind, int col0, int row0, int g, bool mirror, bool split) {
+                                              int kind, int col0, int row0, int g, bool split) {
   uint32_t w[kWords];
   pack_row<kWords>(x, kind, w);
-  store_chunk<kWords>(ring, map, lane, w, col0, row0, split ? 2 * g : g, mirror);
+  store_chunk<kWords>(ring, map, lane, w, col0, row0, split ? 2 * g : g);
   if (split) {
     float lo[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) lo[i] = x[i] - round_op<kOp>(x[i]);
     pack_row<kWords>(lo, kind, w);
-    store_chunk<kWords>(ring, map, lane, w, col0, row0, 2 * g + 1, mirror);
+    store_chunk<kWords>(ring, map, lane, w, col0, row0, 2 * g + 1);
   }
 }
 
@@ -388,19 +373,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           uint8_t* sa = stage_a + stage * A_STAGE_BYTES;
           uint8_t* sb = stage_b + stage * B_STAGE_BYTES;
           const int k0 = kb * BKE;
-          if (!pr.a_mn) {
-            tma_load_3d_pair(sa, &P.map_a[tc.p], bar, k0, m0, za);
+          // A block of a symmetric operand below its diagonal is read from the
+          // stored block above it, as an MN-major tile (the MMA issuer makes the
+          // same choice for the stage's descriptors).
+          const bool a_t = below_diagonal(pr.a_sym, tc.ti, k0);
+          const bool b_t = below_diagonal(pr.b_sym, tc.tj, k0);
+          const CUtensorMap* map_a = a_t ? &P.map_at[tc.p] : &P.map_a[tc.p];
+          const CUtensorMap* map_b = b_t ? &P.map_bt[tc.p] : &P.map_b[tc.p];
+          if (!pr.a_mn && !a_t) {
+            tma_load_3d_pair(sa, map_a, bar, k0, m0, za);
           } else {
 #pragma unroll
-            for (int j = 0; j < BM / BKE; ++j)
-              tma_load_3d_pair(sa + j * BKE * 128, &P.map_a[tc.p], bar, m0 + j * BKE, k0, za);
+            for (int j = 0; j < BM / BKE; ++j) tma_load_3d_pair(sa + j * BKE * 128, map_a, bar, m0 + j * BKE, k0, za);
           }
-          if (!pr.b_mn) {
-            tma_load_3d_pair(sb, &P.map_b[tc.p], bar, k0, n0, zb);
+          if (!pr.b_mn && !b_t) {
+            tma_load_3d_pair(sb, map_b, bar, k0, n0, zb);
           } else {
 #pragma unroll
             for (int j = 0; j < BN_CTA / BKE; ++j)
-              tma_load_3d_pair(sb + j * BKE * 128, &P.map_b[tc.p], bar, n0 + j * BKE, k0, zb);
+              tma_load_3d_pair(sb + j * BKE * 128, map_b, bar, n0 + j * BKE, k0, zb);
           }
           issued[stage] = 1;
           issued_phase[stage] = phase;
@@ -425,7 +416,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       for (int t = cluster_id; ok && t < P.total_tiles; t += n_clusters, ++local_t) {
         const TileCoord tc = decode_tile(P, t);
         const GemmProblem& pr = P.prob[tc.p];
-        const int kb_count = (pr.K + BKE - 1) / BKE * (pr.split ? 3 : 1);
+        const int kb_single = (pr.K + BKE - 1) / BKE;
+        const int kb_count = kb_single * (pr.split ? 3 : 1);
         const int acc = local_t & 1;
         const uint32_t acc_phase = (local_t >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, P.err, kDevTimeoutTmemEmpty)) {
@@ -434,21 +426,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        const uint32_t idesc = make_idesc(kOp, PAIR_M, BN, pr.a_mn != 0, pr.b_mn != 0);
-        for (int kb = 0; kb < kb_count; ++kb) {
+        for (int kb = 0, kin = 0; kb < kb_count; ++kb, kin = (kin + 1 == kb_single) ? 0 : kin + 1) {
           if (!mbar_wait(&full[stage], phase, P.err, kDevTimeoutFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          // the stage's operand layouts, as the producer loaded them
+          const bool a_mn = pr.a_mn || below_diagonal(pr.a_sym, tc.ti, kin * BKE);
+          const bool b_mn = pr.b_mn || below_diagonal(pr.b_sym, tc.tj, kin * BKE);
+          const uint32_t idesc = make_idesc(kOp, PAIR_M, BN, a_mn, b_mn);
           const uint32_t a_addr = smem_u32(stage_a + stage * A_STAGE_BYTES);
           const uint32_t b_addr = smem_u32(stage_b + stage * B_STAGE_BYTES);
 #pragma unroll
           for (int kk = 0; kk < KSTEPS; ++kk) {
-            const uint64_t ad = pr.a_mn ? make_sw128_desc(a_addr + kk * UMMA_K * 128, BKE * 128, kMnSbo, kMnLayout)
-                                        : make_sw128_desc(a_addr + kk * 32, 16, 1024);
-            const uint64_t bd = pr.b_mn ? make_sw128_desc(b_addr + kk * UMMA_K * 128, BKE * 128, kMnSbo, kMnLayout)
-                                        : make_sw128_desc(b_addr + kk * 32, 16, 1024);
+            const uint64_t ad = a_mn ? make_sw128_desc(a_addr + kk * UMMA_K * 128, BKE * 128, kMnSbo, kMnLayout)
+                                     : make_sw128_desc(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = b_mn ? make_sw128_desc(b_addr + kk * UMMA_K * 128, BKE * 128, kMnSbo, kMnLayout)
+                                     : make_sw128_desc(b_addr + kk * 32, 16, 1024);
             umma_pair<kOp>(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
           // Release the stage in both CTAs once these MMAs have read it.
@@ -498,7 +493,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const int row0 = tc.ti * PAIR_M + static_cast<int>(rank) * BM + quad * 32;
       const float f = pr.first ? sc * sc * mul : mul;  // gram: s^2 * mul
       const float fa = pr.first ? sc * mul : mul;      // apply: s * mul
-      const bool sym = pr.symmetric != 0;
       const int myrow = row0 + lane;
       const CUtensorMap* map1 = &P.map_out[tc.p];
       const CUtensorMap* map2 = &P.map_out2[tc.p];
@@ -509,11 +503,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         const int col0 = tc.tj * BN + ch * 32;
         float v[32];
         tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + ch * 32, v);
+        // Symmetric outputs: the tile table holds the blocks on and above the
+        // diagonal only, each stored whole; consumers read the blocks below
+        // the diagonal transposed from them (below_diagonal).
         if (row0 >= pr.M || col0 >= pr.N) continue;
-        // Symmetric outputs: chunks below the diagonal are the mirror of chunks
-        // above it; a diagonal chunk is stored whole, without a mirror.
-        if (sym && col0 + 32 <= row0) continue;
-        const bool mirror = sym && col0 >= row0 + 32;
         float x[32];
         const bool split = pr.split != 0;
         if (pr.epi == EPI_GRAM) {
@@ -521,17 +514,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             const float m3 = pr.omul3;
 #pragma unroll
             for (int i = 0; i < 32; ++i) x[i] = zero ? 0.f : (v[i] * f) * m3;
-            store_operand<kOp, kOpWords>(ring, map3, lane, x, kOpKind, col0, row0, tc.g, mirror, split);
+            store_operand<kOp, kOpWords>(ring, map3, lane, x, kOpKind, col0, row0, tc.g, split);
           }
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const float a = zero ? 0.f : v[i] * f;
             x[i] = (myrow == col0 + i) ? a - 1.f : a;  // A'
           }
-          store_operand<kOp, kOpWords>(ring, map1, lane, x, kOpKind, col0, row0, tc.g, mirror, split);
+          store_operand<kOp, kOpWords>(ring, map1, lane, x, kOpKind, col0, row0, tc.g, split);
 #pragma unroll
           for (int i = 0; i < 32; ++i) x[i] = fmaf(P.gamma, x[i], (myrow == col0 + i) ? P.beta : 0.f);  // B'
-          store_operand<kOp, kOpWords>(ring, map2, lane, x, kOpKind, col0, row0, tc.g, mirror, split);
+          store_operand<kOp, kOpWords>(ring, map2, lane, x, kOpKind, col0, row0, tc.g, split);
         } else if (pr.epi == EPI_POLY) {
           const float pm = pr.mul, om = pr.omul;
 #pragma unroll
@@ -541,24 +534,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             const float m3 = pr.omul3;
 #pragma unroll
             for (int i = 0; i < 32; ++i) y[i] = x[i] * m3;
-            store_operand<kOp, kOpWords>(ring, map3, lane, y, kOpKind, col0, row0, tc.g, mirror, split);
+            store_operand<kOp, kOpWords>(ring, map3, lane, y, kOpKind, col0, row0, tc.g, split);
           }
 #pragma unroll
           for (int i = 0; i < 32; ++i) x[i] *= om;
-          store_operand<kOp, kOpWords>(ring, map1, lane, x, kOpKind, col0, row0, tc.g, mirror, split);
+          store_operand<kOp, kOpWords>(ring, map1, lane, x, kOpKind, col0, row0, tc.g, split);
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) x[i] = zero ? 0.f : v[i] * fa;
           if (pr.epi == EPI_APPLY) {
-            store_operand<kOp, kOpWords>(ring, map1, lane, x, kOpKind, col0, row0, tc.g, mirror, split);
+            store_operand<kOp, kOpWords>(ring, map1, lane, x, kOpKind, col0, row0, tc.g, split);
           } else if (pr.epi == EPI_U_BF16) {
             uint32_t w[16];
             pack_row<16>(x, 3, w);
-            store_chunk<16>(ring, map1, lane, w, col0, row0, tc.g, false);
+            store_chunk<16>(ring, map1, lane, w, col0, row0, tc.g);
           } else {
             uint32_t w[32];
             pack_row<32>(x, 0, w);
-            store_chunk<32>(ring, map1, lane, w, col0, row0, tc.g, false);
+            store_chunk<32>(ring, map1, lane, w, col0, row0, tc.g);
           }
         }
       }
@@ -815,6 +808,7 @@ struct OpDesc {
   long long inner = 0, outer = 0, ld = 0, bs = 0;
   int box = 0;
   bool mn = false;
+  bool sym = false;  // a symmetric m x m buffer holding its upper 256 x 256 blocks
 };
 
 struct OutDesc {
@@ -837,7 +831,8 @@ struct ClassGeom {
   bool wide;
   long long xbs, mbs;
 
-  OpDesc mat(const void* buf, int box) const { return OpDesc{buf, m, m, k->ld_m, mbs, box, false}; }
+  // m x m operands are symmetric and stored as their upper 256 x 256 blocks
+  OpDesc mat(const void* buf, int box) const { return OpDesc{buf, m, m, k->ld_m, mbs, box, false, true}; }
   OutDesc mat_out(const void* buf) const { return OutDesc{buf, op, m, m, k->ld_m, mbs}; }
   OutDesc x_out(const void* buf) const { return OutDesc{buf, op, k->cols, k->rows, k->ld_x, xbs}; }
   OutDesc u_out() const {
@@ -918,11 +913,16 @@ struct ClassGeom {
 };
 
 int encode_pending(GemmParams& L, int pi, const Pending& q, int op) {
+  const int mn_box = 128 / op_bytes(op);  // MN-major boxes: one stage of K by one swizzle atom of M
   int rc = encode_operand(&L.map_a[pi], q.a.base, op, q.a.inner, q.a.outer, q.pr.batch, q.a.ld, q.a.bs, q.a.box,
                           q.a.mn);
   if (!rc)
     rc = encode_operand(&L.map_b[pi], q.b.base, op, q.b.inner, q.b.outer, q.pr.batch, q.b.ld, q.b.bs, q.b.box,
                         q.b.mn);
+  if (!rc && q.a.sym)
+    rc = encode_operand(&L.map_at[pi], q.a.base, op, q.a.inner, q.a.outer, q.pr.batch, q.a.ld, q.a.bs, mn_box, true);
+  if (!rc && q.b.sym)
+    rc = encode_operand(&L.map_bt[pi], q.b.base, op, q.b.inner, q.b.outer, q.pr.batch, q.b.ld, q.b.bs, mn_box, true);
   if (!rc)
     rc = encode_output(&L.map_out[pi], q.o1.base, q.o1.dtype, q.o1.inner, q.o1.outer, q.pr.batch, q.o1.ld,
                        q.o1.bs);
@@ -935,11 +935,9 @@ int encode_pending(GemmParams& L, int pi, const Pending& q, int op) {
   if (rc) return rc;
   GemmProblem& pr = L.prob[pi];
   pr = q.pr;
-  pr.out = const_cast<void*>(q.o1.base);
-  pr.out_ld = q.o1.ld;
-  pr.out_bs = q.o1.bs;
-  pr.out2 = const_cast<void*>(q.o2.base);
-  pr.out3 = const_cast<void*>(q.o3.base);
+  pr.a_sym = q.a.sym ? 1 : 0;
+  pr.b_sym = q.b.sym ? 1 : 0;
+  pr.out3 = q.o3.base;
   return MUON_OK;
 }
 
