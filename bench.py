@@ -129,9 +129,9 @@ GRAM_SEGMENT = 3  # iterations between restarts of the gram-form Newton-Schulz
 
 # DRAM bytes (read + write) per ns_gemm launch: ncu's dram__bytes_read.sum +
 # dram__bytes_write.sum over the 17 ns_gemm launches of one captured step of
-# each configuration on one GPU (c2: 57.55 GB read + 34.43 GB written; c2s:
-# 7.05 GB + 4.34 GB), divided by 17.
-NS_TRAFFIC_PER_LAUNCH = {"c2": 91.98e9 / 17, "c2s": 11.39e9 / 17}
+# the configuration on one GPU (c2: 49.48 GB read + 22.82 GB written), divided
+# by 17.
+NS_TRAFFIC_PER_LAUNCH = {"c2": 72.30e9 / 17}
 
 
 def ns_executed_flops(shape, steps=NS_STEPS, algo="standard"):
