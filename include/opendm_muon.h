@@ -210,6 +210,8 @@ float muon_ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dt
  *               types; x1 is the ping-pong partner)
  *   ap, bp, mm: [count][m][ld_m]     m = min(rows, cols)
  *   aa, pa, qa, qb: [count][m][ld_m] (MUON_NS_GRAM only; NULL otherwise)
+ * The m x m buffers hold symmetric matrices as their 256 x 256 blocks on and
+ * above the diagonal; the blocks below it are never written or read.
  * ld_x and ld_m must make rows 16-byte aligned (multiple of 8 for 2-byte,
  * of 4 for 4-byte types), and every buffer must be 16-byte aligned.
  * `scales` holds the per-matrix input scale produced by muon_momentum.
