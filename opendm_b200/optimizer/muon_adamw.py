@@ -113,6 +113,13 @@ class MuonShardPlan:
     process_group: object | None = None
 
 
+def _as_matrix(t: torch.Tensor, shape) -> torch.Tensor:
+    """`t` as the [rows, cols] matrix `shape`: itself when it has that shape
+    already (a view costs microseconds per call, and most parameters need
+    none), else a view (flat FSDP storage of a whole matrix)."""
+    return t if t.shape == shape else t.view(shape)
+
+
 def _dist_ready() -> bool:
     return dist.is_available() and dist.is_initialized()
 
@@ -674,6 +681,7 @@ class MuonAdamW(torch.optim.Optimizer):
         others, partial, step_tensors = [], [], []
         partial_local: dict[int, tuple] = {}  # matrix index -> (param, grad, state, eff), local shards only
         lr_scale, moonlight = float(group["muon_lr_scale"]), float(group["muon_moonlight_coefficient"])
+        eff_of: dict = {}  # per shape: the update scale depends on the shape alone within a step
         for index, (param, shape, plan) in enumerate(zip(group["params"], group["muon_shapes"], plans, strict=True)):
             if plan.local_numel == 0:
                 continue
@@ -689,17 +697,20 @@ class MuonAdamW(torch.optim.Optimizer):
             if other and self.state_sharding:
                 continue  # the owner advances this matrix's momentum; the all-gather brings the parameter
             if other:  # momentum only
-                others.append(MatrixItem(param.data.view(shape),
-                                         grad.detach().view(shape) if grad is not None else None,
-                                         state["exp_avg"].view(shape)))
+                others.append(MatrixItem(_as_matrix(param.data, shape),
+                                         _as_matrix(grad.detach(), shape) if grad is not None else None,
+                                         _as_matrix(state["exp_avg"], shape)))
                 continue
-            eff = effective_lr(lr, lr_scale, moonlight, shape, self.scale_mode)
+            eff = eff_of.get(shape)
+            if eff is None:
+                eff = eff_of[shape] = effective_lr(lr, lr_scale, moonlight, shape, self.scale_mode)
             if plan.kind == "partial":
                 partial.append((param, grad, state, shape, plan, eff))
                 partial_local[index] = (param, grad, state, eff)
                 continue
-            item = MatrixItem(param.data.view(shape), grad.detach().view(shape) if grad is not None else None,
-                              state["exp_avg"].view(shape), eff)
+            item = MatrixItem(_as_matrix(param.data, shape),
+                              _as_matrix(grad.detach(), shape) if grad is not None else None,
+                              _as_matrix(state["exp_avg"], shape), eff)
             owned[waves[index] if waves else 0].append(item)
         if step_tensors:
             torch._foreach_add_(step_tensors, 1.0)
