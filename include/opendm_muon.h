@@ -197,7 +197,7 @@ float muon_ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dt
  *                     muon_ns_gram_segment() = 3 iterations, after which A is
  *                     recomputed from X (a restart that keeps the rounding of
  *                     the m x m products from growing; split fp16 operands
- *                     need it too, since fp32 accumulation then dominates).
+ *                     need it too: without it rank-1 inputs reach 2.5e-2).
  *                     For n >= ~1.5 m it executes about 1.7x fewer FLOPs; it
  *                     needs MUON_F16, MUON_F16X3 or MUON_TF32 operands.
  *                     muon_ns_choose_algo returns the cheaper one for a shape.
