@@ -602,7 +602,7 @@ class MuonAdamW(torch.optim.Optimizer):
         """Waves per step: one per ~1/3-1/4 of a rank's Newton-Schulz work.
         Every wave adds a full set of Newton-Schulz launches (fixed fill and
         drain time), so a fourth wave pays off only when each rank carries a
-        large share (>= 16 dense TFLOP), as at 8 ranks on BASELINE config 4."""
+        large share (>= 16 dense TFLOP), as at 8 ranks on benchmark config 4."""
         if self.allgather_waves is not None:
             return int(self.allgather_waves)
         if device.type != "cuda" or len(shapes) < 6 * world:

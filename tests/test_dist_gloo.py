@@ -18,7 +18,7 @@ import torch.multiprocessing as mp
 from oracle import muon_oracle as O
 
 WORLD = 2
-# 8 fp32 matrices + 4 fp32 vectors of length 512 on AdamW.
+# benchmark config 1: 8 fp32 matrices + 4 fp32 vectors of length 512 on AdamW.
 C1_MUON = [(512, 512), (512, 2048), (2048, 512), (1024, 1024)] * 2
 C1_ADAM = [(512,)] * 4
 SMALL_MUON = [(64, 64), (64, 160), (160, 64), (96, 96), (48, 200), (33, 70)]
@@ -203,7 +203,7 @@ def _check(res, muon, adam, steps, check_exp_avg=True):
 
 
 def test_c1_sharded_two_ranks(tmp_path):
-    """BASELINE config 1 on gloo world size 2: each matrix orthogonalised by one
+    """benchmark config 1 on gloo world size 2: each matrix orthogonalised by one
     owner, parameters all-gathered; both ranks equal the single-process oracle."""
     res = _run("replicated", C1_MUON, C1_ADAM, 2, tmp_path)
     _check(res, C1_MUON, C1_ADAM, 2)

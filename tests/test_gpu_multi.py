@@ -22,7 +22,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 WORLD = 2
-# One BASELINE config 2 decoder layer (q/o, k/v, gate/up, down) plus a tall
+# One benchmark config 2 decoder layer (q/o, k/v, gate/up, down) plus a tall
 # and a ragged matrix, bf16 parameters, and AdamW vectors.
 MUON = [(2048, 2048), (256, 2048), (256, 2048), (2048, 2048), (8192, 2048), (8192, 2048), (2048, 8192),
         (1000, 300), (72, 130)]

@@ -1,6 +1,6 @@
 """GPU parity of the drop-in MuonAdamW (through the C ABI) against the
-reference's golden outputs and the CPU oracle, at fixture
-and full BASELINE config 2 layer sizes, plus size-independent properties of
+reference's golden outputs and the CPU oracle, at fixture, benchmark config 1
+and full benchmark config 2 layer sizes, plus size-independent properties of
 the Newton-Schulz at the largest shapes.
 
 Tolerances: fp32 parameters within 1e-3 relative Frobenius of the reference
@@ -185,14 +185,14 @@ def _run_config(shapes_muon, shapes_adam, dtype, steps, seed=0, precision="fp16"
 
 
 def test_baseline_config1_single_gpu():
-    """BASELINE config 1 shapes (fp32): 512^2, 512x2048, 2048x512, 1024^2 x2 + 4 vectors; 2 steps."""
+    """benchmark config 1 shapes (fp32): 512^2, 512x2048, 2048x512, 1024^2 x2 + 4 vectors; 2 steps."""
     _run_config([(512, 512), (512, 2048), (2048, 512), (1024, 1024)] * 2, [(512,)] * 4, torch.float32, 2)
 
 
 @pytest.mark.parametrize("precision", ["fp16", "tf32"])
 @pytest.mark.parametrize("steps", [1, 2])
 def test_baseline_config2_layer_bf16(steps, precision):
-    """One full BASELINE config 2 decoder layer (bf16 params): q/o 2048^2,
+    """One full benchmark config 2 decoder layer (bf16 params): q/o 2048^2,
     k/v 256x2048, gate/up 8192x2048, down 2048x8192 + norms; 1 and 2 steps,
     both 11-bit operand precisions."""
     shapes = [(2048, 2048), (256, 2048), (256, 2048), (2048, 2048), (8192, 2048), (8192, 2048), (2048, 8192)]
@@ -200,7 +200,7 @@ def test_baseline_config2_layer_bf16(steps, precision):
 
 
 def test_parity_precision_meets_the_bf16_parameter_bar():
-    """precision="parity" (split fp16 operands): one full BASELINE config 2
+    """precision="parity" (split fp16 operands): one full benchmark config 2
     decoder layer with bf16 parameters meets the 1e-3 parameter bar itself
     after one step, and fp32 parameters (config 1 shapes) stay within it over
     two steps."""
@@ -226,7 +226,7 @@ def test_update_parity_at_config2_shapes():
 
 @pytest.mark.parametrize("shape", [(4096, 4096), (11008, 4096), (4096, 11008), (2560, 9728)])
 def test_ns_scale_invariance_and_band_at_full_size(shape):
-    """Size-independent properties at BASELINE config 4/5 shapes: scaling the
+    """Size-independent properties at benchmark config 4/5 shapes: scaling the
     input by a power of two gives a bit-identical result (every rounding is
     scale-equivariant), another scale changes it only by operand rounding, and
     the singular values stay in the quintic's band (max about 1.2; most above

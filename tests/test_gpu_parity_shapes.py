@@ -1,4 +1,4 @@
-"""GPU parity against the CPU oracle at every Muon shape class of BASELINE
+"""GPU parity against the CPU oracle at every Muon shape class of the benchmark
 configs 4 (~4B VLA: ViT, LM and action-expert matrices) and 5 (7B decoder,
 gradients with 1% heavy-tail entries N(0, 1e-1) over an N(0, 1e-3) bulk).
 

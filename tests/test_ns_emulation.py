@@ -106,7 +106,7 @@ def test_reference_tf32_recipe_has_the_bf16_parameter_floor(shape):
     """A measured point for the bf16-parameter floor: the reference's own
     MuonAdamW step (muon_adamw.py:381-414) with its Newton-Schulz in TF32 (its
     GPU recipe, dm05_exp.py:323-324; emulated here with the reference's own
-    grouping) against the same step in fp32, on BASELINE config 2 layer shapes
+    grouping) against the same step in fp32, on benchmark config 2 layer shapes
     with bf16 parameters N(0, 0.02) and gradients N(0, 1e-3). A ~1e-3 update
     difference flips a few percent of the bf16 roundings by a whole ulp, so
     the reference itself lands at ~0.85-0.95e-3 of parameter error, at the
