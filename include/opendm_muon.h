@@ -14,8 +14,10 @@
  *    muon_last_error().
  *  - Every buffer is caller-owned device memory given as a plain pointer with
  *    sizes and leading dimensions in elements. The library allocates no device
- *    memory, performs no host synchronisation and issues no collectives.
- *    (muon_ns_plan_create allocates only the host-side plan object.)
+ *    memory, performs no host synchronisation (muon_read_error, which waits
+ *    for its stream to read the error word, is the one exception) and issues
+ *    no collectives. (muon_ns_plan_create allocates only the host-side plan
+ *    object.)
  *  - `stream` is a cudaStream_t passed as void*. NULL means the legacy
  *    default stream.
  *  - Device kernels bound every spin-wait. A wait that times out writes a
@@ -198,8 +200,10 @@ float muon_ns_operand_scale(int32_t rows, int32_t cols, int iteration, int op_dt
  *                     recomputed from X (a restart that keeps the rounding of
  *                     the m x m products from growing; split fp16 operands
  *                     need it too: without it rank-1 inputs reach 2.5e-2).
- *                     For n >= ~1.5 m it executes about 1.7x fewer FLOPs; it
- *                     needs MUON_F16, MUON_F16X3 or MUON_TF32 operands.
+ *                     At 5 iterations it executes at least 10% fewer FLOPs
+ *                     for n >~ 1.4 m (1.16x fewer at n = 1.5 m, 1.6-1.85x
+ *                     at n >= 4 m); it needs MUON_F16, MUON_F16X3 or
+ *                     MUON_TF32 operands.
  *                     muon_ns_choose_algo returns the cheaper one for a shape.
  * Both give the same result up to operand rounding.
  *
@@ -258,7 +262,7 @@ typedef struct muon_ns_plan muon_ns_plan;
 
 /* Build launch descriptors (tensor maps, tile schedules) for `n_classes`
  * classes iterated `steps` times with operands of `op_dtype`
- * (MUON_TF32, MUON_F16 or MUON_BF16). The plan stores pointers, not data: buffers must
+ * (MUON_TF32, MUON_F16, MUON_F16X3 or MUON_BF16). The plan stores pointers, not data: buffers must
  * outlive it and stay at the same addresses. */
 int muon_ns_plan_create(const muon_ns_class* classes, int n_classes, int op_dtype, int steps,
                         muon_ns_plan** plan_out);
