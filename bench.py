@@ -34,9 +34,10 @@ them). `cpu_baseline` (N = 1, rank 0) is the numpy oracle
 of the reference algorithm on the host cores, timed on one matrix of every
 shape class and extrapolated by multiplicity.
 
---impl reference prints the same metric for the reference algorithm on the
-host CPU (the numpy oracle; the reference itself is PyTorch code that runs
-only from its own checkout), rank 0 only.
+--impl reference prints the same metric, with the same `config` object, for
+the reference algorithm on the host CPU (the numpy oracle; the reference itself
+is PyTorch code that runs only from its own checkout), rank 0 only; each step
+times one matrix of every shape class and extrapolates by multiplicity.
 """
 
 from __future__ import annotations
@@ -123,6 +124,19 @@ DESCRIPTIONS = {
 def ns_flops(shape, steps=NS_STEPS):
     m, n = min(shape), max(shape)
     return steps * (4.0 * m * m * n + 2.0 * m ** 3)
+
+
+def line_config(cfg: str, precision: str, world: int, adamw_sharding: bool) -> dict:
+    """The JSON line's `config` object. Both arms print this same object, so
+    the reference arm's line names the same workload as this library's."""
+    muon_shapes = [s for n, s in config_params(cfg) if is_muon(n, s)]
+    parallelism = f"dp{world}"
+    if world > 1:
+        parallelism += (" (FLOP-balanced NS owners, bf16 param all-gather, owner-only momentum"
+                        + (", AdamW element ranges per rank" if adamw_sharding else "") + ")")
+    return {"workload": cfg, "description": DESCRIPTIONS[cfg], "muon_matrices": len(muon_shapes),
+            "ns_tflop_per_step": round(sum(ns_flops(s) for s in muon_shapes) / 1e12, 2), "precision": precision,
+            "parallelism": parallelism, "l2": "inputs larger than L2 (params+grads+state >> 126 MB)"}
 
 
 GRAM_SEGMENT = 3  # iterations between restarts of the gram-form Newton-Schulz
@@ -308,6 +322,7 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     cfg = args.config
     for _ in range(args.warmup):
         cpu_sample(cfg)
@@ -319,12 +334,12 @@ def run_reference(args):
     value = statistics.median(times)
     line = {"metric": "muon_step_ms", "value": round(value, 3), "unit": "ms", "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value, 3),
-            "higher_is_better": False, "scaling": "strong" if args.gpus > 1 else "weak", "vs_baseline": None,
+            "higher_is_better": False, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic",
-            "config": {"workload": cfg, "description": DESCRIPTIONS[cfg], "parallelism": "cpu",
-                       "precision": "fp32 (reference algorithm)"},
+            "config": line_config(cfg, args.precision, world, args.adamw_sharding),
             "cpu_baseline": {"value": round(value, 3), "unit": "ms", "cores": cores(), "kind": "port",
-                             "sample": sample},
+                             "sample": sample,
+                             "arithmetic": "fp32 throughout (the reference algorithm), on the host cores"},
             "e2e": {"value": round(value, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -590,13 +605,7 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 3),
             "higher_is_better": False, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
             "dtype": args.precision, "data": "synthetic",
-            "config": {"workload": cfg, "description": DESCRIPTIONS[cfg], "muon_matrices": len(muon_shapes),
-                       "ns_tflop_per_step": round(total_flops / 1e12, 2), "precision": args.precision,
-                       "parallelism": f"dp{world}" + (" (FLOP-balanced NS owners, bf16 param all-gather,"
-                                                      " owner-only momentum"
-                                                      + (", AdamW element ranges per rank" if args.adamw_sharding
-                                                         else "") + ")" if world > 1 else ""),
-                       "l2": "inputs larger than L2 (params+grads+state >> 126 MB)"},
+            "config": line_config(cfg, args.precision, world, args.adamw_sharding),
             "e2e": {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "note": "MuonAdamW.step() with this step's gradients copied in from pinned host memory; the "
                             "updated parameters stay on the device for the next forward pass, as in training, so "

@@ -92,3 +92,30 @@ def test_clock_sampler_parses_nvidia_smi_lines():
     s2.proc = FakeProc()
     assert s2.stop()["reasons"] == ["hw_slowdown", "sw_power_cap"]
     assert bench.ClockSampler([0]).stop() is None  # never started
+
+
+def test_reference_arm_line_names_the_same_workload(monkeypatch, capsys):
+    """`--impl reference` prints one line, on rank 0 only, whose `config` is
+    the object this library's arm prints for the same arguments, with the
+    reference-arm keys (impl, cpu_baseline, e2e without copies). The timed
+    sample is replaced by a fixed figure: the line's assembly is what is
+    checked here, not the CPU time."""
+    import json
+
+    monkeypatch.setattr(bench, "cpu_sample", lambda cfg: (1234.5, f"stub sample of {cfg}"))
+    for world in (1, 8):
+        monkeypatch.setenv("WORLD_SIZE", str(world))
+        monkeypatch.setenv("RANK", "1")
+        bench.main(["--impl", "reference", "--gpus", str(world), "--steps", "2", "--warmup", "3"])
+        assert capsys.readouterr().out == ""  # other ranks exit without work
+        monkeypatch.setenv("RANK", "0")
+        bench.main(["--impl", "reference", "--gpus", str(world), "--steps", "2", "--warmup", "3"])
+        lines = [ln for ln in capsys.readouterr().out.splitlines() if ln.startswith("{")]
+        assert len(lines) == 1
+        d = json.loads(lines[0])
+        assert d["config"] == bench.line_config("c2", "fp16", world, True)
+        assert d["impl"] == "reference" and d["metric"] == "muon_step_ms" and d["unit"] == "ms"
+        assert d["higher_is_better"] is False and d["value"] == 1234.5 and d["n_gpus"] == world
+        assert d["scaling"] == ("strong" if world > 1 else "weak")
+        assert d["cpu_baseline"]["value"] == d["value"] and d["cpu_baseline"]["kind"] == "port"
+        assert d["e2e"] == {"value": 1234.5, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
