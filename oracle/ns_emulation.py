@@ -16,6 +16,10 @@ epilogue arithmetic in fp32. Two forms:
 * gram: the iteration on A = X X^T, A <- P (P A) with P = alpha I + A' B',
   accumulating Q = P ... P and applying X <- Q X every `restart` iterations.
 
+`emulate_split` runs either form with split fp16 operands (hi + lo pairs,
+three passes per product, precision="parity"), with the accumulation either
+exact (rounded once to fp32) or modelled as a truncating multi-term adder.
+
 Scales (as the kernels choose them): X at iteration 0 times 2^round(log2
 sqrt(m n)), later times 2^round(log2 sqrt(n)); gram-form A, P and P A times
 2^round(log2(m / 4)), Q times 2^round(log2(m / 64)).
@@ -143,6 +147,105 @@ def emulate_gram(g: np.ndarray, steps: int = 5, restart: int = 3, op: str = "fp1
         xs = _f32(acc) if last else rnd(acc)
         s = s_next
     return (xs.T if tall else xs).astype(np.float32)
+
+
+# ------------------------------------------------- split fp16 operands
+def _split_f16(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """The stored pair of a split operand: hi = fp16(x), lo = fp16(x - hi),
+    subnormals included (the kernels' MUON_F16X3 epilogue stores)."""
+    hi = _f16(x)
+    return hi, _f16(np.asarray(x, np.float64) - hi)
+
+
+def _rz_f32(x: np.ndarray) -> np.ndarray:
+    """x cut toward zero to fp32's 24-bit significand."""
+    m, e = np.frexp(np.asarray(x, np.float64))
+    return np.ldexp(np.trunc(m * 2.0 ** 24) / 2.0 ** 24, e)
+
+
+def _split_product(a, b, acc: str, bits: int, block: int) -> np.ndarray:
+    """A B for split operand pairs a = (hi, lo), b = (hi, lo): the passes
+    hi*hi, hi*lo and lo*hi, in that order, into one fp32 accumulator (lo*lo
+    dropped), as the kernels issue them (one whole K loop per pass).
+
+    acc "exact": the products exact, the whole sum rounded once to fp32.
+    acc "truncate": K in blocks of `block` products; per block the
+    accumulator and the block's exact products are cut toward zero to `bits`
+    fraction bits below the leading bit of the largest of them, added exactly,
+    and the sum cut toward zero to fp32. This models a fused multi-term adder
+    with truncating alignment, of the kind Fasi, Higham, Mikaitis and Pranesh
+    describe for earlier tensor cores ("Numerical behavior of NVIDIA tensor
+    cores", PeerJ Computer Science 7:e330, 2021); its parameters are a
+    hypothesis held against the errors measured on the B200, not a
+    specification of its hardware."""
+    passes = [(a[0], b[0]), (a[0], b[1]), (a[1], b[0])]
+    if acc == "exact":
+        return _f32(sum(x @ y for x, y in passes))
+    if acc != "truncate":
+        raise ValueError(f"unknown accumulation model {acc!r}")
+    out = np.zeros((a[0].shape[0], b[0].shape[1]))
+    for x, y in passes:
+        for k0 in range(0, x.shape[1], block):
+            terms = x[:, k0:k0 + block, None] * y[None, k0:k0 + block, :]  # exact products
+            _, e = np.frexp(np.maximum(np.abs(out), np.abs(terms).max(axis=1)))
+            ulp = np.ldexp(1.0, e - 1 - bits)
+            cut = np.trunc(out / ulp) * ulp + (np.trunc(terms / ulp[:, None, :]) * ulp[:, None, :]).sum(axis=1)
+            out = _rz_f32(cut)
+    return out
+
+
+def emulate_split(g: np.ndarray, steps: int = 5, form: str = "standard", restart: int = 3, acc: str = "exact",
+                  bits: int = 23, block: int = 16) -> np.ndarray:
+    """Newton-Schulz with split fp16 operands (precision="parity") in the
+    standard or the gram form (restart every `restart` iterations; restart
+    >= steps: one segment, no restart), at the fp16 power-of-two scales, with
+    the products of `_split_product` under accumulation model `acc`."""
+    x, tall = _prepare(g)
+    m, n = x.shape
+    eye = np.eye(m)
+
+    def mm(u, v):
+        return _split_product(u, v, acc, bits, block)
+
+    def tr(u):
+        return tuple(t.T for t in u)
+
+    s = x_scale(m, n, 0)
+    xs = _split_f16(x * s)
+    if form == "standard":
+        for it in range(steps):
+            last = it == steps - 1
+            s_next = 1.0 if last else x_scale(m, n, it + 1)
+            ap = mm(xs, tr(xs)) / (s * s) - eye
+            bp = GAMMA * ap + BETA * eye
+            mmat = _split_f16(mm(_split_f16(ap), _split_f16(bp)) + ALPHA * eye)
+            out = mm(mmat, xs) * (s_next / s)
+            xs = (out, np.zeros_like(out)) if last else _split_f16(out)
+            s = s_next
+        res = xs[0]
+        return (res.T if tall else res).astype(np.float32)
+    if form != "gram":
+        raise ValueError(f"unknown form {form!r}")
+    sa, sq = _pow2(m / 4.0), _pow2(m / 64.0)
+    bounds = list(range(0, steps, restart)) + [steps]
+    for s0, s1 in zip(bounds, bounds[1:]):
+        p = pa = q = None
+        for j in range(s0, s1):
+            a = mm(xs, tr(xs)) / (s * s) if j == s0 else mm(p, pa) / (sa * sa)
+            ap = a - eye
+            bp = GAMMA * ap + BETA * eye
+            p_true = mm(_split_f16(ap * sa), _split_f16(bp * sa)) / (sa * sa) + ALPHA * eye
+            p = _split_f16(p_true * sa)
+            q = _split_f16(p_true * sq) if j == s0 else _split_f16(mm(p, q) / sa)
+            if j < s1 - 1:
+                pa = _split_f16(mm(p, _split_f16(a * sa)) / sa)
+        last = s1 == steps
+        s_next = 1.0 if last else x_scale(m, n, s1)
+        out = mm(q, xs) * (s_next / (sq * s))
+        xs = (out, np.zeros_like(out)) if last else _split_f16(out)
+        s = s_next
+    res = xs[0]
+    return (res.T if tall else res).astype(np.float32)
 
 
 def structured_input(shape: tuple[int, int], kind: str, seed: int = 0) -> np.ndarray:
