@@ -251,6 +251,29 @@ def test_param_groups_order_and_defaults():
     assert g1["muon_ns_steps"] == 3
 
 
+def test_add_param_group_adds_an_adamw_group():
+    """torch.optim.Optimizer.add_param_group after construction, which the
+    reference does not override: the new group gets every default key with
+    use_muon False, so its parameters take the AdamW path with the reference's
+    state (step, exp_avg, exp_avg_sq), and the Muon group is unchanged."""
+    m = Tiny()
+    mark_muon_parameters(m)
+    eng = OracleEngine()
+    opt = MuonAdamW(m, lr=2e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, _engine=eng)
+    extra = torch.nn.Parameter(torch.randn(32, generator=torch.Generator().manual_seed(3)) * 0.02)
+    opt.add_param_group({"params": [extra]})
+    new = opt.param_groups[-1]
+    assert len(opt.param_groups) == 3 and new["use_muon"] is False
+    assert set(new) == set(opt.param_groups[0])
+    for p in list(m.parameters()) + [extra]:
+        p.grad = torch.full_like(p, 1e-3)
+    before = extra.detach().clone()
+    opt.step()
+    assert sorted(opt.state[extra]) == ["exp_avg", "exp_avg_sq", "step"]
+    assert float(opt.state[extra]["step"]) == 1.0 and not torch.equal(before, extra.detach())
+    assert eng.calls["muon"] == 1
+
+
 def test_muon_group_inactive_without_grads():
     m = Tiny()
     mark_muon_parameters(m)
