@@ -251,6 +251,44 @@ def test_param_groups_order_and_defaults():
     assert g1["muon_ns_steps"] == 3
 
 
+@pytest.mark.parametrize("mode", ["reference", "shape"])
+def test_update_scale_per_matrix(mode):
+    """The update scale each matrix hands the engine: the reference's
+    lr * lr_scale * coefficient * sqrt(max(rows, cols)) (muon_adamw.py:408-413)
+    by default, lr * lr_scale * max(1, rows / cols) ** 0.5 with
+    scale_mode="shape", read from the group at every step (a scheduler's new
+    lr takes effect on the next step)."""
+    import math
+
+    class Recording(OracleEngine):
+        def __init__(self):
+            super().__init__()
+            self.effs = []
+
+        def muon_matrices(self, items, **kw):
+            self.effs.append(sorted((tuple(it.param.shape), it.eff) for it in items))
+            super().muon_matrices(items, **kw)
+
+    m = torch.nn.Module()
+    m.wide = torch.nn.Parameter(torch.randn(8, 32) * 0.02)
+    m.tall = torch.nn.Parameter(torch.randn(32, 8) * 0.02)
+    mark_muon_parameters(m, predicate=lambda n, p: p.ndim == 2)
+    eng = Recording()
+    opt = MuonAdamW(m, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0, muon_lr_scale=0.5,
+                    scale_mode=mode, _engine=eng)
+    for lr in (0.02, 0.005):
+        opt.param_groups[1]["lr"] = lr
+        for p in m.parameters():
+            p.grad = torch.full_like(p, 1e-3)
+        opt.step()
+        want = {(8, 32): lr * 0.5 * (0.2 * math.sqrt(32) if mode == "reference" else 1.0),
+                (32, 8): lr * 0.5 * (0.2 * math.sqrt(32) if mode == "reference" else 2.0)}
+        got = dict(eng.effs[-1])
+        assert got.keys() == want.keys()
+        for k in want:
+            assert got[k] == pytest.approx(want[k], rel=1e-12), (k, got[k], want[k])
+
+
 def test_add_param_group_adds_an_adamw_group():
     """torch.optim.Optimizer.add_param_group after construction, which the
     reference does not override: the new group gets every default key with
