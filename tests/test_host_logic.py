@@ -251,6 +251,63 @@ def test_param_groups_order_and_defaults():
     assert g1["muon_ns_steps"] == 3
 
 
+def test_reference_caller_sequence_with_a_warmup_schedule():
+    """The calls the reference's trainer makes, replayed on this optimizer
+    (dm05_exp cannot be imported here: it needs flask): prepare_model marks
+    the default Muon set (dm05_exp.py:276-278, is_default_muon_parameter),
+    build_muon_adamw constructs the optimizer with DM05OptimizerConfig's
+    defaults (:255-267, :280-292; DMTrainer.create_optimizer, trainer.py:122-130),
+    then the HF loop's order each step: gradients, optimizer.step(),
+    lr_scheduler.step() (a warmup LambdaLR rewriting group["lr"]). Only the
+    action expert's layer weights go to Muon, and every step matches the
+    oracle optimizer run at the scheduled learning rate."""
+    gen = torch.Generator().manual_seed(11)
+
+    def linear(o, i):
+        lin = torch.nn.Linear(i, o, bias=False)
+        lin.weight.data = torch.randn(o, i, generator=gen) * 0.02
+        return lin
+
+    model = torch.nn.Module()
+    model.model = torch.nn.Module()
+    model.model.embed_tokens = torch.nn.Embedding(40, 16)
+    model.model.language_model = torch.nn.Module()
+    model.model.language_model.layers = torch.nn.ModuleList([linear(16, 16)])
+    model.model.action_expert = torch.nn.Module()
+    model.model.action_expert.layers = torch.nn.ModuleList([linear(48, 16), linear(16, 48)])
+    model.model.action_expert.norm = torch.nn.LayerNorm(16, bias=False)
+    cfg = {"base_lr": 2.5e-5, "weight_decay": 1e-10, "warmup_steps": 4, "adam_beta1": 0.9, "adam_beta2": 0.95,
+           "adam_epsilon": 1e-8, "muon_momentum": 0.95, "muon_nesterov": True, "muon_ns_steps": 5,
+           "muon_lr_scale": 1.0, "muon_moonlight_coefficient": 0.2}
+    selected = mark_muon_parameters(model, predicate=is_default_muon_parameter)
+    assert sorted(selected) == ["model.action_expert.layers.0.weight", "model.action_expert.layers.1.weight"]
+    opt = MuonAdamW(model, lr=cfg["base_lr"], betas=(cfg["adam_beta1"], cfg["adam_beta2"]), eps=cfg["adam_epsilon"],
+                    weight_decay=cfg["weight_decay"], muon_momentum=cfg["muon_momentum"],
+                    muon_nesterov=cfg["muon_nesterov"], muon_ns_steps=cfg["muon_ns_steps"],
+                    muon_lr_scale=cfg["muon_lr_scale"], muon_moonlight_coefficient=cfg["muon_moonlight_coefficient"],
+                    _engine=OracleEngine())
+    sched = torch.optim.lr_scheduler.LambdaLR(opt, lambda s: min(1.0, (s + 1) / cfg["warmup_steps"]))
+    ref = O.OracleMuonAdamW(lr=cfg["base_lr"], betas=(cfg["adam_beta1"], cfg["adam_beta2"]), eps=cfg["adam_epsilon"],
+                            weight_decay=cfg["weight_decay"])
+    host = {n: p.detach().numpy().copy() for n, p in model.named_parameters()}
+    muon = {n: host[n] for n in selected}
+    adam = {n: v for n, v in host.items() if n not in muon}
+    for step in range(3):
+        grads = {}
+        for n, p in model.named_parameters():
+            p.grad = torch.randn(p.shape, generator=gen) * 1e-3
+            grads[n] = p.grad.numpy().copy()
+        lrs = {g["lr"] for g in opt.param_groups}
+        assert lrs == {cfg["base_lr"] * min(1.0, (step + 1) / cfg["warmup_steps"])}
+        ref.lr = lrs.pop()
+        ref.step(muon, {n: grads[n] for n in muon}, adam, {n: grads[n] for n in adam})
+        opt.step()
+        sched.step()
+        for n, p in model.named_parameters():
+            want = muon.get(n, adam.get(n))
+            assert O.rel_frobenius(p.detach().numpy(), want) < 1e-6, (step, n)
+
+
 @pytest.mark.parametrize("mode", ["reference", "shape"])
 def test_update_scale_per_matrix(mode):
     """The update scale each matrix hands the engine: the reference's
