@@ -411,6 +411,20 @@ def test_zeropower_cpu_has_no_fallback():
         zeropower_via_newtonschulz5(torch.ones(4, 4))
 
 
+def test_unsupported_dtypes_and_devices_raise():
+    """The kernels take bfloat16 or float32 tensors on a CUDA device; any other
+    dtype, and a CPU engine, raise RuntimeError naming the problem instead of
+    running some other path."""
+    from opendm_b200 import engine as E
+
+    assert E._dtype_code(torch.zeros(1, dtype=torch.bfloat16)) != E._dtype_code(torch.zeros(1))
+    for dt in (torch.float16, torch.float64):
+        with pytest.raises(RuntimeError, match=f"unsupported dtype {dt}"):
+            E._dtype_code(torch.zeros(1, dtype=dt))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        E.CudaMuonEngine("cpu")
+
+
 def test_shard_plan_dataclass_matches_reference_fields():
     p = MuonShardPlan("local", 6, 6, (6,), (0,), 0)
     assert p.process_group is None and p.kind == "local"
