@@ -221,6 +221,21 @@ def test_allgather_waves_two_ranks(tmp_path):
     assert res[0]["waves"] == res[1]["waves"] and len(set(res[0]["waves"])) >= 2
 
 
+def test_more_ranks_than_muon_matrices(tmp_path):
+    """Replicated parameters on 3 ranks with only 2 Muon matrices: one rank
+    owns none, and with 3 waves requested some waves are empty on every rank.
+    That rank still takes part in every all-gather (its bucket is padding),
+    and every rank ends with the single-process oracle's parameters, in both
+    the replicated-state and the owner-only-state (waves) schedules."""
+    muon = [(64, 32), (32, 96)]
+    adam = [(16,)]
+    for scenario in ("replicated", "waves"):
+        res = _run(scenario, muon, adam, 2, tmp_path, world=3)
+        _check(res, muon, adam, 2)
+        assert sum(r["muon_calls"] for r in res) == len(muon) * 2  # each matrix orthogonalised once per step
+        assert min(r["muon_calls"] for r in res) == 0
+
+
 def test_owner_only_momentum_consolidates(tmp_path):
     res = _run("state_sharding", SMALL_MUON, SMALL_ADAM, 3, tmp_path)
     _check(res, SMALL_MUON, SMALL_ADAM, 3)
