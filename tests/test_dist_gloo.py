@@ -33,15 +33,19 @@ def _port():
     return port
 
 
-def _data(muon, adam, steps, seed=0):
+def _data(muon, adam, steps, seed=0, inactive=()):
+    """Seeded parameters and per-step gradients; at the steps in `inactive`
+    every Muon gradient is None (the Muon group has nothing to do)."""
     rng = np.random.default_rng(seed)
     params = [(rng.standard_normal(s) * 0.02).astype(np.float32) for s in muon + adam]
     grads = [[(rng.standard_normal(s) * 1e-3).astype(np.float32) for s in muon + adam] for _ in range(steps)]
+    for st in inactive:
+        grads[st][:len(muon)] = [None] * len(muon)
     return params, grads
 
 
-def _oracle(muon, adam, steps):
-    params, grads = _data(muon, adam, steps)
+def _oracle(muon, adam, steps, inactive=()):
+    params, grads = _data(muon, adam, steps, inactive=inactive)
     opt = O.OracleMuonAdamW(lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01)
     mp_ = {str(i): params[i].copy() for i in range(len(muon))}
     ap_ = {str(i): params[i].copy() for i in range(len(muon), len(params))}
@@ -78,9 +82,11 @@ def _worker(rank, port, scenario, muon, adam, steps, outdir, world=WORLD):
     from tests.oracle_engine import OracleEngine
 
     result = {"rank": rank}
+    inactive = (1,) if scenario.endswith("_inactive") else ()  # step 1 without Muon gradients
+    scenario = scenario.removesuffix("_inactive")
     try:
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
-        params, grads = _data(muon, adam, steps)
+        params, grads = _data(muon, adam, steps, inactive=inactive)
         model = torch.nn.Module()
         n_muon = len(muon)
         if scenario in ("replicated", "state_sharding", "fail", "waves", "adam_sharded"):
@@ -137,6 +143,9 @@ def _worker(rank, port, scenario, muon, adam, steps, outdir, world=WORLD):
                 raise SystemExit(3)  # this rank dies between steps
             for i, p in enumerate(plist):
                 g = grads[s][i]
+                if g is None:
+                    p.grad = None
+                    continue
                 if slices is not None and i < n_muon:
                     a, b = slices[i]
                     g = g.reshape(-1)[a:b]
@@ -183,8 +192,8 @@ def _run(scenario, muon, adam, steps, tmp_path, world=WORLD):
     return [torch.load(os.path.join(tmp_path, f"rank{r}.pt"), weights_only=False) for r in range(world)]
 
 
-def _check(res, muon, adam, steps, check_exp_avg=True):
-    final, exp_avg = _oracle(muon, adam, steps)
+def _check(res, muon, adam, steps, check_exp_avg=True, inactive=()):
+    final, exp_avg = _oracle(muon, adam, steps, inactive=inactive)
     for r in res:
         assert "error" not in r, r.get("trace")
         for i, got in enumerate(r["params"]):
@@ -234,6 +243,19 @@ def test_more_ranks_than_muon_matrices(tmp_path):
         _check(res, muon, adam, 2)
         assert sum(r["muon_calls"] for r in res) == len(muon) * 2  # each matrix orthogonalised once per step
         assert min(r["muon_calls"] for r in res) == 0
+
+
+def test_step_without_muon_gradients_on_every_rank(tmp_path):
+    """A step in which no rank has a Muon gradient (reference muon_adamw.py:350-360:
+    the group is inactive, so momentum, step counts and parameters stay as
+    they are while AdamW still steps). The check is reduced on the host
+    (gloo), and every rank skips the same collectives: the replicated, the
+    owner-only-state (waves) and the FSDP flat-shard schedules all end with
+    the single-process oracle's parameters and momentum."""
+    muon = SMALL_MUON[:4]
+    for scenario in ("replicated", "waves", "flat"):
+        res = _run(scenario + "_inactive", muon, SMALL_ADAM, 3, tmp_path)
+        _check(res, muon, SMALL_ADAM, 3, inactive=(1,))
 
 
 def test_owner_only_momentum_consolidates(tmp_path):
