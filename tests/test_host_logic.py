@@ -389,8 +389,7 @@ def test_closure_and_lr_read_each_step():
 
     def closure():
         opt.zero_grad()
-        loss = m.head(m.model.action_expert.layers[0].weight.t() @ torch.ones(16, 8) @ x.t()).sum() if False else \
-            (m.model.action_expert.layers[0](x).sum() + m.head(x).sum())
+        loss = m.model.action_expert.layers[0](x).sum() + m.head(x).sum()
         loss.backward()
         return loss
 
@@ -402,6 +401,35 @@ def test_closure_and_lr_read_each_step():
         g["lr"] = 0.0
     opt.step(closure)
     assert torch.equal(before, w)  # lr is read from the group at every step
+
+
+def test_group_hyperparameters_read_each_step():
+    """weight_decay, muon_momentum and muon_nesterov changed in the Muon
+    group between steps (as a scheduler may) take effect on the next step:
+    three steps with different values match the oracle run with the same
+    values (reference muon_adamw.py:362-414 reads them from the group)."""
+    gen = torch.Generator().manual_seed(5)
+    w0 = torch.randn(24, 40, generator=gen) * 0.02
+    m = torch.nn.Module()
+    m.w = torch.nn.Parameter(w0.clone())
+    mark_muon_parameters(m, predicate=lambda n, p: p.ndim == 2)
+    opt = MuonAdamW(m, lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.01, _engine=OracleEngine())
+    p_ref = {"w": w0.numpy().copy()}
+    ref_state = None
+    for wd, mu, nest in [(0.01, 0.95, True), (0.1, 0.9, False), (0.0, 0.5, True)]:
+        g = torch.randn(24, 40, generator=gen) * 1e-3
+        m.w.grad = g.clone()
+        group = opt.param_groups[1]
+        group["weight_decay"], group["muon_momentum"], group["muon_nesterov"] = wd, mu, nest
+        opt.step()
+        ref = O.OracleMuonAdamW(lr=0.02, betas=(0.9, 0.95), eps=1e-8, weight_decay=wd, muon_momentum=mu,
+                                muon_nesterov=nest)
+        if ref_state is not None:
+            ref.muon_state = ref_state
+        ref.step(p_ref, {"w": g.numpy()}, {}, {})
+        ref_state = ref.muon_state
+        assert O.rel_frobenius(m.w.detach().numpy(), p_ref["w"]) < 1e-6
+        assert O.rel_frobenius(opt.state[m.w]["exp_avg"].numpy(), ref_state["w"].exp_avg) < 1e-6
 
 
 def test_zeropower_cpu_has_no_fallback():
