@@ -464,7 +464,6 @@ def run_ours(args):
     ag_wait_ms = max_over_ranks(per_step("allgather_wait"))
 
     muon_shapes = [s for n, s in spec if is_muon(n, s)]
-    total_flops = sum(ns_flops(s) for s in muon_shapes)
     # FLOPs this rank ran (its owned matrices); the roofline uses the busiest rank.
     owners = opt._owners.get(id(opt.param_groups[1]))
     if owners is not None:
